@@ -1,0 +1,342 @@
+#!/usr/bin/env python
+"""Batch-one Qwen3-0.6B decode benchmark on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mkb|reference]
+
+One step = one greedy decode token (batch 1) of the 28-layer Qwen3-0.6B
+architecture with random-init BF16 weights (synthetic data), max cache 512, a
+32-token prompt, positions 32.. (config 0). Prints ONE JSON line on rank 0.
+
+* value: tokens/s of the on-device greedy loop (DecodeEngine.generate: one
+  persistent launch decodes the K tokens, argmax feeding the next embedding),
+  device-timed with CUDA events on the launching stream; with N GPUs each rank
+  runs its own replica (prompt seed = rank) and value = all tokens / max time.
+* e2e: the same metric through the public per-token call (mkb_engine_step):
+  every step copies (token, position) host->device from pinned memory, replays
+  the CUDA graph and reads the argmax id (and status word) back to the host.
+* roofline: decode_kernel's algorithmic bytes (every weight byte once per token
+  + KV bytes read) / its measured launch duration, against the measured HBM peak.
+* cpu_baseline: HF Qwen3 FP32 decode on this host's cores (oracle), rank 0, N=1.
+
+``--impl reference`` times the reference's model path on the host CPU (HF
+Qwen3ForCausalLM FP32, the comparison decode of model.py:139-180) for the same
+config/metric, and, when ``oracle/_ref`` holds the reference CUDA kernel built
+from its own sources, its per-token time on this GPU as an extra field.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HIDDEN, INTER, VOCAB, LAYERS = 1024, 3072, 151936, 28
+PROMPT, MAX_SEQ = 32, 512
+WEIGHT_BYTES = LAYERS * (31_457_280 + 4_608) + 311_164_928 + 2_048 + 2_048   # 1,192,101,888
+KV_BYTES_PER_POS = LAYERS * 8 * 128 * 2 * 2                                   # 114,688
+METRIC = "batch-1 decode tok/s (Qwen3-0.6B, 512-token cache)"
+
+
+def args_parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["mkb", "reference"], default="mkb")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def synthetic_weights(seed: int, device):
+    """Random-init Qwen3-0.6B weights generated on the device (N(0, 0.02), norms 1)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def lin(*shape):
+        return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+
+    ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=device)  # noqa: E731
+    embed = lin(VOCAB, HIDDEN)
+    layers = []
+    for _ in range(LAYERS):
+        layers += [ones(HIDDEN), lin(2048, HIDDEN), lin(1024, HIDDEN), lin(1024, HIDDEN), ones(128), ones(128),
+                   lin(HIDDEN, 2048), ones(HIDDEN), lin(INTER, HIDDEN), lin(INTER, HIDDEN), lin(HIDDEN, INTER)]
+    return embed, ones(HIDDEN), layers
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx.append(float(p[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic_per_token():
+    """DRAM bytes per token of decode_kernel from the committed ncu summary, if any."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "decode_kernel_traffic.json")) as f:
+            return float(json.load(f)["dram_bytes_per_token"])
+    except Exception:
+        return None
+
+
+def cpu_baseline(steps_cap: int = 128, budget_s: float = 12.0):
+    """HF Qwen3 FP32 decode on the host CPU (the oracle), bounded sample."""
+    from oracle import configs as C
+    from oracle import hf_reference as H
+    from oracle import weights as W
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    w = W.make_weights(0)
+    model = H.build_model(w, threads=threads)
+    ids = C.config0_prompt(0)
+    logits, cache = H.prefill(model, ids)
+    tok = int(torch.argmax(logits))
+    n, t0 = 0, time.perf_counter()
+    while n < steps_cap:
+        logits, cache = H.step(model, cache, tok)
+        tok = int(torch.argmax(logits))
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    cpu = "unknown"
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                cpu = ln.split(":", 1)[1].strip()
+                break
+    except Exception:
+        pass
+    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"HF transformers Qwen3ForCausalLM FP32 eager, {n} greedy decode steps at positions "
+                      f"32..{31 + n} after a 32-token prefill, {threads} threads, {cpu}"}
+
+
+def run_reference(a, rank, world):
+    if rank != 0:
+        return
+    base = cpu_baseline(steps_cap=max(a.steps, 1), budget_s=60.0)
+    line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 / base["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random-init weights, random prompt ids)",
+            "config": {"workload": "config0: Qwen3-0.6B batch-1 greedy decode, 32-token prompt, cache 512",
+                       "model": "Qwen3-0.6B", "global_batch": 1, "seq_len": MAX_SEQ, "parallelism": "none (CPU)"},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    ref_gpu = reference_kernel_on_gpu(a)
+    if ref_gpu is not None:
+        line["reference_cuda_kernel_b200"] = ref_gpu
+    print(json.dumps(line), flush=True)
+
+
+def reference_kernel_on_gpu(a):
+    """The reference's own megakernel (built from its sources into oracle/_ref),
+    timed per call on this GPU the way model.py:107-127 times it (its binding's
+    per-call table allocation and cudaFree included)."""
+    if not torch.cuda.is_available():
+        return None
+    try:
+        from oracle import ref_kernel
+        return ref_kernel.time_reference(steps=min(a.steps, 64), warmup=a.warmup)
+    except Exception as e:  # the reference kernel is optional context, never the product
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+
+
+def main():
+    a = args_parse()
+    rank, world, local = dist_env()
+    if a.impl == "reference":
+        run_reference(a, rank, world)
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    import megakernel_b200 as mk
+
+    embed, final_norm, layers = synthetic_weights(1000 + rank, dev)
+    k = torch.zeros((LAYERS, 8, MAX_SEQ, 128), dtype=torch.bfloat16, device=dev)
+    v = torch.zeros_like(k)
+    eng = mk.DecodeEngine(embed, final_norm, layers, k, v, fused_down=True, use_graph=True)
+    g = torch.Generator().manual_seed(rank)
+    prompt = torch.randint(0, VOCAB, (PROMPT,), generator=g).tolist()
+    # prefill the cache by decoding the prompt through the engine (positions 0..31)
+    tok = prompt[0]
+    for p in range(PROMPT):
+        nxt = eng.step(prompt[p], p)
+    first = nxt
+    span = MAX_SEQ - PROMPT
+    steps, warm = max(1, a.steps), max(3, a.warmup)
+
+    def greedy(n_tok):
+        """n_tok greedy tokens in launches of <= span tokens from position 32; returns launches."""
+        done, launches = 0, 0
+        out = torch.empty(span, dtype=torch.int32, device=dev)
+        while done < n_tok:
+            n = min(span, n_tok - done)
+            eng.generate(first, PROMPT, n, out=out)
+            done += n
+            launches += 1
+        return launches
+
+    greedy(warm)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        launches = greedy(steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    dev_ms = ev0.elapsed_time(ev1)
+    st = eng.status()
+    assert st[0] == 0, f"in-kernel error {st}"
+
+    # e2e through the public per-token call
+    for i in range(warm):
+        eng.step(first, PROMPT + i)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    t = first
+    for i in range(steps):
+        t = eng.step(t, PROMPT + (i % span))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+
+    times = torch.tensor([dev_ms, e2e_s * 1000.0], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
+    dev_ms, e2e_ms = float(times[0]), float(times[1])
+
+    # algorithmic bytes of the timed launches (positions 32.. wrap every `span` tokens)
+    alg = 0
+    for i in range(steps):
+        cl = PROMPT + (i % span) + 1
+        alg += WEIGHT_BYTES + KV_BYTES_PER_POS * cl
+    per_launch_bytes = alg / launches
+    per_launch_s = dev_ms / 1000.0 / launches
+    peak, peak_kind = measured_peak()
+    achieved = per_launch_bytes / per_launch_s / 1e9
+    traffic_tok = ncu_traffic_per_token()
+    toks_per_launch = steps / launches
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": world * steps / (dev_ms / 1000.0), "unit": "tok/s", "n_gpus": world,
+            "steps": steps, "warmup": warm, "ms_per_step": dev_ms / steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init BF16 weights N(0,0.02), random prompt ids)",
+            "config": {"workload": "config0: Qwen3-0.6B batch-1 greedy decode, 32-token prompt, cache 512",
+                       "model": "Qwen3-0.6B", "global_batch": world, "seq_len": MAX_SEQ,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2: 1.19 GB of weights streamed per token vs 126 MB L2",
+                       "us_per_token": dev_ms * 1000.0 / steps, "tokens_per_launch": toks_per_launch},
+            "e2e": {"value": world * steps / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 8, "us_per_token": e2e_ms * 1000.0 / steps,
+                    "api": "mkb_engine_step (graph replay, host token in/out)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_kind,
+                         "traffic": (traffic_tok * toks_per_launch) if traffic_tok else None,
+                         "kernel": "decode_kernel", "algorithmic_bytes_per_launch": per_launch_bytes},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not a.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline()
+            except Exception as e:
+                line["cpu_baseline"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,157 @@
+/* C ABI of the B200 batch-one Qwen3-0.6B decode engine (libmkb200.so).
+ *
+ * Plain pointers and sizes only; every pointer named "device" is a CUDA device
+ * pointer, every weight is BF16 in the reference's (Hugging Face nn.Linear)
+ * [out, in] row-major layout unless stated. Weights and KV rows must be
+ * 16-byte aligned (bulk-copy rule); a misaligned operand is reported as an error
+ * instead of being copied.
+ *
+ * Error model: functions return cudaError_t. Launch-time errors come back
+ * directly; in-kernel failures (a bounded wait that expired, bad arguments seen
+ * on the device) are recorded in the workspace and read with
+ * mkb_workspace_status(); the engine calls check it after every step.
+ */
+#ifndef MKB200_H
+#define MKB200_H
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- drop-in for the reference launcher ------------------------------------
+ * Same signature, argument meaning and return type as the reference's
+ * `launch_decode_kernel` (megakernel.cu:898-927, declared in
+ * pytorch_binding.cu:9-33). `layer_weights` is a DEVICE array of 28
+ * LayerWeights structs (11 pointers each, config.cuh:77-89 order). Appends K/V
+ * at `position`, attends over `cache_len` keys and writes FP32 logits to
+ * `g_logits`. g_residual receives the final residual, g_q/g_k/g_v the last
+ * layer's raw QKV projections and g_mlp_intermediate its SwiGLU vector;
+ * hidden_buffer, g_activations, g_attn_output and g_normalized are not used.
+ * The extra synchronisation workspace is allocated once per device on first use
+ * (mkb_default_workspace); calls on one device must not overlap in time. */
+cudaError_t launch_decode_kernel(int token_id, const void* embed_weight, const void* lm_head_weight,
+                                 const void* final_norm_weight, const void* layer_weights,
+                                 const void* cos_table, const void* sin_table, void* k_cache, void* v_cache,
+                                 void* hidden_buffer, void* g_residual, void* g_activations,
+                                 void* g_attn_output, void* g_normalized, void* g_mlp_intermediate,
+                                 void* g_logits, void* g_q, void* g_k, void* g_v, int position, int cache_len,
+                                 int max_seq_len, cudaStream_t stream);
+
+/* ---- explicit-argument launch ----------------------------------------------
+ * Generalises the reference launcher (megakernel.cu:898-994): layer range,
+ * input residual instead of the embedding gather, optional LM head, several
+ * greedy tokens per launch, step state in device memory (for CUDA graphs), a
+ * transposed down weight (fewer grid transitions) and FP32 RoPE tables. */
+enum {
+  MKB_FLAG_LM_HEAD = 1,          /* final norm + LM head + argmax */
+  MKB_FLAG_SKIP_FINAL_NORM = 2,  /* LM head reads the residual as-is */
+  MKB_FLAG_ADVANCE_STEP = 4      /* write argmax / position+1 back to `step` */
+};
+
+typedef struct mkb_decode_args {
+  const void* embed;           /* device [vocab, 1024] */
+  const void* lm_head;         /* device [vocab, 1024] (tied: == embed) */
+  const void* final_norm;      /* device [1024] */
+  const void* layers;          /* device LayerWeights[n_layers] */
+  const void* down_t;          /* device array of n_layers pointers to [3072, 1024]
+                                  transposed down weights, or NULL */
+  const void* cos_table;       /* device [max_seq, 128] */
+  const void* sin_table;
+  int rope_fp32;               /* 1: FP32 tables, 0: BF16 */
+  void* k_cache;               /* device [n_layers, 8, max_seq, 128] BF16 */
+  void* v_cache;
+  int max_seq;
+  int layer_begin, layer_end;  /* run layers [begin, end) */
+  int token, position, cache_len; /* used when step == NULL */
+  int* step;                   /* device int[4] {token, position, -, count} or NULL */
+  int n_tokens;                /* greedy tokens in this launch (>= 1) */
+  int flags;
+  const float* input_residual; /* device [1024] or NULL (embedding gather) */
+  float* logits;               /* device [vocab] or NULL */
+  int* out_tokens;             /* device [n_tokens] or NULL */
+  float* residual_out;         /* device [1024] or NULL */
+  float* q_out;                /* device [2048] / [1024] / [1024] / [3072] or NULL */
+  float* k_out;                /*   (NULL: workspace scratch) */
+  float* v_out;
+  float* mlp_out;
+  void* workspace;             /* device, mkb_workspace_bytes(); NULL = default */
+  int grid;                    /* CTAs; 0 = one per SM */
+  int splits;                  /* attention sequence splits; 0 = automatic */
+  unsigned long long timeout_ns; /* bound on every in-kernel wait; 0 = 1 s */
+  int withhold_cta;            /* test hook (-1 = off): that CTA never publishes its
+                                  first QKV arrival, so the others' waits expire */
+} mkb_decode_args;
+
+void mkb_decode_args_init(mkb_decode_args* a);
+cudaError_t mkb_decode(const mkb_decode_args* a, cudaStream_t stream);
+
+/* ---- workspace ---------------------------------------------------------------- */
+size_t mkb_workspace_bytes(void);
+/* Zero a workspace (required after a launch reported an in-kernel error). */
+cudaError_t mkb_workspace_reset(void* workspace, cudaStream_t stream);
+/* Synchronous read of the in-kernel status: out[0] error code (0 = ok),
+ * out[1] CTA, out[2] layer, out[3] stage, out[4] token. */
+cudaError_t mkb_workspace_status(const void* workspace, uint32_t out[8]);
+/* The per-device workspace used when mkb_decode_args.workspace is NULL and by
+ * launch_decode_kernel (allocated and zeroed on first use). */
+cudaError_t mkb_default_workspace(int device, void** out);
+const char* mkb_error_name(uint32_t code);
+
+/* ---- layout helper -------------------------------------------------------------
+ * down [1024, 3072] -> down_t [3072, 1024] (BF16), used by the engine. */
+cudaError_t mkb_transpose_down(const void* down, void* down_t, cudaStream_t stream);
+
+/* ---- resident engine -------------------------------------------------------------
+ * Keeps the device LayerWeights table, transposed down weights, workspace and a
+ * CUDA graph of the per-token launch resident; the caller keeps ownership of
+ * weights, RoPE tables and the KV cache. */
+typedef struct mkb_model {
+  const void* embed;
+  const void* lm_head;
+  const void* final_norm;
+  const void* const* layer_weights; /* HOST array of n_layers*11 device pointers,
+                                       LayerWeights order (model.py:30-44) */
+  int n_layers;
+  const void* cos_table;
+  const void* sin_table;
+  int rope_fp32;
+  void* k_cache;
+  void* v_cache;
+  int max_seq;
+  int fused_down;                   /* 1: transposed down weight (3 transitions/layer) */
+  int use_graph;                    /* 1: replay the per-token launch as a CUDA graph */
+  float* logits;                    /* device [vocab] for the last token's logits, or NULL
+                                       (the engine then owns the buffer) */
+} mkb_model;
+
+typedef struct mkb_engine mkb_engine;
+cudaError_t mkb_engine_create(const mkb_model* model, mkb_engine** out);
+/* One token: host->device copy of (token, position), graph replay, device->host
+ * copy of the argmax id; synchronises `stream`. */
+cudaError_t mkb_engine_step(mkb_engine* e, int token, int position, int* next_token, cudaStream_t stream);
+/* n greedy tokens in one persistent launch, starting from `token` at `position`;
+ * ids land in out_tokens (device, n entries). Asynchronous. */
+cudaError_t mkb_engine_generate(mkb_engine* e, int token, int position, int n, int* out_tokens,
+                                cudaStream_t stream);
+float* mkb_engine_logits(mkb_engine* e);   /* device [vocab], last token's logits */
+void* mkb_engine_workspace(mkb_engine* e);
+int mkb_engine_grid(mkb_engine* e);
+void mkb_engine_destroy(mkb_engine* e);
+
+/* ---- schedule introspection (host only, no GPU needed) ------------------------ */
+/* out[0..13] = qa, qb, in_bc, h, c, oa, ob, ja, jb, da, db, va, vb, group_size. */
+int mkb_plan_query(int grid, int cta, int32_t out[16]);
+int mkb_choose_splits(int max_cache_len, int group_size);
+void mkb_key_range(int cache_len, int splits, int c, int32_t out[2]);
+int mkb_qkv_chunk_end(int r, int qb);
+size_t mkb_smem_bytes(void);
+int mkb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MKB200_H */

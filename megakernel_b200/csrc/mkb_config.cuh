@@ -1,0 +1,200 @@
+// Model constants, device data layouts and the static work split of the
+// B200 decode kernel. Shared by the kernel (device), the launchers (host) and
+// the host-side schedule query used by the CPU tests.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+
+namespace mkb {
+
+// Qwen3-0.6B dimensions (reference config.cuh:9-18).
+constexpr int kHidden = 1024;
+constexpr int kInter = 3072;
+constexpr int kNQ = 16;
+constexpr int kNKV = 8;
+constexpr int kHeadDim = 128;
+constexpr int kQSize = kNQ * kHeadDim;         // 2048
+constexpr int kKVSize = kNKV * kHeadDim;       // 1024
+constexpr int kQKVRows = kQSize + 2 * kKVSize; // 4096
+constexpr int kVocab = 151936;
+constexpr int kMaxLayers = 28;
+constexpr float kEps = 1e-6f;
+
+// Execution shape: one CTA per SM, 16 consumer warps + 1 producer warp.
+constexpr int kConsumerWarps = 16;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;
+// Shared-memory weight ring: kSlots slots of kSlotBytes, filled by cp.async.bulk.
+constexpr int kSlotBytes = 32768;
+constexpr int kSlots = 6;
+constexpr int kMaxGrid = 256;
+constexpr int kMaxSplits = 32;
+
+// Chunk geometry (rows per ring slot) for each streamed matrix.
+constexpr int kRowsPerChunk1024 = kSlotBytes / (kHidden * 2);   // 16 rows of 2 KB
+constexpr int kKeysPerChunk = kSlotBytes / 2 / (kHeadDim * 2);  // 64 keys: K half + V half
+constexpr int kORowsPerChunk = kSlotBytes / (2 * kHeadDim * 2);   // 64 rows of 512 B (2 heads)
+constexpr int kGUPerChunk = kSlotBytes / 2 / (kHidden * 2);     // 8 gate rows + 8 up rows
+constexpr int kDownRowsPerChunk = kSlotBytes / (kInter * 2);    // 5 rows of 6 KB (HF layout)
+
+// Error codes written to Workspace::error[0].
+enum ErrorCode : uint32_t {
+  kErrNone = 0,
+  kErrTimeoutTransition = 1,   // a grid transition counter never reached its target
+  kErrTimeoutRing = 2,         // a shared-memory ring slot never filled / emptied
+  kErrTimeoutToken = 3,        // the greedy token broadcast never arrived
+  kErrBadArgs = 4,             // position / cache_len / token out of range
+};
+
+// Flags in DecodeParams::flags.
+enum : int {
+  kFlagLmHead = 1,          // run final norm + LM head + argmax
+  kFlagSkipFinalNorm = 2,   // LM head consumes the residual as-is (isolated LM-head checks)
+  kFlagAdvanceStep = 4,     // write the argmax and position+1 back into the step state
+};
+
+}  // namespace mkb
+
+// Reference-compatible per-layer weight table: same 11 pointers in the same
+// order as the reference's LayerWeights (config.cuh:77-89), so a device table
+// built for the reference launcher can be handed to this one unchanged.
+struct LayerWeights {
+  const __nv_bfloat16* norm_weight;
+  const __nv_bfloat16* q_weight;
+  const __nv_bfloat16* k_weight;
+  const __nv_bfloat16* v_weight;
+  const __nv_bfloat16* q_norm_weight;
+  const __nv_bfloat16* k_norm_weight;
+  const __nv_bfloat16* o_proj_weight;
+  const __nv_bfloat16* post_attn_norm_weight;
+  const __nv_bfloat16* gate_proj_weight;
+  const __nv_bfloat16* up_proj_weight;
+  const __nv_bfloat16* down_proj_weight;
+};
+
+namespace mkb {
+
+// Persistent device workspace. Zeroed once at allocation; a successful launch
+// leaves every counter and accumulator at zero again, so launches (and CUDA
+// graph replays) need no reset. After a launch that reported an error the
+// owner must zero it before the next launch.
+struct alignas(128) Workspace {
+  // Grid transition counters, one per 128-byte line. Index [layer][k]:
+  // k=0 QKV done, 1 attention+o_proj done, 2 gate/up(+down) done, 3 down done
+  // (separate-down schedule only).
+  uint32_t sync[kMaxLayers][4][32];
+  uint32_t att_sync[kMaxLayers][kNKV][32];   // split attention partials published
+  uint32_t arrive[32];                       // end-of-token arrivals (last one reduces)
+  uint32_t tok_flag[32];                     // greedy token broadcast (multi-token launches)
+  uint32_t error[32];                        // [0] code, [1] cta, [2] layer, [3] stage, [4] token
+  float acc_mid[kMaxLayers][kHidden];        // sum of o_proj partials per layer
+  float acc_down[kMaxLayers][kHidden];       // sum of down-proj partials per layer
+  float att_part[kNKV][kMaxSplits][2][kHeadDim + 4];  // split attention (m, l, o[128])
+  float qkv[kQKVRows];
+  float mlp[kInter];
+  float resid[kHidden];
+  float cand_val[kMaxGrid];
+  int cand_idx[kMaxGrid];
+};
+
+// Launch parameters (passed by value; all pointers are device pointers).
+struct DecodeParams {
+  const __nv_bfloat16* embed;        // [V, H] token embedding (gather)
+  const __nv_bfloat16* lm_head;      // [V, H] LM head rows (tied: == embed)
+  const __nv_bfloat16* final_norm;   // [H]
+  const LayerWeights* layers;        // device table, indexed by absolute layer
+  const __nv_bfloat16* const* down_t;  // device array of transposed down weights
+                                       // [I, H] per layer; null = reference layout
+  const void* cos_table;             // [max_seq, 128]
+  const void* sin_table;
+  int rope_fp32;                     // 1: tables are FP32, 0: BF16
+  __nv_bfloat16* k_cache;            // [L, 8, max_seq, 128]
+  __nv_bfloat16* v_cache;
+  int max_seq;
+  int layer_begin, layer_end;        // layers [begin, end) run this launch
+  int token, position, cache_len;    // used when step == nullptr
+  int* step;                         // device {token, position, cache_len, count} or null
+  int n_tokens;                      // greedy tokens decoded by this launch (>= 1)
+  int flags;
+  const float* input_residual;       // replaces the embedding gather when non-null
+  float* logits;                     // [V] FP32 (last token of the launch) or null
+  int* out_tokens;                   // [n_tokens] argmax ids or null
+  float* residual_out;               // [H] final residual or null
+  float* q_out;                      // raw QKV GEMV outputs (FP32)
+  float* k_out;
+  float* v_out;
+  float* mlp_out;                    // SwiGLU output [I] (reference-layout schedule)
+  Workspace* ws;
+  int grid;                          // CTAs (== gridDim.x)
+  int group_size;                    // CTAs per KV head in the attention stage
+  int splits;                        // sequence splits of the attention (>= 1)
+  unsigned long long timeout_ns;     // bound on every wait
+  int withhold_cta;                  // test hook: this CTA never publishes its first
+                                     // QKV arrival (-1 = off); the others time out
+};
+
+// ---------------------------------------------------------------------------
+// Static work split (identical on host and device).
+// ---------------------------------------------------------------------------
+__host__ __device__ inline int part(int n, int parts, int i) {
+  return (int)(((long long)n * i) / parts);
+}
+
+struct Plan {
+  int qa, qb;     // QKV rows [qa, qb) of the concatenated [Wq; Wk; Wv]
+  int in_bc;      // takes part in attention + o_proj
+  int h, c;       // KV head and index inside its group
+  int oa, ob;     // o_proj rows
+  int ja, jb;     // gate/up rows (and rows of the transposed down weight)
+  int da, db;     // down rows (reference layout)
+  int va, vb;     // LM-head rows
+};
+
+__host__ __device__ inline Plan make_plan(int cta, int grid, int group_size, int vocab) {
+  Plan p;
+  p.qa = part(kQKVRows, grid, cta);
+  p.qb = part(kQKVRows, grid, cta + 1);
+  const int nbc = kNKV * group_size;
+  p.in_bc = cta < nbc;
+  p.h = p.in_bc ? cta / group_size : 0;
+  p.c = p.in_bc ? cta % group_size : 0;
+  p.oa = p.in_bc ? part(kHidden, group_size, p.c) : 0;
+  p.ob = p.in_bc ? part(kHidden, group_size, p.c + 1) : 0;
+  p.ja = part(kInter, grid, cta);
+  p.jb = part(kInter, grid, cta + 1);
+  p.da = part(kHidden, grid, cta);
+  p.db = part(kHidden, grid, cta + 1);
+  p.va = part(vocab, grid, cta);
+  p.vb = part(vocab, grid, cta + 1);
+  return p;
+}
+
+// End of the QKV chunk that starts at row r: at most 16 rows, never crossing
+// the q/k/v matrix boundaries.
+__host__ __device__ inline int qkv_chunk_end(int r, int qb) {
+  int e = r + kRowsPerChunk1024;
+  const int bound = r < kQSize ? kQSize : (r < kQSize + kKVSize ? kQSize + kKVSize : kQKVRows);
+  if (e > bound) e = bound;
+  if (e > qb) e = qb;
+  return e;
+}
+
+// Keys [ka, kb) that CTA c of a group attends over.
+__host__ __device__ inline void key_range(int cache_len, int splits, int c, int* ka, int* kb) {
+  if (splits <= 1) { *ka = 0; *kb = cache_len; return; }
+  if (c >= splits) { *ka = 0; *kb = 0; return; }
+  *ka = part(cache_len, splits, c);
+  *kb = part(cache_len, splits, c + 1);
+}
+
+// Attention sequence splits for a launch whose longest cache is max_cache_len.
+__host__ __device__ inline int choose_splits(int max_cache_len, int group_size) {
+  if (max_cache_len <= 384) return 1;
+  int s = (max_cache_len + 255) / 256;
+  if (s > group_size) s = group_size;
+  if (s > kMaxSplits) s = kMaxSplits;
+  return s;
+}
+
+}  // namespace mkb

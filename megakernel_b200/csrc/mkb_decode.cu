@@ -1,0 +1,1003 @@
+// Persistent single-launch batch-one Qwen3-0.6B decode kernel for sm_100a.
+//
+// Structure (one CTA per SM, 17 warps):
+//   * warp 16 (producer) walks this CTA's fixed chunk schedule for the whole
+//     launch and streams every weight byte (and the KV rows that do not depend
+//     on the current token) into a 6 x 32 KB shared-memory ring with 1-D bulk
+//     async copies (cp.async.bulk, completion on mbarriers). It never waits on
+//     a grid transition (except a one-off acquire before re-reading KV rows in a
+//     multi-token launch), so HBM keeps streaming while the consumers wait.
+//   * warps 0-15 (consumers) run the stages of each layer and hand off between
+//     CTAs through gpu-scope release/acquire counters in the workspace:
+//        A  : input RMSNorm + QKV GEMV rows                        -> T_A
+//        BC : q/k RMSNorm + RoPE + KV append, GQA decode attention,
+//             o_proj partial of this KV head (red.add into acc_mid) -> T_BC
+//        DE : post RMSNorm + gate/up SwiGLU rows + down-proj partial
+//             over the same rows of the transposed down weight
+//             (red.add into acc_down)                               -> T_DE
+//        (reference-layout down weight: D writes the SwiGLU vector -> T_D,
+//         E computes whole down rows and writes the residual       -> T_E)
+//     then final RMSNorm + tied LM head + block/grid argmax.
+// Every wait is bounded by DecodeParams::timeout_ns; on expiry the kernel
+// records an error in Workspace::error, stops issuing copies, drains the ones in
+// flight and returns, so the host gets a status instead of a hang.
+//
+// Reference: megakernel.cu:744-893 (decode_kernel) and the stage functions it
+// calls (megakernel.cu:9-739); see the per-stage comments below.
+
+#include <cfloat>
+#include <climits>
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "mkb_config.cuh"
+#include "mkb_ptx.cuh"
+
+namespace mkb {
+
+struct __align__(128) Smem {
+  uint8_t ring[kSlots][kSlotBytes];
+  uint64_t full[kSlots];
+  uint64_t empty[kSlots];
+  float r[kHidden];      // residual entering the current layer
+  float rmid[kHidden];   // residual after attention + o_proj
+  union {
+    float att[kConsumerWarps][2][kHeadDim + 4];  // per-warp attention partials
+    float x[kInter];                             // SwiGLU vector (reference-layout down)
+  } u;
+  float q[2][kHeadDim];  // rotated, pre-scaled queries of this KV head's two Q heads
+  float knew[kHeadDim];  // rotated new key (BF16-rounded)
+  float vnew[kHeadDim];  // new value (BF16-rounded)
+  float attn[2 * kHeadDim];
+  float gu[2][32];
+  float m[32];
+  float dpart[8][4];
+  float red[32];
+  float best_v[kConsumerWarps];
+  int best_i[kConsumerWarps];
+  int token;
+  int is_last;
+  int abort;
+};
+
+constexpr size_t kSmemBytes = sizeof(Smem);
+static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+
+struct Ctl {
+  Smem* sm;
+  Workspace* ws;
+  uint64_t timeout;
+  int cta;
+};
+
+__device__ __forceinline__ bool aborted(const Ctl& c) {
+  return *reinterpret_cast<volatile int*>(&c.sm->abort) != 0;
+}
+
+__device__ void raise_error(const Ctl& c, uint32_t code, int layer, int stage, int tok) {
+  if (atomicCAS(&c.ws->error[0], 0u, code) == 0u) {
+    c.ws->error[1] = static_cast<uint32_t>(c.cta);
+    c.ws->error[2] = static_cast<uint32_t>(layer);
+    c.ws->error[3] = static_cast<uint32_t>(stage);
+    c.ws->error[4] = static_cast<uint32_t>(tok);
+  }
+  *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
+}
+
+// Bounded spin until *ctr >= target (wrap-safe). Single thread.
+__device__ void spin_geq(const Ctl& c, const uint32_t* ctr, uint32_t target, uint32_t code, int layer,
+                         int stage, int tok) {
+  if (aborted(c)) return;
+  if (static_cast<int>(ld_acquire(ctr) - target) >= 0) return;
+  const uint64_t t0 = global_ns();
+  uint32_t it = 0;
+  while (true) {
+    if (static_cast<int>(ld_acquire(ctr) - target) >= 0) return;
+    if ((++it & 15u) == 0u) {
+      if (ld_relaxed(&c.ws->error[0]) != 0u) {
+        *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
+        return;
+      }
+      if (global_ns() - t0 > c.timeout) {
+        raise_error(c, code, layer, stage, tok);
+        return;
+      }
+    }
+  }
+}
+
+// Consumer-side transition: thread 0 waits, then all consumers proceed.
+__device__ __forceinline__ void transition_wait(const Ctl& c, const uint32_t* ctr, uint32_t target, int layer,
+                                                int stage, int tok) {
+  if (threadIdx.x == 0) spin_geq(c, ctr, target, kErrTimeoutTransition, layer, stage, tok);
+  consumer_sync(kConsumerThreads);
+}
+
+// Consumer-side publish: every consumer's writes are ordered before the add.
+__device__ __forceinline__ void transition_publish(uint32_t* ctr) {
+  consumer_sync(kConsumerThreads);
+  if (threadIdx.x == 0) release_add(ctr, 1u);
+}
+
+// ---- ring (consumer side) ----------------------------------------------------
+__device__ __forceinline__ uint32_t ring_wait(const Ctl& c, uint32_t n, int layer, int stage, int tok) {
+  const int s = static_cast<int>(n % kSlots);
+  const uint32_t ph = (n / kSlots) & 1u;
+  if (!mbar_test(&c.sm->full[s], ph)) {
+    const uint64_t t0 = global_ns();
+    while (!mbar_test(&c.sm->full[s], ph)) {
+      if (aborted(c)) break;
+      if (global_ns() - t0 > c.timeout) {
+        raise_error(c, kErrTimeoutRing, layer, stage, tok);
+        break;
+      }
+    }
+  }
+  return smem_addr(c.sm->ring[s]);
+}
+__device__ __forceinline__ void ring_done(const Ctl& c, uint32_t& n) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&c.sm->empty[n % kSlots]);
+  ++n;
+}
+
+// ---- math helpers ------------------------------------------------------------
+// RMSNorm of a 1024-vector held in shared memory; each lane receives the 32
+// normalised elements lane*8 + g*256 + e (g < 4, e < 8) it needs for its part of
+// every 2 KB weight row. Same formula as megakernel.cu:704-739.
+__device__ void norm_to_regs(const float* v, const __nv_bfloat16* w, bool skip, float xr[32], float* s_red) {
+  const int tid = threadIdx.x;
+  const float a = v[tid], b = v[tid + kConsumerThreads];
+  const float ss = warp_sum(a * a + b * b);
+  if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+  consumer_sync(kConsumerThreads);
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kConsumerWarps; ++i) tot += s_red[i];
+  const float rstd = skip ? 1.0f : rsqrtf(tot * (1.0f / kHidden) + kEps);
+  const int lane = tid & 31;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int idx = lane * 8 + g * 256;
+    const float4 v0 = *reinterpret_cast<const float4*>(v + idx);
+    const float4 v1 = *reinterpret_cast<const float4*>(v + idx + 4);
+    uint4 wv;
+    if (skip) {
+      wv = make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);  // bf16 1.0 pairs
+    } else {
+      wv = __ldg(reinterpret_cast<const uint4*>(w + idx));
+    }
+    xr[g * 8 + 0] = v0.x * rstd * bf_lo(wv.x);
+    xr[g * 8 + 1] = v0.y * rstd * bf_hi(wv.x);
+    xr[g * 8 + 2] = v0.z * rstd * bf_lo(wv.y);
+    xr[g * 8 + 3] = v0.w * rstd * bf_hi(wv.y);
+    xr[g * 8 + 4] = v1.x * rstd * bf_lo(wv.z);
+    xr[g * 8 + 5] = v1.y * rstd * bf_hi(wv.z);
+    xr[g * 8 + 6] = v1.z * rstd * bf_lo(wv.w);
+    xr[g * 8 + 7] = v1.w * rstd * bf_hi(wv.w);
+  }
+  consumer_sync(kConsumerThreads);  // s_red free for the next reduction
+}
+
+__device__ __forceinline__ float dot8(const uint4 w, const float* x) {
+  float s = bf_lo(w.x) * x[0];
+  s = fmaf(bf_hi(w.x), x[1], s);
+  s = fmaf(bf_lo(w.y), x[2], s);
+  s = fmaf(bf_hi(w.y), x[3], s);
+  s = fmaf(bf_lo(w.z), x[4], s);
+  s = fmaf(bf_hi(w.z), x[5], s);
+  s = fmaf(bf_lo(w.w), x[6], s);
+  s = fmaf(bf_hi(w.w), x[7], s);
+  return s;
+}
+
+// This lane's share of a 2 KB (1024-element) BF16 row in shared memory.
+__device__ __forceinline__ float dot_row1024(uint32_t row, const float xr[32], int lane) {
+  const uint4 w0 = lds128(row + lane * 16 + 0 * 512);
+  const uint4 w1 = lds128(row + lane * 16 + 1 * 512);
+  const uint4 w2 = lds128(row + lane * 16 + 2 * 512);
+  const uint4 w3 = lds128(row + lane * 16 + 3 * 512);
+  return (dot8(w0, xr) + dot8(w1, xr + 8)) + (dot8(w2, xr + 16) + dot8(w3, xr + 24));
+}
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  const bool vn = v != v, bn = bv != bv;
+  if (vn || bn) return vn && (!bn || i < bi);  // torch.argmax: NaN is the maximum
+  return v > bv || (v == bv && i < bi);
+}
+
+__device__ __forceinline__ float rope_at(const void* table, int fp32, size_t idx) {
+  return fp32 ? __ldg(static_cast<const float*>(table) + idx)
+              : __bfloat162float(static_cast<const __nv_bfloat16*>(table)[idx]);
+}
+
+// Pointer field of a device-resident table, read through the read-only path.
+template <typename T>
+__device__ __forceinline__ const T* ldg_ptr(const T* const* field) {
+  return reinterpret_cast<const T*>(__ldg(reinterpret_cast<const unsigned long long*>(field)));
+}
+
+// ---- producer ----------------------------------------------------------------
+struct Producer {
+  const Ctl& c;
+  uint32_t n;
+  bool stop;
+  uint64_t pol_w, pol_kv;
+  int lane;
+
+  __device__ Producer(const Ctl& ctl) : c(ctl), n(0), stop(false) {
+    lane = threadIdx.x & 31;
+    pol_w = policy_evict_first();
+    pol_kv = policy_evict_last();
+  }
+
+  // Reserve the next slot for `bytes`; returns its index or -1 once stopped.
+  __device__ int begin(uint32_t bytes) {
+    if (stop) return -1;
+    const int s = static_cast<int>(n % kSlots);
+    const uint32_t ph = ((n / kSlots) & 1u) ^ 1u;
+    int ok = 1;
+    if (lane == 0) {
+      if (!mbar_test(&c.sm->empty[s], ph)) {
+        const uint64_t t0 = global_ns();
+        while (!mbar_test(&c.sm->empty[s], ph)) {
+          if (aborted(c)) { ok = 0; break; }
+          if (global_ns() - t0 > c.timeout) {
+            raise_error(c, kErrTimeoutRing, -1, -1, -1);
+            ok = 0;
+            break;
+          }
+        }
+      }
+      if (ok && aborted(c)) ok = 0;
+      if (ok) mbar_arrive_expect_tx(&c.sm->full[s], bytes);
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) { stop = true; return -1; }
+    return s;
+  }
+  __device__ void end() { __syncwarp(); ++n; }
+
+  // One bulk copy into slot s at byte offset off. Misaligned operands are a
+  // caller error: record it and stop instead of issuing the copy.
+  __device__ void copy(int s, uint32_t off, const void* src, uint32_t bytes, uint64_t pol) {
+    if (bytes == 0) return;
+    if (((reinterpret_cast<uintptr_t>(src) | bytes) & 15u) != 0u) {
+      raise_error(c, kErrBadArgs, -1, -2, -1);
+      return;
+    }
+    bulk_g2s(c.sm->ring[s] + off, src, bytes, &c.sm->full[s], pol);
+  }
+
+  // Wait for every copy still in flight before the CTA exits.
+  __device__ void drain() {
+    if (lane != 0) return;
+    for (int s = 0; s < kSlots; ++s) {
+      if (n <= static_cast<uint32_t>(s)) continue;
+      const uint32_t last = n - 1u - ((n - 1u - s) % kSlots);
+      const uint32_t ph = (last / kSlots) & 1u;
+      const uint64_t t0 = global_ns();
+      while (!mbar_test(&c.sm->full[s], ph)) {
+        if (global_ns() - t0 > c.timeout) break;
+      }
+    }
+  }
+};
+
+__device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int pos0, int cl0,
+                             int splits) {
+  Producer pr(c);
+  const bool fused = p.down_t != nullptr;
+  const int nbc = kNKV * p.group_size;
+  for (int t = 0; t < p.n_tokens && !pr.stop; ++t) {
+    const int pos = pos0 + t;
+    const int cl = cl0 + t;
+    for (int l = p.layer_begin; l < p.layer_end && !pr.stop; ++l) {
+      const LayerWeights* lw = p.layers + l;
+      // A: QKV rows
+      for (int r = pl.qa; r < pl.qb;) {
+        const int e = qkv_chunk_end(r, pl.qb);
+        const __nv_bfloat16* src = r < kQSize ? ldg_ptr(&lw->q_weight) + (size_t)r * kHidden
+                                   : r < kQSize + kKVSize
+                                       ? ldg_ptr(&lw->k_weight) + (size_t)(r - kQSize) * kHidden
+                                       : ldg_ptr(&lw->v_weight) + (size_t)(r - kQSize - kKVSize) * kHidden;
+        const uint32_t bytes = static_cast<uint32_t>(e - r) * kHidden * 2u;
+        const int s = pr.begin(bytes);
+        if (s < 0) break;
+        if (pr.lane == 0) pr.copy(s, 0, src, bytes, pr.pol_w);
+        pr.end();
+        r = e;
+      }
+      // BC: KV rows of this KV head (old positions only), then the o_proj slice
+      if (pl.in_bc) {
+        int ka, kb;
+        key_range(cl, splits, pl.c, &ka, &kb);
+        if (t > 0 && kb > ka && pr.lane == 0) {
+          // The previous token of this launch appended K/V at pos-1; make it
+          // visible to the bulk-copy engine before re-reading those rows.
+          spin_geq(c, &p.ws->sync[l][1][0], static_cast<uint32_t>(nbc * t), kErrTimeoutTransition, l, 10, t);
+          fence_proxy_async_global();
+        }
+        const size_t head_off = ((size_t)l * kNKV + pl.h) * (size_t)p.max_seq * kHeadDim;
+        const __nv_bfloat16* kbase = p.k_cache + head_off;
+        const __nv_bfloat16* vbase = p.v_cache + head_off;
+        for (int k0 = ka; k0 < kb; k0 += kKeysPerChunk) {
+          const int k1 = min(kb, k0 + kKeysPerChunk);
+          const bool has_pos = pos >= k0 && pos < k1;
+          const uint32_t bytes = 2u * kHeadDim * 2u * static_cast<uint32_t>(k1 - k0 - (has_pos ? 1 : 0));
+          const int s = pr.begin(bytes);
+          if (s < 0) break;
+          if (pr.lane == 0) {
+            const uint32_t row = kHeadDim * 2u;
+            if (!has_pos) {
+              pr.copy(s, 0, kbase + (size_t)k0 * kHeadDim, row * (k1 - k0), pr.pol_kv);
+              pr.copy(s, kSlotBytes / 2, vbase + (size_t)k0 * kHeadDim, row * (k1 - k0), pr.pol_kv);
+            } else {
+              pr.copy(s, 0, kbase + (size_t)k0 * kHeadDim, row * (pos - k0), pr.pol_kv);
+              pr.copy(s, kSlotBytes / 2, vbase + (size_t)k0 * kHeadDim, row * (pos - k0), pr.pol_kv);
+              pr.copy(s, row * (pos + 1 - k0), kbase + (size_t)(pos + 1) * kHeadDim, row * (k1 - pos - 1), pr.pol_kv);
+              pr.copy(s, kSlotBytes / 2 + row * (pos + 1 - k0), vbase + (size_t)(pos + 1) * kHeadDim,
+                      row * (k1 - pos - 1), pr.pol_kv);
+            }
+          }
+          pr.end();
+        }
+        const __nv_bfloat16* wo = ldg_ptr(&lw->o_proj_weight);
+        for (int o0 = pl.oa; o0 < pl.ob; o0 += kORowsPerChunk) {
+          const int o1 = min(pl.ob, o0 + kORowsPerChunk);
+          const int s = pr.begin(static_cast<uint32_t>(o1 - o0) * 512u);
+          if (s < 0) break;
+          for (int row = o0 + pr.lane; row < o1; row += 32)
+            pr.copy(s, static_cast<uint32_t>(row - o0) * 512u, wo + (size_t)row * kQSize + pl.h * 2 * kHeadDim, 512u,
+                    pr.pol_w);
+          pr.end();
+        }
+      }
+      // DE / D: gate and up rows
+      const __nv_bfloat16* wg = ldg_ptr(&lw->gate_proj_weight);
+      const __nv_bfloat16* wu = ldg_ptr(&lw->up_proj_weight);
+      for (int j0 = pl.ja; j0 < pl.jb; j0 += kGUPerChunk) {
+        const int j1 = min(pl.jb, j0 + kGUPerChunk);
+        const uint32_t half = static_cast<uint32_t>(j1 - j0) * kHidden * 2u;
+        const int s = pr.begin(2u * half);
+        if (s < 0) break;
+        if (pr.lane == 0) {
+          pr.copy(s, 0, wg + (size_t)j0 * kHidden, half, pr.pol_w);
+          pr.copy(s, kSlotBytes / 2, wu + (size_t)j0 * kHidden, half, pr.pol_w);
+        }
+        pr.end();
+      }
+      if (fused) {
+        const __nv_bfloat16* wdt = ldg_ptr(p.down_t + l);
+        for (int j0 = pl.ja; j0 < pl.jb; j0 += kRowsPerChunk1024) {
+          const int j1 = min(pl.jb, j0 + kRowsPerChunk1024);
+          const uint32_t bytes = static_cast<uint32_t>(j1 - j0) * kHidden * 2u;
+          const int s = pr.begin(bytes);
+          if (s < 0) break;
+          if (pr.lane == 0) pr.copy(s, 0, wdt + (size_t)j0 * kHidden, bytes, pr.pol_w);
+          pr.end();
+        }
+      } else {
+        const __nv_bfloat16* wd = ldg_ptr(&lw->down_proj_weight);
+        for (int d0 = pl.da; d0 < pl.db; d0 += kDownRowsPerChunk) {
+          const int d1 = min(pl.db, d0 + kDownRowsPerChunk);
+          const uint32_t bytes = static_cast<uint32_t>(d1 - d0) * kInter * 2u;
+          const int s = pr.begin(bytes);
+          if (s < 0) break;
+          if (pr.lane == 0) pr.copy(s, 0, wd + (size_t)d0 * kInter, bytes, pr.pol_w);
+          pr.end();
+        }
+      }
+    }
+    if (p.flags & kFlagLmHead) {
+      for (int v0 = pl.va; v0 < pl.vb; v0 += kRowsPerChunk1024) {
+        const int v1 = min(pl.vb, v0 + kRowsPerChunk1024);
+        const uint32_t bytes = static_cast<uint32_t>(v1 - v0) * kHidden * 2u;
+        const int s = pr.begin(bytes);
+        if (s < 0) break;
+        if (pr.lane == 0) pr.copy(s, 0, p.lm_head + (size_t)v0 * kHidden, bytes, pr.pol_w);
+        pr.end();
+      }
+    }
+  }
+  pr.drain();
+}
+
+// ---- consumers -----------------------------------------------------------------
+
+__device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int token0, int pos0, int cl0,
+                             int splits) {
+  Smem& sm = *c.sm;
+  Workspace* ws = p.ws;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const bool fused = p.down_t != nullptr;
+  const int G = p.grid;
+  const int nbc = kNKV * p.group_size;
+  const int lb = p.layer_begin, le = p.layer_end;
+  const int zero_cta = G - 1;
+  uint32_t n = 0;
+  float xr[32];
+
+  int token = token0;
+  for (int t = 0; t < p.n_tokens; ++t) {
+    const int pos = pos0 + t;
+    const int cl = cl0 + t;
+    const uint32_t tgtG = static_cast<uint32_t>(G * (t + 1));
+    const uint32_t tgtBC = static_cast<uint32_t>(nbc * (t + 1));
+
+    // ---- token input: embedding gather (megakernel.cu:783-795) ----
+    if (t > 0) {
+      if (tid == 0) spin_geq(c, &ws->tok_flag[0], static_cast<uint32_t>(t), kErrTimeoutToken, -1, 9, t);
+      consumer_sync(kConsumerThreads);
+      if (tid == 0) sm.token = static_cast<int>(__ldcg(reinterpret_cast<const int*>(&ws->tok_flag[1])));
+      consumer_sync(kConsumerThreads);
+      token = sm.token;
+    }
+    token = min(max(token, 0), kVocab - 1);
+    for (int i = tid; i < kHidden; i += kConsumerThreads)
+      sm.r[i] = p.input_residual ? __ldcg(p.input_residual + i)
+                                 : __bfloat162float(p.embed[(size_t)token * kHidden + i]);
+    consumer_sync(kConsumerThreads);
+
+    for (int l = lb; l < le; ++l) {
+      const LayerWeights* lw = p.layers + l;
+      // ================= A: RMSNorm + QKV (megakernel.cu:704-739, 633-701) ======
+      if (l > lb) {
+        transition_wait(c, &ws->sync[l - 1][fused ? 2 : 3][0], tgtG, l, 0, t);
+        for (int i = tid; i < kHidden; i += kConsumerThreads)
+          sm.r[i] = fused ? sm.rmid[i] + __ldcg(&ws->acc_down[l - 1][i]) : __ldcg(&ws->resid[i]);
+        consumer_sync(kConsumerThreads);
+      }
+      norm_to_regs(sm.r, ldg_ptr(&lw->norm_weight), false, xr, sm.red);
+      for (int r = pl.qa; r < pl.qb;) {
+        const int e = qkv_chunk_end(r, pl.qb);
+        const uint32_t sa = ring_wait(c, n, l, 0, t);
+        const int row = r + warp;
+        if (row < e) {
+          const float v = warp_sum(dot_row1024(sa + warp * 2048, xr, lane));
+          if (lane == 0) {
+            float* dst = row < kQSize ? p.q_out + row
+                         : row < kQSize + kKVSize ? p.k_out + (row - kQSize)
+                                                  : p.v_out + (row - kQSize - kKVSize);
+            *dst = v;
+          }
+        }
+        ring_done(c, n);
+        r = e;
+      }
+      if (!(t == 0 && l == lb && c.cta == p.withhold_cta)) transition_publish(&ws->sync[l][0][0]);
+      else consumer_sync(kConsumerThreads);
+
+      // ================= BC: head norm + RoPE + KV append, attention, o_proj =====
+      if (pl.in_bc) {
+        transition_wait(c, &ws->sync[l][0][0], tgtG, l, 1, t);
+        const int h = pl.h;
+        // q_norm / k_norm + rotate-half RoPE (megakernel.cu:490-630)
+        if (warp < 3) {
+          const float* src = warp < 2 ? p.q_out + (2 * h + warp) * kHeadDim : p.k_out + h * kHeadDim;
+          const float x0 = __ldcg(src + lane), x1 = __ldcg(src + lane + 32);
+          const float x2 = __ldcg(src + lane + 64), x3 = __ldcg(src + lane + 96);
+          const float ss = warp_sum(x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3);
+          const float rstd = rsqrtf(ss * (1.0f / kHeadDim) + kEps);
+          const __nv_bfloat16* nw = warp < 2 ? ldg_ptr(&lw->q_norm_weight) : ldg_ptr(&lw->k_norm_weight);
+          const float y0 = x0 * rstd * __bfloat162float(nw[lane]);
+          const float y1 = x1 * rstd * __bfloat162float(nw[lane + 32]);
+          const float y2 = x2 * rstd * __bfloat162float(nw[lane + 64]);
+          const float y3 = x3 * rstd * __bfloat162float(nw[lane + 96]);
+          const size_t rb = (size_t)pos * kHeadDim;
+          const float c0 = rope_at(p.cos_table, p.rope_fp32, rb + lane);
+          const float s0 = rope_at(p.sin_table, p.rope_fp32, rb + lane);
+          const float c1 = rope_at(p.cos_table, p.rope_fp32, rb + lane + 32);
+          const float s1 = rope_at(p.sin_table, p.rope_fp32, rb + lane + 32);
+          const float o0 = y0 * c0 - y2 * s0, o2 = y2 * c0 + y0 * s0;
+          const float o1 = y1 * c1 - y3 * s1, o3 = y3 * c1 + y1 * s1;
+          if (warp < 2) {
+            const float sc = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
+            sm.q[warp][lane] = o0 * sc;
+            sm.q[warp][lane + 32] = o1 * sc;
+            sm.q[warp][lane + 64] = o2 * sc;
+            sm.q[warp][lane + 96] = o3 * sc;
+          } else {
+            const __nv_bfloat16 b0 = __float2bfloat16(o0), b1 = __float2bfloat16(o1);
+            const __nv_bfloat16 b2 = __float2bfloat16(o2), b3 = __float2bfloat16(o3);
+            sm.knew[lane] = __bfloat162float(b0);
+            sm.knew[lane + 32] = __bfloat162float(b1);
+            sm.knew[lane + 64] = __bfloat162float(b2);
+            sm.knew[lane + 96] = __bfloat162float(b3);
+            if (pl.c == 0) {
+              __nv_bfloat16* dst = p.k_cache + (((size_t)l * kNKV + h) * p.max_seq + pos) * kHeadDim;
+              dst[lane] = b0;
+              dst[lane + 32] = b1;
+              dst[lane + 64] = b2;
+              dst[lane + 96] = b3;
+            }
+          }
+        } else if (warp == 3) {
+          __nv_bfloat16* dst = p.v_cache + (((size_t)l * kNKV + h) * p.max_seq + pos) * kHeadDim;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat16 b = __float2bfloat16(__ldcg(p.v_out + h * kHeadDim + lane + 32 * i));
+            sm.vnew[lane + 32 * i] = __bfloat162float(b);
+            if (pl.c == 0) dst[lane + 32 * i] = b;
+          }
+        }
+        consumer_sync(kConsumerThreads);
+
+        // GQA decode attention over keys [ka, kb) (megakernel.cu:228-370),
+        // per-warp online softmax in the exp2 domain, then a 16-warp combine.
+        int ka, kb;
+        key_range(cl, splits, pl.c, &ka, &kb);
+        if (kb > ka) {
+          float q0[4], q1[4];
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            q0[d] = sm.q[0][lane * 4 + d];
+            q1[d] = sm.q[1][lane * 4 + d];
+          }
+          float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+          float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int k0 = ka; k0 < kb; k0 += kKeysPerChunk) {
+            const int k1 = min(kb, k0 + kKeysPerChunk);
+            const uint32_t sa = ring_wait(c, n, l, 1, t);
+            float s0[4], s1[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int kk = k0 + warp * 4 + i;
+              float kx0 = 0.f, kx1 = 0.f, kx2 = 0.f, kx3 = 0.f;
+              if (kk < k1) {
+                if (kk == pos) {
+                  kx0 = sm.knew[lane * 4 + 0];
+                  kx1 = sm.knew[lane * 4 + 1];
+                  kx2 = sm.knew[lane * 4 + 2];
+                  kx3 = sm.knew[lane * 4 + 3];
+                } else {
+                  const uint2 u = lds64(sa + (kk - k0) * (kHeadDim * 2) + lane * 8);
+                  kx0 = bf_lo(u.x);
+                  kx1 = bf_hi(u.x);
+                  kx2 = bf_lo(u.y);
+                  kx3 = bf_hi(u.y);
+                }
+              }
+              s0[i] = fmaf(q0[3], kx3, fmaf(q0[2], kx2, fmaf(q0[1], kx1, q0[0] * kx0)));
+              s1[i] = fmaf(q1[3], kx3, fmaf(q1[2], kx2, fmaf(q1[1], kx1, q1[0] * kx0)));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                s0[i] += __shfl_xor_sync(0xffffffffu, s0[i], o);
+                s1[i] += __shfl_xor_sync(0xffffffffu, s1[i], o);
+              }
+            }
+            float mx0 = m0, mx1 = m1;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              if (k0 + warp * 4 + i >= k1) {
+                s0[i] = -INFINITY;
+                s1[i] = -INFINITY;
+              }
+              mx0 = fmaxf(mx0, s0[i]);
+              mx1 = fmaxf(mx1, s1[i]);
+            }
+            float p0[4] = {0.f, 0.f, 0.f, 0.f}, p1[4] = {0.f, 0.f, 0.f, 0.f};
+            if (mx0 > -INFINITY) {
+              const float sc = exp2f(m0 - mx0);
+              float ps = 0.f;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                p0[i] = exp2f(s0[i] - mx0);
+                ps += p0[i];
+              }
+              l0 = l0 * sc + ps;
+#pragma unroll
+              for (int d = 0; d < 4; ++d) a0[d] *= sc;
+              m0 = mx0;
+            }
+            if (mx1 > -INFINITY) {
+              const float sc = exp2f(m1 - mx1);
+              float ps = 0.f;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                p1[i] = exp2f(s1[i] - mx1);
+                ps += p1[i];
+              }
+              l1 = l1 * sc + ps;
+#pragma unroll
+              for (int d = 0; d < 4; ++d) a1[d] *= sc;
+              m1 = mx1;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int kk = k0 + warp * 4 + i;
+              if (kk < k1) {
+                float vx[4];
+                if (kk == pos) {
+#pragma unroll
+                  for (int d = 0; d < 4; ++d) vx[d] = sm.vnew[lane * 4 + d];
+                } else {
+                  const uint2 u = lds64(sa + kSlotBytes / 2 + (kk - k0) * (kHeadDim * 2) + lane * 8);
+                  vx[0] = bf_lo(u.x);
+                  vx[1] = bf_hi(u.x);
+                  vx[2] = bf_lo(u.y);
+                  vx[3] = bf_hi(u.y);
+                }
+#pragma unroll
+                for (int d = 0; d < 4; ++d) {
+                  a0[d] = fmaf(p0[i], vx[d], a0[d]);
+                  a1[d] = fmaf(p1[i], vx[d], a1[d]);
+                }
+              }
+            }
+            ring_done(c, n);
+          }
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            sm.u.att[warp][0][lane * 4 + d] = a0[d];
+            sm.u.att[warp][1][lane * 4 + d] = a1[d];
+          }
+          if (lane == 0) {
+            sm.u.att[warp][0][kHeadDim] = m0;
+            sm.u.att[warp][0][kHeadDim + 1] = l0;
+            sm.u.att[warp][1][kHeadDim] = m1;
+            sm.u.att[warp][1][kHeadDim + 1] = l1;
+          }
+          consumer_sync(kConsumerThreads);
+          if (tid < 2 * kHeadDim) {
+            const int hh = tid >> 7, d = tid & (kHeadDim - 1);
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.u.att[w][hh][kHeadDim]);
+            float L = 0.f, O = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+              const float mw = sm.u.att[w][hh][kHeadDim];
+              const float f = mw > -INFINITY ? exp2f(mw - M) : 0.f;
+              L = fmaf(sm.u.att[w][hh][kHeadDim + 1], f, L);
+              O = fmaf(sm.u.att[w][hh][d], f, O);
+            }
+            if (splits <= 1) {
+              sm.attn[tid] = O / L;
+            } else {
+              float* dst = ws->att_part[h][pl.c][hh];
+              dst[d] = O;
+              if (d == 0) {
+                dst[kHeadDim] = M;
+                dst[kHeadDim + 1] = L;
+              }
+            }
+          }
+          consumer_sync(kConsumerThreads);
+          if (splits > 1 && tid == 0) release_add(&ws->att_sync[l][h][0], 1u);
+        }
+        if (splits > 1) {
+          transition_wait(c, &ws->att_sync[l][h][0], static_cast<uint32_t>(splits * (t + 1)), l, 2, t);
+          if (tid < 2 * kHeadDim) {
+            const int hh = tid >> 7, d = tid & (kHeadDim - 1);
+            float M = -INFINITY;
+            for (int s = 0; s < splits; ++s) M = fmaxf(M, __ldcg(&ws->att_part[h][s][hh][kHeadDim]));
+            float L = 0.f, O = 0.f;
+            for (int s = 0; s < splits; ++s) {
+              const float ms = __ldcg(&ws->att_part[h][s][hh][kHeadDim]);
+              const float f = ms > -INFINITY ? exp2f(ms - M) : 0.f;
+              L = fmaf(__ldcg(&ws->att_part[h][s][hh][kHeadDim + 1]), f, L);
+              O = fmaf(__ldcg(&ws->att_part[h][s][hh][d]), f, O);
+            }
+            sm.attn[tid] = O / L;
+          }
+          consumer_sync(kConsumerThreads);
+        }
+
+        // o_proj partial of this KV head's two Q heads (megakernel.cu:191-225)
+        {
+          float xo[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) xo[e] = sm.attn[lane * 8 + e];
+          for (int o0 = pl.oa; o0 < pl.ob; o0 += kORowsPerChunk) {
+            const int o1 = min(pl.ob, o0 + kORowsPerChunk);
+            const uint32_t sa = ring_wait(c, n, l, 3, t);
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int row = o0 + warp * 4 + i;
+              v[i] = row < o1 ? dot8(lds128(sa + (row - o0) * 512 + lane * 16), xo) : 0.f;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
+            }
+            if (lane < 4) {
+              const int row = o0 + warp * 4 + lane;
+              const float val = lane == 0 ? v[0] : lane == 1 ? v[1] : lane == 2 ? v[2] : v[3];
+              if (row < o1) red_add_f32(&ws->acc_mid[l][row], val);
+            }
+            ring_done(c, n);
+          }
+        }
+        transition_publish(&ws->sync[l][1][0]);
+      }
+      // Zero the previous layer's accumulators: every CTA has read them (it
+      // passed T_A of this layer), and their next use is the next token.
+      if (c.cta == zero_cta && l > lb) {
+        if (!pl.in_bc) transition_wait(c, &ws->sync[l][0][0], tgtG, l, 1, t);
+        for (int i = tid; i < kHidden; i += kConsumerThreads) {
+          ws->acc_mid[l - 1][i] = 0.f;
+          ws->acc_down[l - 1][i] = 0.f;
+        }
+      }
+
+      // ================= DE: post norm, SwiGLU rows, down partial ===============
+      transition_wait(c, &ws->sync[l][1][0], tgtBC, l, 4, t);
+      for (int i = tid; i < kHidden; i += kConsumerThreads) sm.rmid[i] = sm.r[i] + __ldcg(&ws->acc_mid[l][i]);
+      consumer_sync(kConsumerThreads);
+      norm_to_regs(sm.rmid, ldg_ptr(&lw->post_attn_norm_weight), false, xr, sm.red);
+      // gate/up rows (megakernel.cu:100-142)
+      for (int j0 = pl.ja; j0 < pl.jb; j0 += kGUPerChunk) {
+        const int j1 = min(pl.jb, j0 + kGUPerChunk);
+        const uint32_t sa = ring_wait(c, n, l, 4, t);
+        const int jj = j0 + (warp & 7);
+        if (jj < j1) {
+          const float v =
+              warp_sum(dot_row1024(sa + (warp >= 8 ? kSlotBytes / 2 : 0) + (warp & 7) * 2048, xr, lane));
+          if (lane == 0) sm.gu[warp >> 3][jj - pl.ja] = v;
+        }
+        ring_done(c, n);
+      }
+      consumer_sync(kConsumerThreads);
+      if (tid < pl.jb - pl.ja) {
+        const float g = sm.gu[0][tid], u = sm.gu[1][tid];
+        sm.m[tid] = g / (1.0f + expf(-g)) * u;  // silu (config.cuh:177-179) * up
+      }
+      consumer_sync(kConsumerThreads);
+      if (fused) {
+        // down-proj partial over this CTA's intermediate rows: warp w owns
+        // outputs [64w, 64w+64), two per lane (megakernel.cu:53-90, split by K)
+        const int col = warp * 64 + lane * 2;
+        float pa = 0.f, pb = 0.f;
+        for (int j0 = pl.ja; j0 < pl.jb; j0 += kRowsPerChunk1024) {
+          const int j1 = min(pl.jb, j0 + kRowsPerChunk1024);
+          const uint32_t sa = ring_wait(c, n, l, 5, t);
+          for (int jj = j0; jj < j1; ++jj) {
+            const uint32_t w = lds32(sa + (jj - j0) * 2048 + col * 2);
+            const float mj = sm.m[jj - pl.ja];
+            pa = fmaf(bf_lo(w), mj, pa);
+            pb = fmaf(bf_hi(w), mj, pb);
+          }
+          ring_done(c, n);
+        }
+        red_add_v2_f32(&ws->acc_down[l][col], pa, pb);
+        transition_publish(&ws->sync[l][2][0]);
+      } else {
+        // reference layout: publish the SwiGLU vector, then whole down rows
+        for (int j = tid; j < pl.jb - pl.ja; j += kConsumerThreads) p.mlp_out[pl.ja + j] = sm.m[j];
+        transition_publish(&ws->sync[l][2][0]);
+        transition_wait(c, &ws->sync[l][2][0], tgtG, l, 6, t);
+        for (int i = tid; i < kInter; i += kConsumerThreads) sm.u.x[i] = __ldcg(p.mlp_out + i);
+        consumer_sync(kConsumerThreads);
+        for (int d0 = pl.da; d0 < pl.db; d0 += kDownRowsPerChunk) {
+          const int d1 = min(pl.db, d0 + kDownRowsPerChunk);
+          const uint32_t sa = ring_wait(c, n, l, 6, t);
+          const int row = warp / 3, third = warp % 3;
+          if (warp < 15 && d0 + row < d1) {
+            float acc = 0.f;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int e = third * kHidden + lane * 8 + g * 256;
+              const uint4 w = lds128(sa + row * (kInter * 2) + e * 2);
+              acc += dot8(w, sm.u.x + e);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) sm.dpart[row][third] = acc;
+          }
+          ring_done(c, n);
+          consumer_sync(kConsumerThreads);
+          if (tid < d1 - d0) {
+            const int d = d0 + tid;
+            ws->resid[d] = sm.rmid[d] + (sm.dpart[tid][0] + sm.dpart[tid][1] + sm.dpart[tid][2]);
+          }
+          consumer_sync(kConsumerThreads);
+        }
+        transition_publish(&ws->sync[l][3][0]);
+      }
+    }
+
+    // ================= final residual, LM head + argmax (megakernel.cu:870-886) ==
+    if (le > lb) {
+      transition_wait(c, &ws->sync[le - 1][fused ? 2 : 3][0], tgtG, le - 1, 7, t);
+      for (int i = tid; i < kHidden; i += kConsumerThreads)
+        sm.r[i] = fused ? sm.rmid[i] + __ldcg(&ws->acc_down[le - 1][i]) : __ldcg(&ws->resid[i]);
+      consumer_sync(kConsumerThreads);
+    }
+    if (c.cta == 0 && p.residual_out != nullptr && t == p.n_tokens - 1)
+      for (int i = tid; i < kHidden; i += kConsumerThreads) p.residual_out[i] = sm.r[i];
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    if (p.flags & kFlagLmHead) {
+      norm_to_regs(sm.r, p.final_norm, (p.flags & kFlagSkipFinalNorm) != 0, xr, sm.red);
+      for (int v0 = pl.va; v0 < pl.vb; v0 += kRowsPerChunk1024) {
+        const int v1 = min(pl.vb, v0 + kRowsPerChunk1024);
+        const uint32_t sa = ring_wait(c, n, -1, 8, t);
+        const int row = v0 + warp;
+        if (row < v1) {
+          const float v = warp_sum(dot_row1024(sa + warp * 2048, xr, lane));
+          if (lane == 0 && p.logits != nullptr) p.logits[row] = v;
+          if (better(v, row, bv, bi)) {
+            bv = v;
+            bi = row;
+          }
+        }
+        ring_done(c, n);
+      }
+      if (lane == 0) {
+        sm.best_v[warp] = bv;
+        sm.best_i[warp] = bi;
+      }
+      consumer_sync(kConsumerThreads);
+      if (tid == 0) {
+        for (int w = 0; w < kConsumerWarps; ++w)
+          if (better(sm.best_v[w], sm.best_i[w], bv, bi)) {
+            bv = sm.best_v[w];
+            bi = sm.best_i[w];
+          }
+        ws->cand_val[c.cta] = bv;
+        ws->cand_idx[c.cta] = bi;
+      }
+    }
+
+    // ---- end of token: the last CTA to arrive reduces the argmax and resets ---
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) {
+      // One thread decides for the whole CTA, so every consumer takes the same path.
+      if (aborted(c)) {
+        sm.is_last = -1;
+      } else {
+        uint32_t old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&ws->arrive[0]) : "memory");
+        sm.is_last = (old == tgtG - 1u) ? 1 : 0;
+      }
+    }
+    consumer_sync(kConsumerThreads);
+    const int last_state = sm.is_last;
+    consumer_sync(kConsumerThreads);
+    if (last_state < 0) return;
+    if (last_state) {
+      int best = -1;
+      if (p.flags & kFlagLmHead) {
+        float v = -INFINITY;
+        int i = INT_MAX;
+        if (tid < G) {
+          v = __ldcg(&ws->cand_val[tid]);
+          i = __ldcg(&ws->cand_idx[tid]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+          if (better(ov, oi, v, i)) {
+            v = ov;
+            i = oi;
+          }
+        }
+        if (lane == 0) {
+          sm.best_v[warp] = v;
+          sm.best_i[warp] = i;
+        }
+        consumer_sync(kConsumerThreads);
+        if (tid == 0) {
+          v = sm.best_v[0];
+          i = sm.best_i[0];
+          for (int w = 1; w < kConsumerWarps; ++w)
+            if (better(sm.best_v[w], sm.best_i[w], v, i)) {
+              v = sm.best_v[w];
+              i = sm.best_i[w];
+            }
+          best = i;
+        }
+      }
+      for (int i = tid; i < kHidden; i += kConsumerThreads) {
+        ws->acc_mid[le > lb ? le - 1 : 0][i] = 0.f;
+        ws->acc_down[le > lb ? le - 1 : 0][i] = 0.f;
+      }
+      const bool last_tok = t == p.n_tokens - 1;
+      if (last_tok) {
+        for (int i = tid; i < kMaxLayers * 4; i += kConsumerThreads) ws->sync[i >> 2][i & 3][0] = 0u;
+        for (int i = tid; i < kMaxLayers * kNKV; i += kConsumerThreads) ws->att_sync[i / kNKV][i % kNKV][0] = 0u;
+      }
+      consumer_sync(kConsumerThreads);
+      if (tid == 0) {
+        if (p.flags & kFlagLmHead) {
+          if (p.out_tokens != nullptr) p.out_tokens[t] = best;
+          if (p.step != nullptr && (p.flags & kFlagAdvanceStep)) {
+            p.step[0] = best;
+            p.step[1] = pos + 1;
+            p.step[3] += 1;
+          }
+        }
+        if (last_tok) {
+          ws->arrive[0] = 0u;
+          ws->tok_flag[0] = 0u;
+        } else {
+          ws->tok_flag[1] = static_cast<uint32_t>(best);
+          __threadfence();
+          st_release(&ws->tok_flag[0], static_cast<uint32_t>(t + 1));
+        }
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem* sm = reinterpret_cast<Smem*>(smem_raw);
+  Ctl c{sm, p.ws, p.timeout_ns, static_cast<int>(blockIdx.x)};
+
+  int token = p.token, pos = p.position, cl = p.cache_len;
+  if (p.step != nullptr) {
+    token = __ldcg(p.step + 0);
+    pos = __ldcg(p.step + 1);
+    cl = pos + 1;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&sm->full[s], 1);
+      mbar_init(&sm->empty[s], kConsumerWarps);
+    }
+    sm->abort = 0;
+    sm->is_last = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // Attention splits: fixed for the launch, from its longest cache (the step
+  // state may supply the position, so this is decided on the device).
+  const int last_cl = cl + p.n_tokens - 1;
+  const int splits = p.splits > 0 ? p.splits : choose_splits(last_cl, p.group_size);
+  // Argument guard (uniform over the grid, before any wait).
+  if (token < 0 || token >= kVocab || pos < 0 || pos + p.n_tokens > p.max_seq || cl < 1 ||
+      last_cl > p.max_seq || p.grid != static_cast<int>(gridDim.x) || p.grid > kMaxGrid ||
+      p.group_size * kNKV > p.grid || splits < 1 || splits > kMaxSplits ||
+      (splits > 1 && splits > p.group_size)) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(c, kErrBadArgs, -1, -1, -1);
+    return;
+  }
+
+  const Plan pl = make_plan(blockIdx.x, p.grid, p.group_size, kVocab);
+  if (threadIdx.x >= kConsumerThreads) {
+    producer_run(p, pl, c, pos, cl, splits);
+  } else {
+    consumer_run(p, pl, c, token, pos, cl, splits);
+  }
+}
+
+// ---- host-side launch ----------------------------------------------------------
+cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 64 && !configured[dev]) {
+    e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_kernel, p);
+}
+
+size_t decode_smem_bytes() { return kSmemBytes; }
+
+}  // namespace mkb

@@ -1,0 +1,458 @@
+// Host side of libmkb200.so: the C ABI declared in include/mkb200.h.
+//
+//  * launch_decode_kernel -- drop-in for the reference launcher
+//    (megakernel.cu:898-994): same arguments, reference weight layout.
+//  * mkb_decode            -- explicit-argument launch of the same kernel.
+//  * mkb_engine_*          -- resident engine: device LayerWeights table,
+//    transposed down weights, workspace, step state and a CUDA graph of the
+//    per-token launch stay alive across tokens (the reference rebuilt and freed
+//    its table on every call, pytorch_binding.cu:84-126).
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/mkb200.h"
+#include "mkb_config.cuh"
+
+namespace mkb {
+cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream);
+size_t decode_smem_bytes();
+}  // namespace mkb
+
+using namespace mkb;
+
+namespace {
+
+constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s per wait
+
+struct DeviceInfo {
+  int sms = 0;
+  void* ws = nullptr;
+};
+std::mutex g_mu;
+DeviceInfo g_dev[64];
+
+cudaError_t device_info(int dev, DeviceInfo** out) {
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.sms == 0) {
+    cudaError_t e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
+  *out = &d;
+  return cudaSuccess;
+}
+
+cudaError_t default_ws(int dev, void** out) {
+  DeviceInfo* d = nullptr;
+  cudaError_t e = device_info(dev, &d);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (d->ws == nullptr) {
+    void* p = nullptr;
+    e = cudaMalloc(&p, sizeof(Workspace));
+    if (e != cudaSuccess) return e;
+    e = cudaMemset(p, 0, sizeof(Workspace));
+    if (e != cudaSuccess) return e;
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return e;
+    d->ws = p;
+  }
+  *out = d->ws;
+  return cudaSuccess;
+}
+
+int grid_for(int sms) { return sms > kMaxGrid ? kMaxGrid : sms; }
+
+// Fill DecodeParams from the C argument block; resolves every default.
+cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p) {
+  if (a == nullptr) return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  DeviceInfo* d = nullptr;
+  e = device_info(dev, &d);
+  if (e != cudaSuccess) return e;
+  void* ws = a->workspace;
+  if (ws == nullptr) {
+    e = default_ws(dev, &ws);
+    if (e != cudaSuccess) return e;
+  }
+  std::memset(p, 0, sizeof(*p));
+  p->embed = static_cast<const __nv_bfloat16*>(a->embed);
+  p->lm_head = static_cast<const __nv_bfloat16*>(a->lm_head ? a->lm_head : a->embed);
+  p->final_norm = static_cast<const __nv_bfloat16*>(a->final_norm);
+  p->layers = static_cast<const LayerWeights*>(a->layers);
+  p->down_t = static_cast<const __nv_bfloat16* const*>(a->down_t);
+  p->cos_table = a->cos_table;
+  p->sin_table = a->sin_table;
+  p->rope_fp32 = a->rope_fp32;
+  p->k_cache = static_cast<__nv_bfloat16*>(a->k_cache);
+  p->v_cache = static_cast<__nv_bfloat16*>(a->v_cache);
+  p->max_seq = a->max_seq;
+  p->layer_begin = a->layer_begin;
+  p->layer_end = a->layer_end;
+  p->token = a->token;
+  p->position = a->position;
+  p->cache_len = a->cache_len;
+  p->step = a->step;
+  p->n_tokens = a->n_tokens < 1 ? 1 : a->n_tokens;
+  p->flags = a->flags;
+  p->input_residual = a->input_residual;
+  p->logits = a->logits;
+  p->out_tokens = a->out_tokens;
+  p->residual_out = a->residual_out;
+  Workspace* w = static_cast<Workspace*>(ws);
+  p->q_out = a->q_out ? a->q_out : w->qkv;
+  p->k_out = a->k_out ? a->k_out : w->qkv + kQSize;
+  p->v_out = a->v_out ? a->v_out : w->qkv + kQSize + kKVSize;
+  p->mlp_out = a->mlp_out ? a->mlp_out : w->mlp;
+  p->ws = w;
+  p->grid = a->grid > 0 ? a->grid : grid_for(d->sms);
+  if (p->grid > d->sms || p->grid > kMaxGrid || p->grid < 128) return cudaErrorInvalidConfiguration;
+  p->group_size = p->grid / kNKV;
+  p->splits = a->splits > 0 ? a->splits : 0;  // 0: chosen on the device per launch
+  if (p->splits > kMaxSplits || p->splits > p->group_size) return cudaErrorInvalidValue;
+  p->timeout_ns = a->timeout_ns ? a->timeout_ns : kDefaultTimeoutNs;
+  p->withhold_cta = a->withhold_cta;
+  // Host-side validation of what the host can see (the kernel re-checks the rest).
+  if (!p->embed || !p->layers || !p->k_cache || !p->v_cache || !p->cos_table || !p->sin_table)
+    return cudaErrorInvalidValue;
+  if (p->layer_begin < 0 || p->layer_end < p->layer_begin || p->layer_end > kMaxLayers) return cudaErrorInvalidValue;
+  if ((p->flags & kFlagLmHead) && !(p->flags & kFlagSkipFinalNorm) && !p->final_norm) return cudaErrorInvalidValue;
+  if (p->max_seq < 1) return cudaErrorInvalidValue;
+  if (!a->step) {
+    if (a->token < 0 || a->token >= kVocab) return cudaErrorInvalidValue;
+    if (a->position < 0 || a->position + p->n_tokens > a->max_seq) return cudaErrorInvalidValue;
+    if (a->cache_len < 1 || a->cache_len + p->n_tokens - 1 > a->max_seq) return cudaErrorInvalidValue;
+  }
+  auto misaligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) != 0u; };
+  if (misaligned(p->embed) || misaligned(p->lm_head) || misaligned(p->k_cache) || misaligned(p->v_cache))
+    return cudaErrorMisalignedAddress;
+  return cudaSuccess;
+}
+
+// [1024, 3072] -> [3072, 1024] BF16 transpose through 32x32 shared tiles.
+__global__ void transpose_down_kernel(const __nv_bfloat16* __restrict__ src, __nv_bfloat16* __restrict__ dst) {
+  __shared__ __nv_bfloat16 tile[32][33];
+  const int bx = blockIdx.x * 32, by = blockIdx.y * 32;  // bx over 3072 cols, by over 1024 rows
+  for (int i = threadIdx.y; i < 32; i += blockDim.y)
+    tile[i][threadIdx.x] = src[(size_t)(by + i) * kInter + bx + threadIdx.x];
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y)
+    dst[(size_t)(bx + i) * kHidden + by + threadIdx.x] = tile[threadIdx.x][i];
+}
+
+}  // namespace
+
+extern "C" {
+
+int mkb_version(void) { return 1; }
+size_t mkb_workspace_bytes(void) { return sizeof(Workspace); }
+size_t mkb_smem_bytes(void) { return decode_smem_bytes(); }
+
+void mkb_decode_args_init(mkb_decode_args* a) {
+  std::memset(a, 0, sizeof(*a));
+  a->n_tokens = 1;
+  a->withhold_cta = -1;
+  a->layer_end = kMaxLayers;
+  a->flags = MKB_FLAG_LM_HEAD;
+}
+
+cudaError_t mkb_decode(const mkb_decode_args* a, cudaStream_t stream) {
+  DecodeParams p;
+  cudaError_t e = to_params(a, &p);
+  if (e != cudaSuccess) return e;
+  return launch_decode(p, stream);
+}
+
+cudaError_t launch_decode_kernel(int token_id, const void* embed_weight, const void* lm_head_weight,
+                                 const void* final_norm_weight, const void* layer_weights,
+                                 const void* cos_table, const void* sin_table, void* k_cache, void* v_cache,
+                                 void* hidden_buffer, void* g_residual, void* g_activations,
+                                 void* g_attn_output, void* g_normalized, void* g_mlp_intermediate,
+                                 void* g_logits, void* g_q, void* g_k, void* g_v, int position, int cache_len,
+                                 int max_seq_len, cudaStream_t stream) {
+  (void)hidden_buffer;
+  (void)g_activations;
+  (void)g_attn_output;
+  (void)g_normalized;
+  mkb_decode_args a;
+  mkb_decode_args_init(&a);
+  a.embed = embed_weight;
+  a.lm_head = lm_head_weight;
+  a.final_norm = final_norm_weight;
+  a.layers = layer_weights;
+  a.cos_table = cos_table;
+  a.sin_table = sin_table;
+  a.rope_fp32 = 0;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.max_seq = max_seq_len;
+  a.layer_begin = 0;
+  a.layer_end = kMaxLayers;
+  a.token = token_id;
+  a.position = position;
+  a.cache_len = cache_len;
+  a.flags = MKB_FLAG_LM_HEAD;
+  a.logits = static_cast<float*>(g_logits);
+  a.residual_out = static_cast<float*>(g_residual);
+  a.q_out = static_cast<float*>(g_q);
+  a.k_out = static_cast<float*>(g_k);
+  a.v_out = static_cast<float*>(g_v);
+  a.mlp_out = static_cast<float*>(g_mlp_intermediate);
+  return mkb_decode(&a, stream);
+}
+
+cudaError_t mkb_default_workspace(int device, void** out) { return default_ws(device, out); }
+
+cudaError_t mkb_workspace_reset(void* workspace, cudaStream_t stream) {
+  return cudaMemsetAsync(workspace, 0, sizeof(Workspace), stream);
+}
+
+cudaError_t mkb_workspace_status(const void* workspace, uint32_t out[8]) {
+  const Workspace* w = static_cast<const Workspace*>(workspace);
+  return cudaMemcpy(out, w->error, 8 * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+}
+
+const char* mkb_error_name(uint32_t code) {
+  switch (code) {
+    case kErrNone: return "ok";
+    case kErrTimeoutTransition: return "timeout waiting for a grid transition";
+    case kErrTimeoutRing: return "timeout waiting for a shared-memory ring slot";
+    case kErrTimeoutToken: return "timeout waiting for the greedy token broadcast";
+    case kErrBadArgs: return "bad arguments (range or alignment) seen on the device";
+    default: return "unknown";
+  }
+}
+
+cudaError_t mkb_transpose_down(const void* down, void* down_t, cudaStream_t stream) {
+  dim3 grid(kInter / 32, kHidden / 32), block(32, 8);
+  transpose_down_kernel<<<grid, block, 0, stream>>>(static_cast<const __nv_bfloat16*>(down),
+                                                    static_cast<__nv_bfloat16*>(down_t));
+  return cudaGetLastError();
+}
+
+int mkb_plan_query(int grid, int cta, int32_t out[16]) {
+  if (grid < kNKV || cta < 0 || cta >= grid) return -1;
+  const int gs = grid / kNKV;
+  const Plan p = make_plan(cta, grid, gs, kVocab);
+  const int32_t v[14] = {p.qa, p.qb, p.in_bc, p.h, p.c, p.oa, p.ob, p.ja, p.jb, p.da, p.db, p.va, p.vb, gs};
+  for (int i = 0; i < 14; ++i) out[i] = v[i];
+  return 0;
+}
+int mkb_choose_splits(int max_cache_len, int group_size) { return choose_splits(max_cache_len, group_size); }
+void mkb_key_range(int cache_len, int splits, int c, int32_t out[2]) {
+  int a, b;
+  key_range(cache_len, splits, c, &a, &b);
+  out[0] = a;
+  out[1] = b;
+}
+int mkb_qkv_chunk_end(int r, int qb) { return qkv_chunk_end(r, qb); }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Resident engine
+// ---------------------------------------------------------------------------
+struct mkb_engine {
+  int device = 0;
+  int n_layers = 0;
+  int max_seq = 0;
+  int grid = 0;
+  LayerWeights* d_layers = nullptr;
+  __nv_bfloat16* d_down_t_buf = nullptr;      // n_layers * [3072, 1024]
+  __nv_bfloat16** d_down_t = nullptr;         // n_layers pointers
+  void* ws = nullptr;
+  int* d_step = nullptr;                      // {token, position, -, count}
+  int* d_out = nullptr;                       // argmax of the last step
+  float* d_logits = nullptr;
+  bool own_logits = false;
+  int* h_io = nullptr;                        // pinned: [0..3] in, [4..7] out
+  cudaGraphExec_t graph = nullptr;
+  cudaStream_t cap_stream = nullptr;
+  mkb_decode_args step_args;
+};
+
+namespace {
+void engine_free(mkb_engine* e) {
+  if (!e) return;
+  if (e->graph) cudaGraphExecDestroy(e->graph);
+  if (e->cap_stream) cudaStreamDestroy(e->cap_stream);
+  cudaFree(e->d_layers);
+  cudaFree(e->d_down_t_buf);
+  cudaFree(e->d_down_t);
+  cudaFree(e->ws);
+  cudaFree(e->d_step);
+  cudaFree(e->d_out);
+  if (e->own_logits) cudaFree(e->d_logits);
+  if (e->h_io) cudaFreeHost(e->h_io);
+  delete e;
+}
+
+cudaError_t engine_check_status(mkb_engine* e) {
+  uint32_t st[8];
+  cudaError_t err = mkb_workspace_status(e->ws, st);
+  if (err != cudaSuccess) return err;
+  if (st[0] != 0) {
+    fprintf(stderr, "mkb200: in-kernel error %u (%s) cta=%u layer=%d stage=%d token=%d\n", st[0],
+            mkb_error_name(st[0]), st[1], static_cast<int>(st[2]), static_cast<int>(st[3]),
+            static_cast<int>(st[4]));
+    cudaMemset(e->ws, 0, sizeof(Workspace));
+    cudaDeviceSynchronize();
+    return cudaErrorLaunchFailure;
+  }
+  return cudaSuccess;
+}
+}  // namespace
+
+extern "C" {
+
+cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
+  if (!m || !out || !m->layer_weights || m->n_layers < 1 || m->n_layers > kMaxLayers || m->max_seq < 1)
+    return cudaErrorInvalidValue;
+  *out = nullptr;
+  mkb_engine* e = new mkb_engine();
+  cudaError_t err = cudaGetDevice(&e->device);
+#define MKB_TRY(x)        \
+  do {                    \
+    err = (x);            \
+    if (err != cudaSuccess) { engine_free(e); return err; } \
+  } while (0)
+  if (err != cudaSuccess) { engine_free(e); return err; }
+  DeviceInfo* d = nullptr;
+  MKB_TRY(device_info(e->device, &d));
+  e->grid = grid_for(d->sms);
+  e->n_layers = m->n_layers;
+  e->max_seq = m->max_seq;
+
+  std::vector<LayerWeights> host(m->n_layers);
+  for (int l = 0; l < m->n_layers; ++l) {
+    const void* const* w = m->layer_weights + (size_t)l * 11;
+    for (int i = 0; i < 11; ++i)
+      if (w[i] == nullptr || (reinterpret_cast<uintptr_t>(w[i]) & 15u)) { engine_free(e); return cudaErrorInvalidValue; }
+    host[l] = LayerWeights{static_cast<const __nv_bfloat16*>(w[0]), static_cast<const __nv_bfloat16*>(w[1]),
+                           static_cast<const __nv_bfloat16*>(w[2]), static_cast<const __nv_bfloat16*>(w[3]),
+                           static_cast<const __nv_bfloat16*>(w[4]), static_cast<const __nv_bfloat16*>(w[5]),
+                           static_cast<const __nv_bfloat16*>(w[6]), static_cast<const __nv_bfloat16*>(w[7]),
+                           static_cast<const __nv_bfloat16*>(w[8]), static_cast<const __nv_bfloat16*>(w[9]),
+                           static_cast<const __nv_bfloat16*>(w[10])};
+  }
+  MKB_TRY(cudaMalloc(&e->d_layers, sizeof(LayerWeights) * m->n_layers));
+  MKB_TRY(cudaMemcpy(e->d_layers, host.data(), sizeof(LayerWeights) * m->n_layers, cudaMemcpyHostToDevice));
+  if (m->fused_down) {
+    const size_t per = (size_t)kInter * kHidden;
+    MKB_TRY(cudaMalloc(&e->d_down_t_buf, per * sizeof(__nv_bfloat16) * m->n_layers));
+    std::vector<__nv_bfloat16*> ptrs(m->n_layers);
+    for (int l = 0; l < m->n_layers; ++l) {
+      ptrs[l] = e->d_down_t_buf + per * l;
+      MKB_TRY(mkb_transpose_down(host[l].down_proj_weight, ptrs[l], 0));
+    }
+    MKB_TRY(cudaMalloc(&e->d_down_t, sizeof(void*) * m->n_layers));
+    MKB_TRY(cudaMemcpy(e->d_down_t, ptrs.data(), sizeof(void*) * m->n_layers, cudaMemcpyHostToDevice));
+  }
+  MKB_TRY(cudaMalloc(&e->ws, sizeof(Workspace)));
+  MKB_TRY(cudaMemset(e->ws, 0, sizeof(Workspace)));
+  MKB_TRY(cudaMalloc(&e->d_step, 4 * sizeof(int)));
+  MKB_TRY(cudaMemset(e->d_step, 0, 4 * sizeof(int)));
+  MKB_TRY(cudaMalloc(&e->d_out, 4 * sizeof(int)));
+  if (m->logits) {
+    e->d_logits = m->logits;
+  } else {
+    MKB_TRY(cudaMalloc(&e->d_logits, sizeof(float) * kVocab));
+    e->own_logits = true;
+  }
+  MKB_TRY(cudaMallocHost(&e->h_io, 8 * sizeof(int)));
+  MKB_TRY(cudaDeviceSynchronize());
+
+  mkb_decode_args& a = e->step_args;
+  mkb_decode_args_init(&a);
+  a.embed = m->embed;
+  a.lm_head = m->lm_head ? m->lm_head : m->embed;
+  a.final_norm = m->final_norm;
+  a.layers = e->d_layers;
+  a.down_t = e->d_down_t;
+  a.cos_table = m->cos_table;
+  a.sin_table = m->sin_table;
+  a.rope_fp32 = m->rope_fp32;
+  a.k_cache = m->k_cache;
+  a.v_cache = m->v_cache;
+  a.max_seq = m->max_seq;
+  a.layer_begin = 0;
+  a.layer_end = m->n_layers;
+  a.step = e->d_step;
+  a.n_tokens = 1;
+  a.flags = MKB_FLAG_LM_HEAD;
+  a.logits = e->d_logits;
+  a.out_tokens = e->d_out;
+  a.workspace = e->ws;
+  a.grid = e->grid;
+
+  if (m->use_graph) {
+    MKB_TRY(cudaStreamCreateWithFlags(&e->cap_stream, cudaStreamNonBlocking));
+    cudaGraph_t g = nullptr;
+    MKB_TRY(cudaStreamBeginCapture(e->cap_stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t le = mkb_decode(&a, e->cap_stream);
+    cudaError_t ce = cudaStreamEndCapture(e->cap_stream, &g);
+    if (le != cudaSuccess || ce != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      cudaGetLastError();
+      engine_free(e);
+      return le != cudaSuccess ? le : ce;
+    }
+    err = cudaGraphInstantiate(&e->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (err != cudaSuccess) { engine_free(e); return err; }
+  }
+#undef MKB_TRY
+  *out = e;
+  return cudaSuccess;
+}
+
+cudaError_t mkb_engine_step(mkb_engine* e, int token, int position, int* next_token, cudaStream_t stream) {
+  if (!e) return cudaErrorInvalidValue;
+  if (token < 0 || token >= kVocab || position < 0 || position >= e->max_seq) return cudaErrorInvalidValue;
+  e->h_io[0] = token;
+  e->h_io[1] = position;
+  cudaError_t err = cudaMemcpyAsync(e->d_step, e->h_io, 2 * sizeof(int), cudaMemcpyHostToDevice, stream);
+  if (err != cudaSuccess) return err;
+  err = e->graph ? cudaGraphLaunch(e->graph, stream) : mkb_decode(&e->step_args, stream);
+  if (err != cudaSuccess) return err;
+  err = cudaMemcpyAsync(e->h_io + 4, e->d_out, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  if (err != cudaSuccess) return err;
+  err = cudaMemcpyAsync(e->h_io + 5, static_cast<Workspace*>(e->ws)->error, sizeof(uint32_t),
+                        cudaMemcpyDeviceToHost, stream);
+  if (err != cudaSuccess) return err;
+  err = cudaStreamSynchronize(stream);
+  if (err != cudaSuccess) return err;
+  if (e->h_io[5] != 0) return engine_check_status(e);
+  if (next_token) *next_token = e->h_io[4];
+  return cudaSuccess;
+}
+
+cudaError_t mkb_engine_generate(mkb_engine* e, int token, int position, int n, int* out_tokens,
+                                cudaStream_t stream) {
+  if (!e || n < 1 || !out_tokens) return cudaErrorInvalidValue;
+  if (token < 0 || token >= kVocab || position < 0 || position + n > e->max_seq) return cudaErrorInvalidValue;
+  mkb_decode_args a = e->step_args;
+  a.step = nullptr;
+  a.token = token;
+  a.position = position;
+  a.cache_len = position + 1;
+  a.n_tokens = n;
+  a.out_tokens = out_tokens;
+  return mkb_decode(&a, stream);
+}
+
+float* mkb_engine_logits(mkb_engine* e) { return e ? e->d_logits : nullptr; }
+void* mkb_engine_workspace(mkb_engine* e) { return e ? e->ws : nullptr; }
+int mkb_engine_grid(mkb_engine* e) { return e ? e->grid : 0; }
+void mkb_engine_destroy(mkb_engine* e) { engine_free(e); }
+
+}  // extern "C"
