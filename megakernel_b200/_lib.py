@@ -62,6 +62,8 @@ class DecodeArgs(Structure):
         ("splits", c_int),
         ("timeout_ns", c_ulonglong),
         ("withhold_cta", c_int),
+        ("trace", c_void_p),
+        ("trace_cap", c_int),
     ]
 
 

@@ -132,6 +132,15 @@ struct DecodeParams {
   unsigned long long timeout_ns;     // bound on every wait
   int withhold_cta;                  // test hook: this CTA never publishes its first
                                      // QKV arrival (-1 = off); the others time out
+  unsigned long long* trace;         // optional [grid][trace_cap] stage time stamps
+  int trace_cap;
+};
+
+// Trace record: (code << 48) | (globaltimer ns & 0xffffffffffff), written by
+// consumer thread 0 of every CTA. code = kind | stage << 2 | layer << 5 | token << 10.
+enum TraceKind : uint32_t { kTrWaitBegin = 0, kTrWaitEnd = 1, kTrPublish = 2, kTrMark = 3 };
+enum TraceStage : uint32_t {
+  kStA = 0, kStBC = 1, kStDE = 2, kStE = 3, kStLM = 4, kStSplit = 5, kStToken = 6, kStEnd = 7
 };
 
 // ---------------------------------------------------------------------------

@@ -69,6 +69,22 @@ struct Ctl {
   Workspace* ws;
   uint64_t timeout;
   int cta;
+  unsigned long long* trace;  // this CTA's row of the trace buffer (or null)
+  int trace_cap;
+};
+
+// Stage time stamp (consumer thread 0 only; no-op without a trace buffer).
+struct Tracer {
+  unsigned long long* row;
+  int cap;
+  int n;
+  __device__ __forceinline__ void mark(uint32_t kind, uint32_t stage, int layer, int tok) {
+    if (row != nullptr && threadIdx.x == 0 && n < cap) {
+      const uint64_t code = kind | (stage << 2) | ((static_cast<uint32_t>(layer) & 31u) << 5) |
+                            ((static_cast<uint32_t>(tok) & 63u) << 10);
+      row[n++] = (code << 48) | (global_ns() & 0xffffffffffffull);
+    }
+  }
 };
 
 __device__ __forceinline__ bool aborted(const Ctl& c) {
@@ -108,16 +124,19 @@ __device__ void spin_geq(const Ctl& c, const uint32_t* ctr, uint32_t target, uin
 }
 
 // Consumer-side transition: thread 0 waits, then all consumers proceed.
-__device__ __forceinline__ void transition_wait(const Ctl& c, const uint32_t* ctr, uint32_t target, int layer,
-                                                int stage, int tok) {
+__device__ __forceinline__ void transition_wait(const Ctl& c, Tracer& tr, const uint32_t* ctr, uint32_t target,
+                                                int layer, int stage, int tok) {
+  tr.mark(kTrWaitBegin, stage, layer, tok);
   if (threadIdx.x == 0) spin_geq(c, ctr, target, kErrTimeoutTransition, layer, stage, tok);
   consumer_sync(kConsumerThreads);
+  tr.mark(kTrWaitEnd, stage, layer, tok);
 }
 
 // Consumer-side publish: every consumer's writes are ordered before the add.
-__device__ __forceinline__ void transition_publish(uint32_t* ctr) {
+__device__ __forceinline__ void transition_publish(Tracer& tr, uint32_t* ctr, int layer, int stage, int tok) {
   consumer_sync(kConsumerThreads);
   if (threadIdx.x == 0) release_add(ctr, 1u);
+  tr.mark(kTrPublish, stage, layer, tok);
 }
 
 // ---- ring (consumer side) ----------------------------------------------------
@@ -420,6 +439,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   const int zero_cta = G - 1;
   uint32_t n = 0;
   float xr[32];
+  Tracer tr{c.trace, c.trace_cap, 0};
 
   int token = token0;
   for (int t = 0; t < p.n_tokens; ++t) {
@@ -427,6 +447,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     const int cl = cl0 + t;
     const uint32_t tgtG = static_cast<uint32_t>(G * (t + 1));
     const uint32_t tgtBC = static_cast<uint32_t>(nbc * (t + 1));
+    tr.mark(kTrMark, kStToken, 0, t);
 
     // ---- token input: embedding gather (megakernel.cu:783-795) ----
     if (t > 0) {
@@ -446,7 +467,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       const LayerWeights* lw = p.layers + l;
       // ================= A: RMSNorm + QKV (megakernel.cu:704-739, 633-701) ======
       if (l > lb) {
-        transition_wait(c, &ws->sync[l - 1][fused ? 2 : 3][0], tgtG, l, 0, t);
+        transition_wait(c, tr, &ws->sync[l - 1][fused ? 2 : 3][0], tgtG, l, kStA, t);
         for (int i = tid; i < kHidden; i += kConsumerThreads)
           sm.r[i] = fused ? sm.rmid[i] + __ldcg(&ws->acc_down[l - 1][i]) : __ldcg(&ws->resid[i]);
         consumer_sync(kConsumerThreads);
@@ -468,12 +489,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         ring_done(c, n);
         r = e;
       }
-      if (!(t == 0 && l == lb && c.cta == p.withhold_cta)) transition_publish(&ws->sync[l][0][0]);
+      if (!(t == 0 && l == lb && c.cta == p.withhold_cta)) transition_publish(tr, &ws->sync[l][0][0], l, kStA, t);
       else consumer_sync(kConsumerThreads);
 
       // ================= BC: head norm + RoPE + KV append, attention, o_proj =====
       if (pl.in_bc) {
-        transition_wait(c, &ws->sync[l][0][0], tgtG, l, 1, t);
+        transition_wait(c, tr, &ws->sync[l][0][0], tgtG, l, kStBC, t);
         const int h = pl.h;
         // q_norm / k_norm + rotate-half RoPE (megakernel.cu:490-630)
         if (warp < 3) {
@@ -673,7 +694,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           if (splits > 1 && tid == 0) release_add(&ws->att_sync[l][h][0], 1u);
         }
         if (splits > 1) {
-          transition_wait(c, &ws->att_sync[l][h][0], static_cast<uint32_t>(splits * (t + 1)), l, 2, t);
+          transition_wait(c, tr, &ws->att_sync[l][h][0], static_cast<uint32_t>(splits * (t + 1)), l, kStSplit, t);
           if (tid < 2 * kHeadDim) {
             const int hh = tid >> 7, d = tid & (kHeadDim - 1);
             float M = -INFINITY;
@@ -717,12 +738,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             ring_done(c, n);
           }
         }
-        transition_publish(&ws->sync[l][1][0]);
+        transition_publish(tr, &ws->sync[l][1][0], l, kStBC, t);
       }
       // Zero the previous layer's accumulators: every CTA has read them (it
       // passed T_A of this layer), and their next use is the next token.
       if (c.cta == zero_cta && l > lb) {
-        if (!pl.in_bc) transition_wait(c, &ws->sync[l][0][0], tgtG, l, 1, t);
+        if (!pl.in_bc) transition_wait(c, tr, &ws->sync[l][0][0], tgtG, l, kStBC, t);
         for (int i = tid; i < kHidden; i += kConsumerThreads) {
           ws->acc_mid[l - 1][i] = 0.f;
           ws->acc_down[l - 1][i] = 0.f;
@@ -730,7 +751,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       }
 
       // ================= DE: post norm, SwiGLU rows, down partial ===============
-      transition_wait(c, &ws->sync[l][1][0], tgtBC, l, 4, t);
+      transition_wait(c, tr, &ws->sync[l][1][0], tgtBC, l, kStDE, t);
       for (int i = tid; i < kHidden; i += kConsumerThreads) sm.rmid[i] = sm.r[i] + __ldcg(&ws->acc_mid[l][i]);
       consumer_sync(kConsumerThreads);
       norm_to_regs(sm.rmid, ldg_ptr(&lw->post_attn_norm_weight), false, xr, sm.red);
@@ -769,12 +790,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           ring_done(c, n);
         }
         red_add_v2_f32(&ws->acc_down[l][col], pa, pb);
-        transition_publish(&ws->sync[l][2][0]);
+        transition_publish(tr, &ws->sync[l][2][0], l, kStDE, t);
       } else {
         // reference layout: publish the SwiGLU vector, then whole down rows
         for (int j = tid; j < pl.jb - pl.ja; j += kConsumerThreads) p.mlp_out[pl.ja + j] = sm.m[j];
-        transition_publish(&ws->sync[l][2][0]);
-        transition_wait(c, &ws->sync[l][2][0], tgtG, l, 6, t);
+        transition_publish(tr, &ws->sync[l][2][0], l, kStDE, t);
+        transition_wait(c, tr, &ws->sync[l][2][0], tgtG, l, kStE, t);
         for (int i = tid; i < kInter; i += kConsumerThreads) sm.u.x[i] = __ldcg(p.mlp_out + i);
         consumer_sync(kConsumerThreads);
         for (int d0 = pl.da; d0 < pl.db; d0 += kDownRowsPerChunk) {
@@ -800,13 +821,13 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           }
           consumer_sync(kConsumerThreads);
         }
-        transition_publish(&ws->sync[l][3][0]);
+        transition_publish(tr, &ws->sync[l][3][0], l, kStE, t);
       }
     }
 
     // ================= final residual, LM head + argmax (megakernel.cu:870-886) ==
     if (le > lb) {
-      transition_wait(c, &ws->sync[le - 1][fused ? 2 : 3][0], tgtG, le - 1, 7, t);
+      transition_wait(c, tr, &ws->sync[le - 1][fused ? 2 : 3][0], tgtG, le - 1, kStLM, t);
       for (int i = tid; i < kHidden; i += kConsumerThreads)
         sm.r[i] = fused ? sm.rmid[i] + __ldcg(&ws->acc_down[le - 1][i]) : __ldcg(&ws->resid[i]);
       consumer_sync(kConsumerThreads);
@@ -848,6 +869,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     }
 
     // ---- end of token: the last CTA to arrive reduces the argmax and resets ---
+    tr.mark(kTrMark, kStLM, 0, t);
     consumer_sync(kConsumerThreads);
     if (tid == 0) {
       // One thread decides for the whole CTA, so every consumer takes the same path.
@@ -862,6 +884,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     consumer_sync(kConsumerThreads);
     const int last_state = sm.is_last;
     consumer_sync(kConsumerThreads);
+    tr.mark(kTrMark, kStEnd, 0, t);
     if (last_state < 0) return;
     if (last_state) {
       int best = -1;
@@ -932,7 +955,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem* sm = reinterpret_cast<Smem*>(smem_raw);
-  Ctl c{sm, p.ws, p.timeout_ns, static_cast<int>(blockIdx.x)};
+  Ctl c{sm, p.ws, p.timeout_ns, static_cast<int>(blockIdx.x),
+        p.trace ? p.trace + (size_t)blockIdx.x * p.trace_cap : nullptr, p.trace_cap};
 
   int token = p.token, pos = p.position, cl = p.cache_len;
   if (p.step != nullptr) {

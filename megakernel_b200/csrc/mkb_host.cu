@@ -121,6 +121,8 @@ cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p) {
   if (p->splits > kMaxSplits || p->splits > p->group_size) return cudaErrorInvalidValue;
   p->timeout_ns = a->timeout_ns ? a->timeout_ns : kDefaultTimeoutNs;
   p->withhold_cta = a->withhold_cta;
+  p->trace = a->trace;
+  p->trace_cap = a->trace ? a->trace_cap : 0;
   // Host-side validation of what the host can see (the kernel re-checks the rest).
   if (!p->embed || !p->layers || !p->k_cache || !p->v_cache || !p->cos_table || !p->sin_table)
     return cudaErrorInvalidValue;

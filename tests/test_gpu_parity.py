@@ -330,7 +330,9 @@ def test_withheld_arrival_times_out_with_status(w_gpu):
     _lib.check(decode_call(withhold_cta=3, timeout_ns=20_000_000, **common), "mkb_decode")
     torch.cuda.synchronize()
     st = _lib.workspace_status(ws.data_ptr())
-    assert st[0] == 1, st            # a grid transition wait expired
+    # the first bound to expire is either a consumer's grid-transition wait (1)
+    # or a producer stuck on a full ring behind those consumers (2)
+    assert st[0] in (1, 2), st
     # the context is still usable: reset the workspace and decode normally
     _lib.check(_lib.load().mkb_workspace_reset(ws.data_ptr(), None), "reset")
     _lib.check(decode_call(withhold_cta=-1, **common), "mkb_decode")
