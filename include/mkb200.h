@@ -85,10 +85,10 @@ typedef struct mkb_decode_args {
                                   first QKV arrival, so the others' waits expire */
   unsigned long long* trace;   /* device [grid][trace_cap] stage time stamps or NULL:
                                   (code << 48) | globaltimer_ns, code = kind | stage<<2 |
-                                  layer<<5 | token<<10 (kind 0 wait begin, 1 wait end,
+                                  layer<<6 | token<<11 (kind 0 wait begin, 1 wait end,
                                   2 publish, 3 mark; stage 0 QKV, 1 attention+o_proj,
                                   2 SwiGLU(+down), 3 down, 4 LM head, 5 split combine,
-                                  6 token start, 7 token end) */
+                                  6 token start, 7 token end, 8-15 sub-stage marks) */
   int trace_cap;
 } mkb_decode_args;
 

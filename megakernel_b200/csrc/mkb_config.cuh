@@ -137,10 +137,13 @@ struct DecodeParams {
 };
 
 // Trace record: (code << 48) | (globaltimer ns & 0xffffffffffff), written by
-// consumer thread 0 of every CTA. code = kind | stage << 2 | layer << 5 | token << 10.
+// consumer thread 0 of every CTA. code = kind | stage << 2 | layer << 6 | token << 11.
 enum TraceKind : uint32_t { kTrWaitBegin = 0, kTrWaitEnd = 1, kTrPublish = 2, kTrMark = 3 };
 enum TraceStage : uint32_t {
-  kStA = 0, kStBC = 1, kStDE = 2, kStE = 3, kStLM = 4, kStSplit = 5, kStToken = 6, kStEnd = 7
+  kStA = 0, kStBC = 1, kStDE = 2, kStE = 3, kStLM = 4, kStSplit = 5, kStToken = 6, kStEnd = 7,
+  // sub-stage marks (kind kTrMark)
+  kSubAInput = 8, kSubANorm = 9, kSubBCPrep = 10, kSubBCAttn = 11, kSubBCComb = 12,
+  kSubDENorm = 13, kSubDEGU = 14, kSubDEDown = 15
 };
 
 // ---------------------------------------------------------------------------

@@ -80,8 +80,8 @@ struct Tracer {
   int n;
   __device__ __forceinline__ void mark(uint32_t kind, uint32_t stage, int layer, int tok) {
     if (row != nullptr && threadIdx.x == 0 && n < cap) {
-      const uint64_t code = kind | (stage << 2) | ((static_cast<uint32_t>(layer) & 31u) << 5) |
-                            ((static_cast<uint32_t>(tok) & 63u) << 10);
+      const uint64_t code = kind | ((stage & 15u) << 2) | ((static_cast<uint32_t>(layer) & 31u) << 6) |
+                            ((static_cast<uint32_t>(tok) & 31u) << 11);
       row[n++] = (code << 48) | (global_ns() & 0xffffffffffffull);
     }
   }
@@ -165,7 +165,17 @@ __device__ __forceinline__ void ring_done(const Ctl& c, uint32_t& n) {
 // RMSNorm of a 1024-vector held in shared memory; each lane receives the 32
 // normalised elements lane*8 + g*256 + e (g < 4, e < 8) it needs for its part of
 // every 2 KB weight row. Same formula as megakernel.cu:704-739.
-__device__ void norm_to_regs(const float* v, const __nv_bfloat16* w, bool skip, float xr[32], float* s_red) {
+// The 4 x 16 B of a 1024-element BF16 norm weight this lane needs (loaded ahead
+// of the grid transition that gates the norm, so the load latency overlaps it).
+__device__ __forceinline__ void load_norm_w(const __nv_bfloat16* w, uint4 wv[4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+    wv[g] = w ? __ldg(reinterpret_cast<const uint4*>(w + lane * 8 + g * 256))
+              : make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);  // bf16 1.0 pairs
+}
+
+__device__ void norm_to_regs(const float* v, const uint4 wvs[4], bool skip, float xr[32], float* s_red) {
   const int tid = threadIdx.x;
   const float a = v[tid], b = v[tid + kConsumerThreads];
   const float ss = warp_sum(a * a + b * b);
@@ -181,12 +191,7 @@ __device__ void norm_to_regs(const float* v, const __nv_bfloat16* w, bool skip, 
     const int idx = lane * 8 + g * 256;
     const float4 v0 = *reinterpret_cast<const float4*>(v + idx);
     const float4 v1 = *reinterpret_cast<const float4*>(v + idx + 4);
-    uint4 wv;
-    if (skip) {
-      wv = make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);  // bf16 1.0 pairs
-    } else {
-      wv = __ldg(reinterpret_cast<const uint4*>(w + idx));
-    }
+    const uint4 wv = wvs[g];
     xr[g * 8 + 0] = v0.x * rstd * bf_lo(wv.x);
     xr[g * 8 + 1] = v0.y * rstd * bf_hi(wv.x);
     xr[g * 8 + 2] = v0.z * rstd * bf_lo(wv.y);
@@ -289,6 +294,12 @@ struct Producer {
     bulk_g2s(c.sm->ring[s] + off, src, bytes, &c.sm->full[s], pol);
   }
 
+  // L2 prefetch (16-byte aligned operands only; others are simply skipped).
+  __device__ void prefetch(const void* src, uint32_t bytes) {
+    if (bytes == 0 || ((reinterpret_cast<uintptr_t>(src) | bytes) & 15u) != 0u) return;
+    bulk_prefetch_l2(src, bytes, pol_kv);
+  }
+
   // Wait for every copy still in flight before the CTA exits.
   __device__ void drain() {
     if (lane != 0) return;
@@ -304,6 +315,51 @@ struct Producer {
   }
 };
 
+// Pull this CTA's bytes of layer `l` (cache length `cl`) into L2 ahead of the
+// ring, so HBM keeps streaming while the consumers wait at grid transitions and
+// the ring refills from L2.
+__device__ void prefetch_layer(Producer& pr, const DecodeParams& p, const Plan& pl, int l, int cl, int splits) {
+  const LayerWeights* lw = p.layers + l;
+  if (pr.lane == 0) {
+    for (int r = pl.qa; r < pl.qb;) {
+      int e = r < kQSize ? kQSize : (r < kQSize + kKVSize ? kQSize + kKVSize : kQKVRows);
+      if (e > pl.qb) e = pl.qb;
+      const __nv_bfloat16* src = r < kQSize ? ldg_ptr(&lw->q_weight) + (size_t)r * kHidden
+                                 : r < kQSize + kKVSize
+                                     ? ldg_ptr(&lw->k_weight) + (size_t)(r - kQSize) * kHidden
+                                     : ldg_ptr(&lw->v_weight) + (size_t)(r - kQSize - kKVSize) * kHidden;
+      pr.prefetch(src, static_cast<uint32_t>(e - r) * kHidden * 2u);
+      r = e;
+    }
+    if (pl.in_bc) {
+      int ka, kb;
+      key_range(cl, splits, pl.c, &ka, &kb);
+      const size_t head_off = ((size_t)l * kNKV + pl.h) * (size_t)p.max_seq * kHeadDim;
+      pr.prefetch(p.k_cache + head_off + (size_t)ka * kHeadDim, static_cast<uint32_t>(kb - ka) * kHeadDim * 2u);
+      pr.prefetch(p.v_cache + head_off + (size_t)ka * kHeadDim, static_cast<uint32_t>(kb - ka) * kHeadDim * 2u);
+    }
+    const uint32_t gu = static_cast<uint32_t>(pl.jb - pl.ja) * kHidden * 2u;
+    pr.prefetch(ldg_ptr(&lw->gate_proj_weight) + (size_t)pl.ja * kHidden, gu);
+    pr.prefetch(ldg_ptr(&lw->up_proj_weight) + (size_t)pl.ja * kHidden, gu);
+    if (p.down_t != nullptr) {
+      pr.prefetch(ldg_ptr(p.down_t + l) + (size_t)pl.ja * kHidden, gu);
+    } else {
+      pr.prefetch(ldg_ptr(&lw->down_proj_weight) + (size_t)pl.da * kInter,
+                  static_cast<uint32_t>(pl.db - pl.da) * kInter * 2u);
+    }
+  }
+  if (pl.in_bc) {
+    const __nv_bfloat16* wo = ldg_ptr(&lw->o_proj_weight);
+    for (int row = pl.oa + pr.lane; row < pl.ob; row += 32)
+      pr.prefetch(wo + (size_t)row * kQSize + pl.h * 2 * kHeadDim, 512u);
+  }
+  __syncwarp();
+}
+
+// Percentage of each CTA's LM-head rows pulled into L2 during the last layers.
+constexpr int kLmPreloadPct = 15;
+constexpr int kLmPreloadLayers = 4;
+
 __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int pos0, int cl0,
                              int splits) {
   Producer pr(c);
@@ -314,6 +370,17 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     const int cl = cl0 + t;
     for (int l = p.layer_begin; l < p.layer_end && !pr.stop; ++l) {
       const LayerWeights* lw = p.layers + l;
+      // L2 prefetch one layer ahead (the next token's first layer after the last)
+      if (l == p.layer_begin && t == 0) prefetch_layer(pr, p, pl, l, cl, splits);
+      if (l + 1 < p.layer_end) prefetch_layer(pr, p, pl, l + 1, cl, splits);
+      else if (t + 1 < p.n_tokens) prefetch_layer(pr, p, pl, p.layer_begin, cl + 1, splits);
+      if ((p.flags & kFlagLmHead) && l >= p.layer_end - kLmPreloadLayers && pr.lane == 0) {
+        const int npre = (pl.vb - pl.va) * kLmPreloadPct / 100;
+        const int part_i = l - (p.layer_end - kLmPreloadLayers);
+        const int r0 = pl.va + part(npre, kLmPreloadLayers, part_i);
+        const int r1 = pl.va + part(npre, kLmPreloadLayers, part_i + 1);
+        pr.prefetch(p.lm_head + (size_t)r0 * kHidden, static_cast<uint32_t>(r1 - r0) * kHidden * 2u);
+      }
       // A: QKV rows
       for (int r = pl.qa; r < pl.qb;) {
         const int e = qkv_chunk_end(r, pl.qb);
@@ -465,14 +532,18 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 
     for (int l = lb; l < le; ++l) {
       const LayerWeights* lw = p.layers + l;
+      uint4 nwv[4];
       // ================= A: RMSNorm + QKV (megakernel.cu:704-739, 633-701) ======
+      load_norm_w(ldg_ptr(&lw->norm_weight), nwv);
       if (l > lb) {
         transition_wait(c, tr, &ws->sync[l - 1][fused ? 2 : 3][0], tgtG, l, kStA, t);
         for (int i = tid; i < kHidden; i += kConsumerThreads)
           sm.r[i] = fused ? sm.rmid[i] + __ldcg(&ws->acc_down[l - 1][i]) : __ldcg(&ws->resid[i]);
         consumer_sync(kConsumerThreads);
       }
-      norm_to_regs(sm.r, ldg_ptr(&lw->norm_weight), false, xr, sm.red);
+      tr.mark(kTrMark, kSubAInput, l, t);
+      norm_to_regs(sm.r, nwv, false, xr, sm.red);
+      tr.mark(kTrMark, kSubANorm, l, t);
       for (int r = pl.qa; r < pl.qb;) {
         const int e = qkv_chunk_end(r, pl.qb);
         const uint32_t sa = ring_wait(c, n, l, 0, t);
@@ -494,8 +565,23 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 
       // ================= BC: head norm + RoPE + KV append, attention, o_proj =====
       if (pl.in_bc) {
-        transition_wait(c, tr, &ws->sync[l][0][0], tgtG, l, kStBC, t);
         const int h = pl.h;
+        // per-head norm weights and this position's RoPE row do not depend on
+        // the transition: load them while it is pending
+        float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f, cs0 = 0.f, sn0 = 0.f, cs1 = 0.f, sn1 = 0.f;
+        if (warp < 3) {
+          const __nv_bfloat16* nw = warp < 2 ? ldg_ptr(&lw->q_norm_weight) : ldg_ptr(&lw->k_norm_weight);
+          w0 = __bfloat162float(nw[lane]);
+          w1 = __bfloat162float(nw[lane + 32]);
+          w2 = __bfloat162float(nw[lane + 64]);
+          w3 = __bfloat162float(nw[lane + 96]);
+          const size_t rb = (size_t)pos * kHeadDim;
+          cs0 = rope_at(p.cos_table, p.rope_fp32, rb + lane);
+          sn0 = rope_at(p.sin_table, p.rope_fp32, rb + lane);
+          cs1 = rope_at(p.cos_table, p.rope_fp32, rb + lane + 32);
+          sn1 = rope_at(p.sin_table, p.rope_fp32, rb + lane + 32);
+        }
+        transition_wait(c, tr, &ws->sync[l][0][0], tgtG, l, kStBC, t);
         // q_norm / k_norm + rotate-half RoPE (megakernel.cu:490-630)
         if (warp < 3) {
           const float* src = warp < 2 ? p.q_out + (2 * h + warp) * kHeadDim : p.k_out + h * kHeadDim;
@@ -503,18 +589,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           const float x2 = __ldcg(src + lane + 64), x3 = __ldcg(src + lane + 96);
           const float ss = warp_sum(x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3);
           const float rstd = rsqrtf(ss * (1.0f / kHeadDim) + kEps);
-          const __nv_bfloat16* nw = warp < 2 ? ldg_ptr(&lw->q_norm_weight) : ldg_ptr(&lw->k_norm_weight);
-          const float y0 = x0 * rstd * __bfloat162float(nw[lane]);
-          const float y1 = x1 * rstd * __bfloat162float(nw[lane + 32]);
-          const float y2 = x2 * rstd * __bfloat162float(nw[lane + 64]);
-          const float y3 = x3 * rstd * __bfloat162float(nw[lane + 96]);
-          const size_t rb = (size_t)pos * kHeadDim;
-          const float c0 = rope_at(p.cos_table, p.rope_fp32, rb + lane);
-          const float s0 = rope_at(p.sin_table, p.rope_fp32, rb + lane);
-          const float c1 = rope_at(p.cos_table, p.rope_fp32, rb + lane + 32);
-          const float s1 = rope_at(p.sin_table, p.rope_fp32, rb + lane + 32);
-          const float o0 = y0 * c0 - y2 * s0, o2 = y2 * c0 + y0 * s0;
-          const float o1 = y1 * c1 - y3 * s1, o3 = y3 * c1 + y1 * s1;
+          const float y0 = x0 * rstd * w0;
+          const float y1 = x1 * rstd * w1;
+          const float y2 = x2 * rstd * w2;
+          const float y3 = x3 * rstd * w3;
+          const float o0 = y0 * cs0 - y2 * sn0, o2 = y2 * cs0 + y0 * sn0;
+          const float o1 = y1 * cs1 - y3 * sn1, o3 = y3 * cs1 + y1 * sn1;
           if (warp < 2) {
             const float sc = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
             sm.q[warp][lane] = o0 * sc;
@@ -546,6 +626,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           }
         }
         consumer_sync(kConsumerThreads);
+        tr.mark(kTrMark, kSubBCPrep, l, t);
 
         // GQA decode attention over keys [ka, kb) (megakernel.cu:228-370),
         // per-warp online softmax in the exp2 domain, then a 16-warp combine.
@@ -654,6 +735,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             }
             ring_done(c, n);
           }
+          tr.mark(kTrMark, kSubBCAttn, l, t);
 #pragma unroll
           for (int d = 0; d < 4; ++d) {
             sm.u.att[warp][0][lane * 4 + d] = a0[d];
@@ -712,6 +794,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         }
 
         // o_proj partial of this KV head's two Q heads (megakernel.cu:191-225)
+        tr.mark(kTrMark, kSubBCComb, l, t);
         {
           float xo[8];
 #pragma unroll
@@ -751,10 +834,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       }
 
       // ================= DE: post norm, SwiGLU rows, down partial ===============
+      load_norm_w(ldg_ptr(&lw->post_attn_norm_weight), nwv);
       transition_wait(c, tr, &ws->sync[l][1][0], tgtBC, l, kStDE, t);
       for (int i = tid; i < kHidden; i += kConsumerThreads) sm.rmid[i] = sm.r[i] + __ldcg(&ws->acc_mid[l][i]);
       consumer_sync(kConsumerThreads);
-      norm_to_regs(sm.rmid, ldg_ptr(&lw->post_attn_norm_weight), false, xr, sm.red);
+      norm_to_regs(sm.rmid, nwv, false, xr, sm.red);
+      tr.mark(kTrMark, kSubDENorm, l, t);
       // gate/up rows (megakernel.cu:100-142)
       for (int j0 = pl.ja; j0 < pl.jb; j0 += kGUPerChunk) {
         const int j1 = min(pl.jb, j0 + kGUPerChunk);
@@ -768,6 +853,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         ring_done(c, n);
       }
       consumer_sync(kConsumerThreads);
+      tr.mark(kTrMark, kSubDEGU, l, t);
       if (tid < pl.jb - pl.ja) {
         const float g = sm.gu[0][tid], u = sm.gu[1][tid];
         sm.m[tid] = g / (1.0f + expf(-g)) * u;  // silu (config.cuh:177-179) * up
@@ -789,6 +875,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           }
           ring_done(c, n);
         }
+        tr.mark(kTrMark, kSubDEDown, l, t);
         red_add_v2_f32(&ws->acc_down[l][col], pa, pb);
         transition_publish(tr, &ws->sync[l][2][0], l, kStDE, t);
       } else {
@@ -826,6 +913,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     }
 
     // ================= final residual, LM head + argmax (megakernel.cu:870-886) ==
+    uint4 fwv[4];
+    load_norm_w((p.flags & kFlagSkipFinalNorm) ? nullptr : p.final_norm, fwv);
     if (le > lb) {
       transition_wait(c, tr, &ws->sync[le - 1][fused ? 2 : 3][0], tgtG, le - 1, kStLM, t);
       for (int i = tid; i < kHidden; i += kConsumerThreads)
@@ -837,7 +926,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     float bv = -INFINITY;
     int bi = INT_MAX;
     if (p.flags & kFlagLmHead) {
-      norm_to_regs(sm.r, p.final_norm, (p.flags & kFlagSkipFinalNorm) != 0, xr, sm.red);
+      norm_to_regs(sm.r, fwv, (p.flags & kFlagSkipFinalNorm) != 0, xr, sm.red);
       for (int v0 = pl.va; v0 < pl.vb; v0 += kRowsPerChunk1024) {
         const int v1 = min(pl.vb, v0 + kRowsPerChunk1024);
         const uint32_t sa = ring_wait(c, n, -1, 8, t);

@@ -60,6 +60,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
 }
+// Bulk prefetch of global memory into L2 (no shared-memory destination).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(policy)
+               : "memory");
+}
 // Orders this thread's earlier generic-proxy global accesses before its later
 // async-proxy (bulk copy) accesses.
 __device__ __forceinline__ void fence_proxy_async_global() {

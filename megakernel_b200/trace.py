@@ -22,7 +22,10 @@ from .engine import build_layer_table, decode_call
 from .rope import rope_tables
 
 STAGE_NAMES = {0: "qkv", 1: "attn+o_proj", 2: "swiglu(+down)", 3: "down", 4: "lm_head",
-               5: "split-combine", 6: "token", 7: "end"}
+               5: "split-combine", 6: "token", 7: "end", 8: "qkv:input", 9: "qkv:norm",
+               10: "attn:head-prep", 11: "attn:softmax-v", 12: "attn:combine", 13: "swiglu:input+norm",
+               14: "swiglu:gate-up", 15: "swiglu:down"}
+KIND_NAMES = {0: "pre-wait", 1: "wait", 2: "publish", 3: "mark"}
 
 
 class TracedDecoder:
@@ -81,7 +84,7 @@ def decode_records(trace: torch.Tensor):
             u = v & ((1 << 64) - 1)
             code = u >> 48
             t = u & ((1 << 48) - 1)
-            recs.append((code & 3, (code >> 2) & 7, (code >> 5) & 31, (code >> 10) & 63, t))
+            recs.append((code & 3, (code >> 2) & 15, (code >> 6) & 31, (code >> 11) & 31, t))
         out.append(recs)
     return out
 
@@ -121,6 +124,12 @@ def summarize(per_cta) -> dict:
                 elif st == 7 and tok_start is not None:
                     token_ns.append(t - tok_start)
         layer_period += [b - a for a, b in zip(a_pub, a_pub[1:])]
+    # time between consecutive stamps of a CTA, labelled by the later stamp
+    seg = defaultdict(list)
+    for recs in per_cta:
+        for prev, cur in zip(recs, recs[1:]):
+            label = (f"{KIND_NAMES[cur[0]]}:{STAGE_NAMES[cur[1]]}" if cur[0] != 3 else STAGE_NAMES[cur[1]])
+            seg[label].append(cur[4] - prev[4])
     med = lambda xs: statistics.median(xs) / 1000.0 if xs else None  # noqa: E731
     mean = lambda xs: statistics.fmean(xs) / 1000.0 if xs else None  # noqa: E731
     span = max(r[-1][4] for r in per_cta if r) - t0
@@ -129,6 +138,8 @@ def summarize(per_cta) -> dict:
         "token_us_max": max(token_ns) / 1000.0 if token_ns else None,
         "layer_period_us_median": med(layer_period),
         "lm_head_us_median": med(lm_ns),
+        "segments": {k: {"mean_us": statistics.fmean(v) / 1000.0, "median_us": statistics.median(v) / 1000.0,
+                         "count": len(v)} for k, v in seg.items()},
         "stages": {STAGE_NAMES[s]: {"wait_us_mean": mean(waits[s]), "wait_us_median": med(waits[s]),
                                     "compute_us_mean": mean(compute[s]), "compute_us_median": med(compute[s])}
                    for s in sorted(set(waits) | set(compute))},
@@ -144,6 +155,9 @@ def format_summary(s: dict) -> str:
         f = lambda v: f"{v:10.3f}" if v is not None else f"{'-':>10s}"  # noqa: E731
         lines.append(f"{name:16s} {f(d['wait_us_mean'])} {f(d['wait_us_median'])} "
                      f"{f(d['compute_us_mean']):>13s} {f(d['compute_us_median']):>12s}")
+    lines.append("segments (time since the CTA's previous stamp, labelled by the later stamp):")
+    for k, d in sorted(s.get("segments", {}).items(), key=lambda kv: -kv[1]["mean_us"] * kv[1]["count"]):
+        lines.append(f"  {k:28s} mean {d['mean_us']:8.3f} us  median {d['median_us']:8.3f} us  n={d['count']}")
     return "\n".join(lines)
 
 
