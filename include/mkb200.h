@@ -83,12 +83,15 @@ typedef struct mkb_decode_args {
   unsigned long long timeout_ns; /* bound on every in-kernel wait; 0 = 1 s */
   int withhold_cta;            /* test hook (-1 = off): that CTA never publishes its
                                   first QKV arrival, so the others' waits expire */
-  unsigned long long* trace;   /* device [grid][trace_cap] stage time stamps or NULL:
+  unsigned long long* trace;   /* device [2*grid][trace_cap] time stamps or NULL; row c:
+                                  consumers of CTA c, row grid+c: its producer. Record =
                                   (code << 48) | globaltimer_ns, code = kind | stage<<2 |
-                                  layer<<6 | token<<11 (kind 0 wait begin, 1 wait end,
+                                  layer<<7 | token<<12 (kind 0 wait begin, 1 wait end,
                                   2 publish, 3 mark; stage 0 QKV, 1 attention+o_proj,
                                   2 SwiGLU(+down), 3 down, 4 LM head, 5 split combine,
-                                  6 token start, 7 token end, 8-15 sub-stage marks) */
+                                  6 token start, 7 token end, 8-15 sub-stage marks,
+                                  16 ring slot fill wait, 17 producer slot wait,
+                                  18 chunk issue) */
   int trace_cap;
 } mkb_decode_args;
 

@@ -132,18 +132,22 @@ struct DecodeParams {
   unsigned long long timeout_ns;     // bound on every wait
   int withhold_cta;                  // test hook: this CTA never publishes its first
                                      // QKV arrival (-1 = off); the others time out
-  unsigned long long* trace;         // optional [grid][trace_cap] stage time stamps
+  unsigned long long* trace;         // optional [2*grid][trace_cap] stage time stamps
   int trace_cap;
 };
 
-// Trace record: (code << 48) | (globaltimer ns & 0xffffffffffff), written by
-// consumer thread 0 of every CTA. code = kind | stage << 2 | layer << 6 | token << 11.
+// Trace record: (code << 48) | (globaltimer ns & 0xffffffffffff). Row cta is
+// written by consumer thread 0 of that CTA, row grid + cta by its producer lane.
+// code = kind | stage << 2 | layer << 7 | token << 12.
 enum TraceKind : uint32_t { kTrWaitBegin = 0, kTrWaitEnd = 1, kTrPublish = 2, kTrMark = 3 };
 enum TraceStage : uint32_t {
   kStA = 0, kStBC = 1, kStDE = 2, kStE = 3, kStLM = 4, kStSplit = 5, kStToken = 6, kStEnd = 7,
   // sub-stage marks (kind kTrMark)
   kSubAInput = 8, kSubANorm = 9, kSubBCPrep = 10, kSubBCAttn = 11, kSubBCComb = 12,
-  kSubDENorm = 13, kSubDEGU = 14, kSubDEDown = 15
+  kSubDENorm = 13, kSubDEGU = 14, kSubDEDown = 15,
+  kStRing = 16,   // consumer waited for a ring slot to fill
+  kStSlot = 17,   // producer waited for a ring slot to empty (layer field = chunk index & 31)
+  kStIssue = 18   // producer issued a chunk
 };
 
 // ---------------------------------------------------------------------------

@@ -78,10 +78,11 @@ struct Tracer {
   unsigned long long* row;
   int cap;
   int n;
+  int who;  // the one thread that records
   __device__ __forceinline__ void mark(uint32_t kind, uint32_t stage, int layer, int tok) {
-    if (row != nullptr && threadIdx.x == 0 && n < cap) {
-      const uint64_t code = kind | ((stage & 15u) << 2) | ((static_cast<uint32_t>(layer) & 31u) << 6) |
-                            ((static_cast<uint32_t>(tok) & 31u) << 11);
+    if (row != nullptr && static_cast<int>(threadIdx.x) == who && n < cap) {
+      const uint64_t code = kind | ((stage & 31u) << 2) | ((static_cast<uint32_t>(layer) & 31u) << 7) |
+                            ((static_cast<uint32_t>(tok) & 15u) << 12);
       row[n++] = (code << 48) | (global_ns() & 0xffffffffffffull);
     }
   }
@@ -140,10 +141,12 @@ __device__ __forceinline__ void transition_publish(Tracer& tr, uint32_t* ctr, in
 }
 
 // ---- ring (consumer side) ----------------------------------------------------
-__device__ __forceinline__ uint32_t ring_wait(const Ctl& c, uint32_t n, int layer, int stage, int tok) {
+__device__ __forceinline__ uint32_t ring_wait(const Ctl& c, uint32_t n, int layer, int stage, int tok,
+                                              Tracer* tr = nullptr) {
   const int s = static_cast<int>(n % kSlots);
   const uint32_t ph = (n / kSlots) & 1u;
   if (!mbar_test(&c.sm->full[s], ph)) {
+    if (tr) tr->mark(kTrWaitBegin, kStRing, layer, tok);
     const uint64_t t0 = global_ns();
     while (!mbar_test(&c.sm->full[s], ph)) {
       if (aborted(c)) break;
@@ -152,6 +155,7 @@ __device__ __forceinline__ uint32_t ring_wait(const Ctl& c, uint32_t n, int laye
         break;
       }
     }
+    if (tr) tr->mark(kTrWaitEnd, kStRing, layer, tok);
   }
   return smem_addr(c.sm->ring[s]);
 }
@@ -249,11 +253,14 @@ struct Producer {
   bool stop;
   uint64_t pol_w, pol_kv;
   int lane;
+  Tracer tr;  // row grid + cta of the trace buffer
 
   __device__ Producer(const Ctl& ctl) : c(ctl), n(0), stop(false) {
     lane = threadIdx.x & 31;
     pol_w = policy_evict_first();
     pol_kv = policy_evict_last();
+    tr = Tracer{ctl.trace ? ctl.trace + ((size_t)gridDim.x + blockIdx.x) * ctl.trace_cap : nullptr,
+                ctl.trace_cap, 0, kConsumerThreads};
   }
 
   // Reserve the next slot for `bytes`; returns its index or -1 once stopped.
@@ -264,6 +271,7 @@ struct Producer {
     int ok = 1;
     if (lane == 0) {
       if (!mbar_test(&c.sm->empty[s], ph)) {
+        tr.mark(kTrWaitBegin, kStSlot, static_cast<int>(n & 31u), 0);
         const uint64_t t0 = global_ns();
         while (!mbar_test(&c.sm->empty[s], ph)) {
           if (aborted(c)) { ok = 0; break; }
@@ -273,9 +281,11 @@ struct Producer {
             break;
           }
         }
+        tr.mark(kTrWaitEnd, kStSlot, static_cast<int>(n & 31u), 0);
       }
       if (ok && aborted(c)) ok = 0;
       if (ok) mbar_arrive_expect_tx(&c.sm->full[s], bytes);
+      tr.mark(kTrMark, kStIssue, static_cast<int>(n & 31u), 0);
     }
     ok = __shfl_sync(0xffffffffu, ok, 0);
     if (!ok) { stop = true; return -1; }
@@ -506,7 +516,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   const int zero_cta = G - 1;
   uint32_t n = 0;
   float xr[32];
-  Tracer tr{c.trace, c.trace_cap, 0};
+  Tracer tr{c.trace, c.trace_cap, 0, 0};
 
   int token = token0;
   for (int t = 0; t < p.n_tokens; ++t) {
@@ -546,7 +556,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       tr.mark(kTrMark, kSubANorm, l, t);
       for (int r = pl.qa; r < pl.qb;) {
         const int e = qkv_chunk_end(r, pl.qb);
-        const uint32_t sa = ring_wait(c, n, l, 0, t);
+        const uint32_t sa = ring_wait(c, n, l, 0, t, &tr);
         const int row = r + warp;
         if (row < e) {
           const float v = warp_sum(dot_row1024(sa + warp * 2048, xr, lane));
@@ -643,7 +653,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
           for (int k0 = ka; k0 < kb; k0 += kKeysPerChunk) {
             const int k1 = min(kb, k0 + kKeysPerChunk);
-            const uint32_t sa = ring_wait(c, n, l, 1, t);
+            const uint32_t sa = ring_wait(c, n, l, 1, t, &tr);
             float s0[4], s1[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -801,7 +811,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           for (int e = 0; e < 8; ++e) xo[e] = sm.attn[lane * 8 + e];
           for (int o0 = pl.oa; o0 < pl.ob; o0 += kORowsPerChunk) {
             const int o1 = min(pl.ob, o0 + kORowsPerChunk);
-            const uint32_t sa = ring_wait(c, n, l, 3, t);
+            const uint32_t sa = ring_wait(c, n, l, 3, t, &tr);
             float v[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -843,7 +853,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       // gate/up rows (megakernel.cu:100-142)
       for (int j0 = pl.ja; j0 < pl.jb; j0 += kGUPerChunk) {
         const int j1 = min(pl.jb, j0 + kGUPerChunk);
-        const uint32_t sa = ring_wait(c, n, l, 4, t);
+        const uint32_t sa = ring_wait(c, n, l, 4, t, &tr);
         const int jj = j0 + (warp & 7);
         if (jj < j1) {
           const float v =
@@ -866,7 +876,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         float pa = 0.f, pb = 0.f;
         for (int j0 = pl.ja; j0 < pl.jb; j0 += kRowsPerChunk1024) {
           const int j1 = min(pl.jb, j0 + kRowsPerChunk1024);
-          const uint32_t sa = ring_wait(c, n, l, 5, t);
+          const uint32_t sa = ring_wait(c, n, l, 5, t, &tr);
           for (int jj = j0; jj < j1; ++jj) {
             const uint32_t w = lds32(sa + (jj - j0) * 2048 + col * 2);
             const float mj = sm.m[jj - pl.ja];
@@ -887,7 +897,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         consumer_sync(kConsumerThreads);
         for (int d0 = pl.da; d0 < pl.db; d0 += kDownRowsPerChunk) {
           const int d1 = min(pl.db, d0 + kDownRowsPerChunk);
-          const uint32_t sa = ring_wait(c, n, l, 6, t);
+          const uint32_t sa = ring_wait(c, n, l, 6, t, &tr);
           const int row = warp / 3, third = warp % 3;
           if (warp < 15 && d0 + row < d1) {
             float acc = 0.f;
@@ -929,7 +939,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       norm_to_regs(sm.r, fwv, (p.flags & kFlagSkipFinalNorm) != 0, xr, sm.red);
       for (int v0 = pl.va; v0 < pl.vb; v0 += kRowsPerChunk1024) {
         const int v1 = min(pl.vb, v0 + kRowsPerChunk1024);
-        const uint32_t sa = ring_wait(c, n, -1, 8, t);
+        const uint32_t sa = ring_wait(c, n, -1, 8, t, &tr);
         const int row = v0 + warp;
         if (row < v1) {
           const float v = warp_sum(dot_row1024(sa + warp * 2048, xr, lane));

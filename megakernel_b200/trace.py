@@ -24,7 +24,7 @@ from .rope import rope_tables
 STAGE_NAMES = {0: "qkv", 1: "attn+o_proj", 2: "swiglu(+down)", 3: "down", 4: "lm_head",
                5: "split-combine", 6: "token", 7: "end", 8: "qkv:input", 9: "qkv:norm",
                10: "attn:head-prep", 11: "attn:softmax-v", 12: "attn:combine", 13: "swiglu:input+norm",
-               14: "swiglu:gate-up", 15: "swiglu:down"}
+               14: "swiglu:gate-up", 15: "swiglu:down", 16: "ring-fill", 17: "slot-free", 18: "issue"}
 KIND_NAMES = {0: "pre-wait", 1: "wait", 2: "publish", 3: "mark"}
 
 
@@ -59,7 +59,7 @@ class TracedDecoder:
         self.grid = min(props.multi_processor_count, 256)
 
     def run(self, token: int, position: int, n_tokens: int = 1, cap: int = 2048, traced: bool = True):
-        trace = torch.zeros((self.grid, cap), dtype=torch.int64, device=self.dev)
+        trace = torch.zeros((2 * self.grid, cap), dtype=torch.int64, device=self.dev)
         code = decode_call(embed=self.embed, lm_head=self.embed, final_norm=self.final_norm, layers=self.table,
                            down_t=(self.down_t.data_ptr() if self.down_t is not None else None),
                            cos_table=self.cos, sin_table=self.sin,
@@ -70,7 +70,11 @@ class TracedDecoder:
                            grid=self.grid, trace=(trace.data_ptr() if traced else None), trace_cap=cap)
         _lib.check(code, "mkb_decode")
         torch.cuda.synchronize(self.dev)
-        return decode_records(trace.cpu()) if traced else None
+        if not traced:
+            return None
+        recs = decode_records(trace.cpu())
+        self.producer_records = recs[self.grid:]
+        return recs[:self.grid]
 
 
 def decode_records(trace: torch.Tensor):
@@ -84,7 +88,7 @@ def decode_records(trace: torch.Tensor):
             u = v & ((1 << 64) - 1)
             code = u >> 48
             t = u & ((1 << 48) - 1)
-            recs.append((code & 3, (code >> 2) & 15, (code >> 6) & 31, (code >> 11) & 31, t))
+            recs.append((code & 3, (code >> 2) & 31, (code >> 7) & 31, (code >> 12) & 15, t))
         out.append(recs)
     return out
 
@@ -191,6 +195,23 @@ def main():
     if res is None:
         print("plain launches done")
         return
+    prod = getattr(td, "producer_records", None)
+    if prod:
+        waits = []
+        issues = []
+        for recs in prod:
+            tot, open_t = 0, None
+            for kind, st, _l, _t, t in recs:
+                if st == 17 and kind == 0:
+                    open_t = t
+                elif st == 17 and kind == 1 and open_t is not None:
+                    tot += t - open_t
+                    open_t = None
+                elif st == 18:
+                    issues.append(t)
+            waits.append(tot)
+        print(f"producer: slot-free waits per CTA per launch: mean {statistics.fmean(waits) / 1000:.1f} us, "
+              f"max {max(waits) / 1000:.1f} us; chunks issued {len(issues)}")
     print(f"config0 shapes, position {a.position}, {a.tokens} token(s) per launch, "
           f"{'reference' if a.reference_layout else 'transposed'} down layout, grid {td.grid}")
     print(format_summary(res))
