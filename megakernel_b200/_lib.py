@@ -11,7 +11,8 @@ from ctypes import (POINTER, Structure, c_float, c_int, c_int32, c_size_t, c_uin
                     c_ulonglong, c_void_p, c_char_p)
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libmkb200.so")
+# MKB200_LIB selects another build of the library (same ABI), e.g. a debug build.
+LIB_PATH = os.environ.get("MKB200_LIB") or os.path.join(HERE, "libmkb200.so")
 
 MKB_FLAG_LM_HEAD = 1
 MKB_FLAG_SKIP_FINAL_NORM = 2

@@ -88,10 +88,14 @@ struct alignas(128) Workspace {
   uint32_t arrive[32];                       // end-of-token arrivals (last one reduces)
   uint32_t tok_flag[32];                     // greedy token broadcast (multi-token launches)
   uint32_t error[32];                        // [0] code, [1] cta, [2] layer, [3] stage, [4] token
+  uint32_t tag_base[32];                     // [0]: tag of the last token decoded (tagged words)
   float acc_mid[kMaxLayers][kHidden];        // sum of o_proj partials per layer
   float acc_down[kMaxLayers][kHidden];       // sum of down-proj partials per layer
   float att_part[kNKV][kMaxSplits][2][kHeadDim + 4];  // split attention (m, l, o[128])
   float qkv[kQKVRows];
+  // Raw QKV outputs of every layer as tagged words (value | tag << 32); the tag
+  // of token t of a launch is tag_base + t + 1, so no reset is ever needed.
+  uint64_t qkv_tagged[kMaxLayers][kQKVRows];
   float mlp[kInter];
   float resid[kHidden];
   float cand_val[kMaxGrid];

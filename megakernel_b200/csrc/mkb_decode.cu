@@ -179,35 +179,6 @@ __device__ __forceinline__ void load_norm_w(const __nv_bfloat16* w, uint4 wv[4])
               : make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);  // bf16 1.0 pairs
 }
 
-__device__ void norm_to_regs(const float* v, const uint4 wvs[4], bool skip, float xr[32], float* s_red) {
-  const int tid = threadIdx.x;
-  const float a = v[tid], b = v[tid + kConsumerThreads];
-  const float ss = warp_sum(a * a + b * b);
-  if ((tid & 31) == 0) s_red[tid >> 5] = ss;
-  consumer_sync(kConsumerThreads);
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < kConsumerWarps; ++i) tot += s_red[i];
-  const float rstd = skip ? 1.0f : rsqrtf(tot * (1.0f / kHidden) + kEps);
-  const int lane = tid & 31;
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    const int idx = lane * 8 + g * 256;
-    const float4 v0 = *reinterpret_cast<const float4*>(v + idx);
-    const float4 v1 = *reinterpret_cast<const float4*>(v + idx + 4);
-    const uint4 wv = wvs[g];
-    xr[g * 8 + 0] = v0.x * rstd * bf_lo(wv.x);
-    xr[g * 8 + 1] = v0.y * rstd * bf_hi(wv.x);
-    xr[g * 8 + 2] = v0.z * rstd * bf_lo(wv.y);
-    xr[g * 8 + 3] = v0.w * rstd * bf_hi(wv.y);
-    xr[g * 8 + 4] = v1.x * rstd * bf_lo(wv.z);
-    xr[g * 8 + 5] = v1.y * rstd * bf_hi(wv.z);
-    xr[g * 8 + 6] = v1.z * rstd * bf_lo(wv.w);
-    xr[g * 8 + 7] = v1.w * rstd * bf_hi(wv.w);
-  }
-  consumer_sync(kConsumerThreads);  // s_red free for the next reduction
-}
-
 __device__ __forceinline__ float dot8(const uint4 w, const float* x) {
   float s = bf_lo(w.x) * x[0];
   s = fmaf(bf_hi(w.x), x[1], s);
@@ -502,8 +473,94 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 
 // ---- consumers -----------------------------------------------------------------
 
+// Wait for `cnt` consecutive chunks from ring position n (all already issued by
+// the producer); their slot addresses go to sa[].
+__device__ __forceinline__ void ring_wait_all(const Ctl& c, uint32_t n, int cnt, uint32_t* sa, int layer, int stage,
+                                              int tok, Tracer* tr) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+    if (i < cnt) sa[i] = ring_wait(c, n + i, layer, stage, tok, tr);
+}
+__device__ __forceinline__ void ring_done_all(const Ctl& c, uint32_t& n, int cnt) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0)
+    for (int i = 0; i < cnt; ++i) mbar_arrive(&c.sm->empty[(n + i) % kSlots]);
+  n += cnt;
+}
+
+// Block-wide sum of a*a + b*b over the consumer threads (one named barrier;
+// s_red alternates between two halves so no trailing barrier is needed).
+__device__ __forceinline__ float block_sumsq(float a, float b, float* s_red, int& flip) {
+  const float ss = warp_sum(a * a + b * b);
+  float* buf = s_red + (flip ? kConsumerWarps : 0);
+  flip ^= 1;
+  if ((threadIdx.x & 31) == 0) buf[threadIdx.x >> 5] = ss;
+  consumer_sync(kConsumerThreads);
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kConsumerWarps; ++i) tot += buf[i];
+  return tot;
+}
+
+// The 32 normalised activations this lane multiplies into every 2 KB row:
+// elements lane*8 + g*256 + e of v * rstd * w (RMSNorm, megakernel.cu:704-739).
+__device__ __forceinline__ void xr_from(const float* v, float rstd, const uint4 wv[4], float xr[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int idx = lane * 8 + g * 256;
+    const float4 v0 = *reinterpret_cast<const float4*>(v + idx);
+    const float4 v1 = *reinterpret_cast<const float4*>(v + idx + 4);
+    xr[g * 8 + 0] = v0.x * rstd * bf_lo(wv[g].x);
+    xr[g * 8 + 1] = v0.y * rstd * bf_hi(wv[g].x);
+    xr[g * 8 + 2] = v0.z * rstd * bf_lo(wv[g].y);
+    xr[g * 8 + 3] = v0.w * rstd * bf_hi(wv[g].y);
+    xr[g * 8 + 4] = v1.x * rstd * bf_lo(wv[g].z);
+    xr[g * 8 + 5] = v1.y * rstd * bf_hi(wv[g].z);
+    xr[g * 8 + 6] = v1.z * rstd * bf_lo(wv[g].w);
+    xr[g * 8 + 7] = v1.w * rstd * bf_hi(wv[g].w);
+  }
+}
+
+// Butterfly sums of three per-lane partials at once (independent shuffle chains).
+__device__ __forceinline__ void warp_sum3(float& a, float& b, float& d) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+    d += __shfl_xor_sync(0xffffffffu, d, o);
+  }
+}
+
+// Bounded poll of two tagged words (16 bytes) until both carry `tag`.
+__device__ __forceinline__ void poll_tagged2(const Ctl& c, const uint64_t* p, uint32_t tag, float& v0, float& v1,
+                                             int layer, int tok) {
+  uint64_t a, b;
+  ld_tagged2(p, a, b);
+  if (static_cast<uint32_t>(a >> 32) != tag || static_cast<uint32_t>(b >> 32) != tag) {
+    const uint64_t t0 = global_ns();
+    uint32_t it = 0;
+    while (true) {
+      ld_tagged2(p, a, b);
+      if (static_cast<uint32_t>(a >> 32) == tag && static_cast<uint32_t>(b >> 32) == tag) break;
+      if ((++it & 15u) == 0u) {
+        if (aborted(c) || ld_relaxed(&c.ws->error[0]) != 0u) {
+          *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
+          break;
+        }
+        if (global_ns() - t0 > c.timeout) {
+          raise_error(c, kErrTimeoutTransition, layer, kStBC, tok);
+          break;
+        }
+      }
+    }
+  }
+  v0 = __uint_as_float(static_cast<uint32_t>(a));
+  v1 = __uint_as_float(static_cast<uint32_t>(b));
+}
+
 __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int token0, int pos0, int cl0,
-                             int splits) {
+                             int splits, uint32_t tag0) {
   Smem& sm = *c.sm;
   Workspace* ws = p.ws;
   const int tid = threadIdx.x;
@@ -515,6 +572,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   const int lb = p.layer_begin, le = p.layer_end;
   const int zero_cta = G - 1;
   uint32_t n = 0;
+  int flip = 0;
   float xr[32];
   Tracer tr{c.trace, c.trace_cap, 0, 0};
 
@@ -524,6 +582,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     const int cl = cl0 + t;
     const uint32_t tgtG = static_cast<uint32_t>(G * (t + 1));
     const uint32_t tgtBC = static_cast<uint32_t>(nbc * (t + 1));
+    const uint32_t tag = tag0 + static_cast<uint32_t>(t) + 1u;
     tr.mark(kTrMark, kStToken, 0, t);
 
     // ---- token input: embedding gather (megakernel.cu:783-795) ----
@@ -535,109 +594,141 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       token = sm.token;
     }
     token = min(max(token, 0), kVocab - 1);
-    for (int i = tid; i < kHidden; i += kConsumerThreads)
-      sm.r[i] = p.input_residual ? __ldcg(p.input_residual + i)
-                                 : __bfloat162float(p.embed[(size_t)token * kHidden + i]);
-    consumer_sync(kConsumerThreads);
+    float r0 = p.input_residual ? __ldcg(p.input_residual + tid)
+                                : __bfloat162float(p.embed[(size_t)token * kHidden + tid]);
+    float r1 = p.input_residual ? __ldcg(p.input_residual + tid + kConsumerThreads)
+                                : __bfloat162float(p.embed[(size_t)token * kHidden + tid + kConsumerThreads]);
 
     for (int l = lb; l < le; ++l) {
       const LayerWeights* lw = p.layers + l;
       uint4 nwv[4];
-      // ================= A: RMSNorm + QKV (megakernel.cu:704-739, 633-701) ======
+      // ================= A: RMSNorm + QKV rows (megakernel.cu:704-739, 633-701) ===
       load_norm_w(ldg_ptr(&lw->norm_weight), nwv);
       if (l > lb) {
         transition_wait(c, tr, &ws->sync[l - 1][fused ? 2 : 3][0], tgtG, l, kStA, t);
-        for (int i = tid; i < kHidden; i += kConsumerThreads)
-          sm.r[i] = fused ? sm.rmid[i] + __ldcg(&ws->acc_down[l - 1][i]) : __ldcg(&ws->resid[i]);
-        consumer_sync(kConsumerThreads);
+        if (fused) {
+          r0 = sm.rmid[tid] + __ldcg(&ws->acc_down[l - 1][tid]);
+          r1 = sm.rmid[tid + kConsumerThreads] + __ldcg(&ws->acc_down[l - 1][tid + kConsumerThreads]);
+        } else {
+          r0 = __ldcg(&ws->resid[tid]);
+          r1 = __ldcg(&ws->resid[tid + kConsumerThreads]);
+        }
+        // Every CTA has finished layer l-1 (and so read the accumulators of
+        // layer l-2): clear those for the next token.
+        if (c.cta == zero_cta && l >= lb + 2) {
+          ws->acc_mid[l - 2][tid] = 0.f;
+          ws->acc_mid[l - 2][tid + kConsumerThreads] = 0.f;
+          ws->acc_down[l - 2][tid] = 0.f;
+          ws->acc_down[l - 2][tid + kConsumerThreads] = 0.f;
+        }
       }
-      tr.mark(kTrMark, kSubAInput, l, t);
-      norm_to_regs(sm.r, nwv, false, xr, sm.red);
+      sm.r[tid] = r0;
+      sm.r[tid + kConsumerThreads] = r1;
+      {
+        const float tot = block_sumsq(r0, r1, sm.red, flip);
+        tr.mark(kTrMark, kSubAInput, l, t);
+        xr_from(sm.r, rsqrtf(tot * (1.0f / kHidden) + kEps), nwv, xr);
+      }
       tr.mark(kTrMark, kSubANorm, l, t);
+      // rows of up to three chunks per pass, reductions interleaved
       for (int r = pl.qa; r < pl.qb;) {
-        const int e = qkv_chunk_end(r, pl.qb);
-        const uint32_t sa = ring_wait(c, n, l, 0, t, &tr);
-        const int row = r + warp;
-        if (row < e) {
-          const float v = warp_sum(dot_row1024(sa + warp * 2048, xr, lane));
-          if (lane == 0) {
+        const int ra0 = r, ea0 = qkv_chunk_end(ra0, pl.qb);
+        const int ra1 = ea0, ea1 = ra1 < pl.qb ? qkv_chunk_end(ra1, pl.qb) : ra1;
+        const int ra2 = ea1, ea2 = ra2 < pl.qb ? qkv_chunk_end(ra2, pl.qb) : ra2;
+        const int na = 1 + (ea1 > ra1) + (ea2 > ra2);
+        r = ea2;
+        uint32_t sa[3];
+        ring_wait_all(c, n, na, sa, l, 0, t, &tr);
+        float v0 = ra0 + warp < ea0 ? dot_row1024(sa[0] + warp * 2048, xr, lane) : 0.f;
+        float v1 = ra1 + warp < ea1 ? dot_row1024(sa[1] + warp * 2048, xr, lane) : 0.f;
+        float v2 = ra2 + warp < ea2 ? dot_row1024(sa[2] + warp * 2048, xr, lane) : 0.f;
+        warp_sum3(v0, v1, v2);
+        ring_done_all(c, n, na);
+        if (lane < 3 && !(t == 0 && l == lb && c.cta == p.withhold_cta)) {
+          const int row = warp + (lane == 0 ? ra0 : (lane == 1 ? ra1 : ra2));
+          const int end = lane == 0 ? ea0 : (lane == 1 ? ea1 : ea2);
+          const float val = lane == 0 ? v0 : (lane == 1 ? v1 : v2);
+          if (row < end) {
+            st_tagged(&ws->qkv_tagged[l][row], val, tag);
             float* dst = row < kQSize ? p.q_out + row
                          : row < kQSize + kKVSize ? p.k_out + (row - kQSize)
                                                   : p.v_out + (row - kQSize - kKVSize);
-            *dst = v;
+            *dst = val;
           }
         }
-        ring_done(c, n);
-        r = e;
       }
-      if (!(t == 0 && l == lb && c.cta == p.withhold_cta)) transition_publish(tr, &ws->sync[l][0][0], l, kStA, t);
-      else consumer_sync(kConsumerThreads);
+      tr.mark(kTrPublish, kStA, l, t);
 
       // ================= BC: head norm + RoPE + KV append, attention, o_proj =====
       if (pl.in_bc) {
         const int h = pl.h;
-        // per-head norm weights and this position's RoPE row do not depend on
-        // the transition: load them while it is pending
+        // Per-head norm weights and this position's RoPE row do not depend on
+        // QKV: load them before polling. Lane owns dims 2l, 2l+1, 64+2l, 65+2l.
         float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f, cs0 = 0.f, sn0 = 0.f, cs1 = 0.f, sn1 = 0.f;
+        const int d0 = 2 * lane;
         if (warp < 3) {
           const __nv_bfloat16* nw = warp < 2 ? ldg_ptr(&lw->q_norm_weight) : ldg_ptr(&lw->k_norm_weight);
-          w0 = __bfloat162float(nw[lane]);
-          w1 = __bfloat162float(nw[lane + 32]);
-          w2 = __bfloat162float(nw[lane + 64]);
-          w3 = __bfloat162float(nw[lane + 96]);
+          w0 = __bfloat162float(nw[d0]);
+          w1 = __bfloat162float(nw[d0 + 1]);
+          w2 = __bfloat162float(nw[d0 + 64]);
+          w3 = __bfloat162float(nw[d0 + 65]);
           const size_t rb = (size_t)pos * kHeadDim;
-          cs0 = rope_at(p.cos_table, p.rope_fp32, rb + lane);
-          sn0 = rope_at(p.sin_table, p.rope_fp32, rb + lane);
-          cs1 = rope_at(p.cos_table, p.rope_fp32, rb + lane + 32);
-          sn1 = rope_at(p.sin_table, p.rope_fp32, rb + lane + 32);
+          cs0 = rope_at(p.cos_table, p.rope_fp32, rb + d0);
+          sn0 = rope_at(p.sin_table, p.rope_fp32, rb + d0);
+          cs1 = rope_at(p.cos_table, p.rope_fp32, rb + d0 + 1);
+          sn1 = rope_at(p.sin_table, p.rope_fp32, rb + d0 + 1);
         }
-        transition_wait(c, tr, &ws->sync[l][0][0], tgtG, l, kStBC, t);
-        // q_norm / k_norm + rotate-half RoPE (megakernel.cu:490-630)
-        if (warp < 3) {
-          const float* src = warp < 2 ? p.q_out + (2 * h + warp) * kHeadDim : p.k_out + h * kHeadDim;
-          const float x0 = __ldcg(src + lane), x1 = __ldcg(src + lane + 32);
-          const float x2 = __ldcg(src + lane + 64), x3 = __ldcg(src + lane + 96);
-          const float ss = warp_sum(x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3);
-          const float rstd = rsqrtf(ss * (1.0f / kHeadDim) + kEps);
-          const float y0 = x0 * rstd * w0;
-          const float y1 = x1 * rstd * w1;
-          const float y2 = x2 * rstd * w2;
-          const float y3 = x3 * rstd * w3;
-          const float o0 = y0 * cs0 - y2 * sn0, o2 = y2 * cs0 + y0 * sn0;
-          const float o1 = y1 * cs1 - y3 * sn1, o3 = y3 * cs1 + y1 * sn1;
-          if (warp < 2) {
-            const float sc = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
-            sm.q[warp][lane] = o0 * sc;
-            sm.q[warp][lane + 32] = o1 * sc;
-            sm.q[warp][lane + 64] = o2 * sc;
-            sm.q[warp][lane + 96] = o3 * sc;
-          } else {
-            const __nv_bfloat16 b0 = __float2bfloat16(o0), b1 = __float2bfloat16(o1);
-            const __nv_bfloat16 b2 = __float2bfloat16(o2), b3 = __float2bfloat16(o3);
-            sm.knew[lane] = __bfloat162float(b0);
-            sm.knew[lane + 32] = __bfloat162float(b1);
-            sm.knew[lane + 64] = __bfloat162float(b2);
-            sm.knew[lane + 96] = __bfloat162float(b3);
-            if (pl.c == 0) {
-              __nv_bfloat16* dst = p.k_cache + (((size_t)l * kNKV + h) * p.max_seq + pos) * kHeadDim;
-              dst[lane] = b0;
-              dst[lane + 32] = b1;
-              dst[lane + 64] = b2;
-              dst[lane + 96] = b3;
+        tr.mark(kTrWaitBegin, kStBC, l, t);
+        if (warp < 4) {
+          const int base = warp < 2 ? (2 * h + warp) * kHeadDim
+                                    : (warp == 2 ? kQSize + h * kHeadDim : kQSize + kKVSize + h * kHeadDim);
+          float x0, x1, x2, x3;  // dims d0, d0+1, d0+64, d0+65
+          poll_tagged2(c, &ws->qkv_tagged[l][base + d0], tag, x0, x1, l, t);
+          poll_tagged2(c, &ws->qkv_tagged[l][base + d0 + 64], tag, x2, x3, l, t);
+          if (warp < 3) {
+            // q_norm / k_norm + rotate-half RoPE (megakernel.cu:490-630)
+            const float ss = warp_sum(x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3);
+            const float rstd = rsqrtf(ss * (1.0f / kHeadDim) + kEps);
+            const float y0 = x0 * rstd * w0, y1 = x1 * rstd * w1;
+            const float y2 = x2 * rstd * w2, y3 = x3 * rstd * w3;
+            const float o0 = y0 * cs0 - y2 * sn0, o2 = y2 * cs0 + y0 * sn0;   // pair (d0, d0+64)
+            const float o1 = y1 * cs1 - y3 * sn1, o3 = y3 * cs1 + y1 * sn1;   // pair (d0+1, d0+65)
+            if (warp < 2) {
+              const float sc = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
+              sm.q[warp][d0] = o0 * sc;
+              sm.q[warp][d0 + 1] = o1 * sc;
+              sm.q[warp][d0 + 64] = o2 * sc;
+              sm.q[warp][d0 + 65] = o3 * sc;
+            } else {
+              const __nv_bfloat162 b01 = __floats2bfloat162_rn(o0, o1);
+              const __nv_bfloat162 b23 = __floats2bfloat162_rn(o2, o3);
+              sm.knew[d0] = __low2float(b01);
+              sm.knew[d0 + 1] = __high2float(b01);
+              sm.knew[d0 + 64] = __low2float(b23);
+              sm.knew[d0 + 65] = __high2float(b23);
+              if (pl.c == 0) {
+                __nv_bfloat16* dst = p.k_cache + (((size_t)l * kNKV + h) * p.max_seq + pos) * kHeadDim;
+                *reinterpret_cast<__nv_bfloat162*>(dst + d0) = b01;
+                *reinterpret_cast<__nv_bfloat162*>(dst + d0 + 64) = b23;
+              }
             }
-          }
-        } else if (warp == 3) {
-          __nv_bfloat16* dst = p.v_cache + (((size_t)l * kNKV + h) * p.max_seq + pos) * kHeadDim;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const __nv_bfloat16 b = __float2bfloat16(__ldcg(p.v_out + h * kHeadDim + lane + 32 * i));
-            sm.vnew[lane + 32 * i] = __bfloat162float(b);
-            if (pl.c == 0) dst[lane + 32 * i] = b;
+          } else {
+            const __nv_bfloat162 b01 = __floats2bfloat162_rn(x0, x1);
+            const __nv_bfloat162 b23 = __floats2bfloat162_rn(x2, x3);
+            sm.vnew[d0] = __low2float(b01);
+            sm.vnew[d0 + 1] = __high2float(b01);
+            sm.vnew[d0 + 64] = __low2float(b23);
+            sm.vnew[d0 + 65] = __high2float(b23);
+            if (pl.c == 0) {
+              __nv_bfloat16* dst = p.v_cache + (((size_t)l * kNKV + h) * p.max_seq + pos) * kHeadDim;
+              *reinterpret_cast<__nv_bfloat162*>(dst + d0) = b01;
+              *reinterpret_cast<__nv_bfloat162*>(dst + d0 + 64) = b23;
+            }
           }
         }
         consumer_sync(kConsumerThreads);
+        tr.mark(kTrWaitEnd, kStBC, l, t);
         tr.mark(kTrMark, kSubBCPrep, l, t);
-
         // GQA decode attention over keys [ka, kb) (megakernel.cu:228-370),
         // per-warp online softmax in the exp2 domain, then a 16-warp combine.
         int ka, kb;
@@ -833,38 +924,42 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         }
         transition_publish(tr, &ws->sync[l][1][0], l, kStBC, t);
       }
-      // Zero the previous layer's accumulators: every CTA has read them (it
-      // passed T_A of this layer), and their next use is the next token.
-      if (c.cta == zero_cta && l > lb) {
-        if (!pl.in_bc) transition_wait(c, tr, &ws->sync[l][0][0], tgtG, l, kStBC, t);
-        for (int i = tid; i < kHidden; i += kConsumerThreads) {
-          ws->acc_mid[l - 1][i] = 0.f;
-          ws->acc_down[l - 1][i] = 0.f;
-        }
-      }
 
       // ================= DE: post norm, SwiGLU rows, down partial ===============
       load_norm_w(ldg_ptr(&lw->post_attn_norm_weight), nwv);
       transition_wait(c, tr, &ws->sync[l][1][0], tgtBC, l, kStDE, t);
-      for (int i = tid; i < kHidden; i += kConsumerThreads) sm.rmid[i] = sm.r[i] + __ldcg(&ws->acc_mid[l][i]);
-      consumer_sync(kConsumerThreads);
-      norm_to_regs(sm.rmid, nwv, false, xr, sm.red);
+      {
+        const float m0 = sm.r[tid] + __ldcg(&ws->acc_mid[l][tid]);
+        const float m1 = sm.r[tid + kConsumerThreads] + __ldcg(&ws->acc_mid[l][tid + kConsumerThreads]);
+        sm.rmid[tid] = m0;
+        sm.rmid[tid + kConsumerThreads] = m1;
+        const float tot = block_sumsq(m0, m1, sm.red, flip);
+        xr_from(sm.rmid, rsqrtf(tot * (1.0f / kHidden) + kEps), nwv, xr);
+      }
       tr.mark(kTrMark, kSubDENorm, l, t);
-      // gate/up rows (megakernel.cu:100-142)
-      for (int j0 = pl.ja; j0 < pl.jb; j0 += kGUPerChunk) {
-        const int j1 = min(pl.jb, j0 + kGUPerChunk);
-        const uint32_t sa = ring_wait(c, n, l, 4, t, &tr);
-        const int jj = j0 + (warp & 7);
-        if (jj < j1) {
-          const float v =
-              warp_sum(dot_row1024(sa + (warp >= 8 ? kSlotBytes / 2 : 0) + (warp & 7) * 2048, xr, lane));
-          if (lane == 0) sm.gu[warp >> 3][jj - pl.ja] = v;
+      const int nj = pl.jb - pl.ja;
+      // gate rows (warps 0-7) and up rows (warps 8-15), three chunks per pass
+      // (megakernel.cu:100-142)
+      for (int jb0 = 0; jb0 < nj; jb0 += 3 * kGUPerChunk) {
+        const int ng = min(3, (nj - jb0 + kGUPerChunk - 1) / kGUPerChunk);
+        uint32_t sa[3];
+        ring_wait_all(c, n, ng, sa, l, 4, t, &tr);
+        const uint32_t half = warp >= 8 ? kSlotBytes / 2 : 0;
+        const int j0 = jb0 + (warp & 7);
+        float v0 = j0 < nj ? dot_row1024(sa[0] + half + (warp & 7) * 2048, xr, lane) : 0.f;
+        float v1 = (ng > 1 && j0 + kGUPerChunk < nj) ? dot_row1024(sa[1] + half + (warp & 7) * 2048, xr, lane) : 0.f;
+        float v2 = (ng > 2 && j0 + 2 * kGUPerChunk < nj) ? dot_row1024(sa[2] + half + (warp & 7) * 2048, xr, lane)
+                                                           : 0.f;
+        warp_sum3(v0, v1, v2);
+        ring_done_all(c, n, ng);
+        if (lane < 3) {
+          const int jj = j0 + lane * kGUPerChunk;
+          if (jj < nj) sm.gu[warp >> 3][jj] = lane == 0 ? v0 : (lane == 1 ? v1 : v2);
         }
-        ring_done(c, n);
       }
       consumer_sync(kConsumerThreads);
       tr.mark(kTrMark, kSubDEGU, l, t);
-      if (tid < pl.jb - pl.ja) {
+      if (tid < nj) {
         const float g = sm.gu[0][tid], u = sm.gu[1][tid];
         sm.m[tid] = g / (1.0f + expf(-g)) * u;  // silu (config.cuh:177-179) * up
       }
@@ -874,23 +969,28 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         // outputs [64w, 64w+64), two per lane (megakernel.cu:53-90, split by K)
         const int col = warp * 64 + lane * 2;
         float pa = 0.f, pb = 0.f;
-        for (int j0 = pl.ja; j0 < pl.jb; j0 += kRowsPerChunk1024) {
-          const int j1 = min(pl.jb, j0 + kRowsPerChunk1024);
-          const uint32_t sa = ring_wait(c, n, l, 5, t, &tr);
-          for (int jj = j0; jj < j1; ++jj) {
-            const uint32_t w = lds32(sa + (jj - j0) * 2048 + col * 2);
-            const float mj = sm.m[jj - pl.ja];
-            pa = fmaf(bf_lo(w), mj, pa);
-            pb = fmaf(bf_hi(w), mj, pb);
+        for (int jb0 = 0; jb0 < nj; jb0 += 3 * kRowsPerChunk1024) {
+          const int nd = min(3, (nj - jb0 + kRowsPerChunk1024 - 1) / kRowsPerChunk1024);
+          uint32_t sa[3];
+          ring_wait_all(c, n, nd, sa, l, 5, t, &tr);
+          for (int i = 0; i < nd; ++i) {
+            const int js = jb0 + i * kRowsPerChunk1024;
+            const int j1 = min(nj, js + kRowsPerChunk1024);
+            for (int jj = js; jj < j1; ++jj) {
+              const uint32_t w = lds32(sa[i] + (jj - js) * 2048 + col * 2);
+              const float mj = sm.m[jj];
+              pa = fmaf(bf_lo(w), mj, pa);
+              pb = fmaf(bf_hi(w), mj, pb);
+            }
           }
-          ring_done(c, n);
+          ring_done_all(c, n, nd);
         }
         tr.mark(kTrMark, kSubDEDown, l, t);
         red_add_v2_f32(&ws->acc_down[l][col], pa, pb);
         transition_publish(tr, &ws->sync[l][2][0], l, kStDE, t);
       } else {
         // reference layout: publish the SwiGLU vector, then whole down rows
-        for (int j = tid; j < pl.jb - pl.ja; j += kConsumerThreads) p.mlp_out[pl.ja + j] = sm.m[j];
+        for (int j = tid; j < nj; j += kConsumerThreads) p.mlp_out[pl.ja + j] = sm.m[j];
         transition_publish(tr, &ws->sync[l][2][0], l, kStDE, t);
         transition_wait(c, tr, &ws->sync[l][2][0], tgtG, l, kStE, t);
         for (int i = tid; i < kInter; i += kConsumerThreads) sm.u.x[i] = __ldcg(p.mlp_out + i);
@@ -927,16 +1027,26 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     load_norm_w((p.flags & kFlagSkipFinalNorm) ? nullptr : p.final_norm, fwv);
     if (le > lb) {
       transition_wait(c, tr, &ws->sync[le - 1][fused ? 2 : 3][0], tgtG, le - 1, kStLM, t);
-      for (int i = tid; i < kHidden; i += kConsumerThreads)
-        sm.r[i] = fused ? sm.rmid[i] + __ldcg(&ws->acc_down[le - 1][i]) : __ldcg(&ws->resid[i]);
-      consumer_sync(kConsumerThreads);
+      if (fused) {
+        r0 = sm.rmid[tid] + __ldcg(&ws->acc_down[le - 1][tid]);
+        r1 = sm.rmid[tid + kConsumerThreads] + __ldcg(&ws->acc_down[le - 1][tid + kConsumerThreads]);
+      } else {
+        r0 = __ldcg(&ws->resid[tid]);
+        r1 = __ldcg(&ws->resid[tid + kConsumerThreads]);
+      }
     }
-    if (c.cta == 0 && p.residual_out != nullptr && t == p.n_tokens - 1)
-      for (int i = tid; i < kHidden; i += kConsumerThreads) p.residual_out[i] = sm.r[i];
+    sm.r[tid] = r0;
+    sm.r[tid + kConsumerThreads] = r1;
+    if (c.cta == 0 && p.residual_out != nullptr && t == p.n_tokens - 1) {
+      p.residual_out[tid] = r0;
+      p.residual_out[tid + kConsumerThreads] = r1;
+    }
     float bv = -INFINITY;
     int bi = INT_MAX;
     if (p.flags & kFlagLmHead) {
-      norm_to_regs(sm.r, fwv, (p.flags & kFlagSkipFinalNorm) != 0, xr, sm.red);
+      const float tot = block_sumsq(r0, r1, sm.red, flip);
+      const float rstd = (p.flags & kFlagSkipFinalNorm) ? 1.0f : rsqrtf(tot * (1.0f / kHidden) + kEps);
+      xr_from(sm.r, rstd, fwv, xr);
       for (int v0 = pl.va; v0 < pl.vb; v0 += kRowsPerChunk1024) {
         const int v1 = min(pl.vb, v0 + kRowsPerChunk1024);
         const uint32_t sa = ring_wait(c, n, -1, 8, t, &tr);
@@ -966,7 +1076,6 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         ws->cand_idx[c.cta] = bi;
       }
     }
-
     // ---- end of token: the last CTA to arrive reduces the argmax and resets ---
     tr.mark(kTrMark, kStLM, 0, t);
     consumer_sync(kConsumerThreads);
@@ -1019,9 +1128,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           best = i;
         }
       }
+      // the last two layers' accumulators (earlier ones were cleared on the way)
       for (int i = tid; i < kHidden; i += kConsumerThreads) {
-        ws->acc_mid[le > lb ? le - 1 : 0][i] = 0.f;
-        ws->acc_down[le > lb ? le - 1 : 0][i] = 0.f;
+        for (int l = max(lb, le - 2); l < le; ++l) {
+          ws->acc_mid[l][i] = 0.f;
+          ws->acc_down[l][i] = 0.f;
+        }
       }
       const bool last_tok = t == p.n_tokens - 1;
       if (last_tok) {
@@ -1041,6 +1153,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         if (last_tok) {
           ws->arrive[0] = 0u;
           ws->tok_flag[0] = 0u;
+          ws->tag_base[0] = tag0 + static_cast<uint32_t>(p.n_tokens);
         } else {
           ws->tok_flag[1] = static_cast<uint32_t>(best);
           __threadfence();
@@ -1051,6 +1164,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   }
 }
 
+
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem* sm = reinterpret_cast<Smem*>(smem_raw);
@@ -1058,6 +1172,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
         p.trace ? p.trace + (size_t)blockIdx.x * p.trace_cap : nullptr, p.trace_cap};
 
   int token = p.token, pos = p.position, cl = p.cache_len;
+  const uint32_t tag0 = __ldcg(&p.ws->tag_base[0]);
   if (p.step != nullptr) {
     token = __ldcg(p.step + 0);
     pos = __ldcg(p.step + 1);
@@ -1092,7 +1207,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
   if (threadIdx.x >= kConsumerThreads) {
     producer_run(p, pl, c, pos, cl, splits);
   } else {
-    consumer_run(p, pl, c, token, pos, cl, splits);
+    consumer_run(p, pl, c, token, pos, cl, splits, tag0);
   }
 }
 

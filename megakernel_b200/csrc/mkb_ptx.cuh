@@ -95,6 +95,15 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
 __device__ __forceinline__ void red_add_v2_f32(float* p, float a, float b) {
   asm volatile("red.relaxed.gpu.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
 }
+// Tagged 8-byte words: (tag << 32) | float bits, written and read as single
+// 64-bit accesses, so a reader that sees the expected tag also sees its value.
+__device__ __forceinline__ void st_tagged(uint64_t* p, float v, uint32_t tag) {
+  const uint64_t w = (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void ld_tagged2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

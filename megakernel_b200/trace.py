@@ -24,7 +24,8 @@ from .rope import rope_tables
 STAGE_NAMES = {0: "qkv", 1: "attn+o_proj", 2: "swiglu(+down)", 3: "down", 4: "lm_head",
                5: "split-combine", 6: "token", 7: "end", 8: "qkv:input", 9: "qkv:norm",
                10: "attn:head-prep", 11: "attn:softmax-v", 12: "attn:combine", 13: "swiglu:input+norm",
-               14: "swiglu:gate-up", 15: "swiglu:down", 16: "ring-fill", 17: "slot-free", 18: "issue"}
+               14: "swiglu:gate-up", 15: "swiglu:down", 16: "ring-fill", 17: "slot-free", 18: "issue",
+               19: "mark19", 20: "mark20", 21: "mark21", 22: "mark22", 23: "mark23"}
 KIND_NAMES = {0: "pre-wait", 1: "wait", 2: "publish", 3: "mark"}
 
 
@@ -132,7 +133,8 @@ def summarize(per_cta) -> dict:
     seg = defaultdict(list)
     for recs in per_cta:
         for prev, cur in zip(recs, recs[1:]):
-            label = (f"{KIND_NAMES[cur[0]]}:{STAGE_NAMES[cur[1]]}" if cur[0] != 3 else STAGE_NAMES[cur[1]])
+            name = STAGE_NAMES.get(cur[1], f"mark{cur[1]}")
+            label = f"{KIND_NAMES[cur[0]]}:{name}" if cur[0] != 3 else name
             seg[label].append(cur[4] - prev[4])
     med = lambda xs: statistics.median(xs) / 1000.0 if xs else None  # noqa: E731
     mean = lambda xs: statistics.fmean(xs) / 1000.0 if xs else None  # noqa: E731
