@@ -64,6 +64,10 @@ struct __align__(128) Smem {
 constexpr size_t kSmemBytes = sizeof(Smem);
 static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 
+// Upper bound on one hardware-suspended mbarrier wait; the enclosing loops
+// re-check the abort flag and the overall timeout after each.
+constexpr uint32_t kSuspendNs = 20000;
+
 struct Ctl {
   Smem* sm;
   Workspace* ws;
@@ -148,7 +152,7 @@ __device__ __forceinline__ uint32_t ring_wait(const Ctl& c, uint32_t n, int laye
   if (!mbar_test(&c.sm->full[s], ph)) {
     if (tr) tr->mark(kTrWaitBegin, kStRing, layer, tok);
     const uint64_t t0 = global_ns();
-    while (!mbar_test(&c.sm->full[s], ph)) {
+    while (!mbar_wait(&c.sm->full[s], ph, kSuspendNs)) {
       if (aborted(c)) break;
       if (global_ns() - t0 > c.timeout) {
         raise_error(c, kErrTimeoutRing, layer, stage, tok);
@@ -244,7 +248,7 @@ struct Producer {
       if (!mbar_test(&c.sm->empty[s], ph)) {
         tr.mark(kTrWaitBegin, kStSlot, static_cast<int>(n & 31u), 0);
         const uint64_t t0 = global_ns();
-        while (!mbar_test(&c.sm->empty[s], ph)) {
+        while (!mbar_wait(&c.sm->empty[s], ph, kSuspendNs)) {
           if (aborted(c)) { ok = 0; break; }
           if (global_ns() - t0 > c.timeout) {
             raise_error(c, kErrTimeoutRing, -1, -1, -1);
@@ -289,7 +293,7 @@ struct Producer {
       const uint32_t last = n - 1u - ((n - 1u - s) % kSlots);
       const uint32_t ph = (last / kSlots) & 1u;
       const uint64_t t0 = global_ns();
-      while (!mbar_test(&c.sm->full[s], ph)) {
+      while (!mbar_wait(&c.sm->full[s], ph, kSuspendNs)) {
         if (global_ns() - t0 > c.timeout) break;
       }
     }
