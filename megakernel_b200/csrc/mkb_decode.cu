@@ -234,8 +234,10 @@ struct Producer {
     lane = threadIdx.x & 31;
     pol_w = policy_evict_first();
     pol_kv = policy_evict_last();
-    tr = Tracer{ctl.trace ? ctl.trace + ((size_t)gridDim.x + blockIdx.x) * ctl.trace_cap : nullptr,
-                ctl.trace_cap, 0, kConsumerThreads};
+    // ctl.trace is this CTA's consumer row (base + cta * cap); its producer row
+    // is base + (grid + cta) * cap.
+    tr = Tracer{ctl.trace ? ctl.trace + (size_t)gridDim.x * ctl.trace_cap : nullptr, ctl.trace_cap, 0,
+                kConsumerThreads};
   }
 
   // Reserve the next slot for `bytes`; returns its index or -1 once stopped.
