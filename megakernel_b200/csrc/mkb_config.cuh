@@ -31,11 +31,16 @@ constexpr int kSlots = 6;
 constexpr int kMaxGrid = 256;
 constexpr int kMaxSplits = 32;
 
-// Chunk geometry (rows per ring slot) for each streamed matrix.
-constexpr int kRowsPerChunk1024 = kSlotBytes / (kHidden * 2);   // 16 rows of 2 KB
+// Chunk geometry (rows per ring slot) for each streamed matrix. Rows read by
+// the tensor-core GEMVs (ldmatrix) are stored at a padded stride so that the 8
+// rows of an 8x8 matrix fall in different shared-memory banks.
+constexpr int kRowStride = kHidden * 2 + 16;                     // 2064 B per padded 2 KB row
+constexpr int kORowStride = 2 * kHeadDim * 2 + 16;              // 528 B per padded o_proj row slice
+constexpr int kRowsPerChunk1024 = kSlotBytes / (kHidden * 2);   // 16 contiguous 2 KB rows (LM head, WdT)
+constexpr int kQKVRowsPerChunk = kSlotBytes / kRowStride;       // 15 padded QKV rows
 constexpr int kKeysPerChunk = kSlotBytes / 2 / (kHeadDim * 2);  // 64 keys: K half + V half
-constexpr int kORowsPerChunk = kSlotBytes / (2 * kHeadDim * 2);   // 64 rows of 512 B (2 heads)
-constexpr int kGUPerChunk = kSlotBytes / 2 / (kHidden * 2);     // 8 gate rows + 8 up rows
+constexpr int kORowsPerChunk = kSlotBytes / kORowStride;        // 62 padded o_proj rows (2 heads)
+constexpr int kGUPerChunk = (kSlotBytes / 2) / kRowStride;      // 7 gate rows + 7 up rows (padded)
 constexpr int kDownRowsPerChunk = kSlotBytes / (kInter * 2);    // 5 rows of 6 KB (HF layout)
 
 // Error codes written to Workspace::error[0].
@@ -190,10 +195,10 @@ __host__ __device__ inline Plan make_plan(int cta, int grid, int group_size, int
   return p;
 }
 
-// End of the QKV chunk that starts at row r: at most 16 rows, never crossing
-// the q/k/v matrix boundaries.
+// End of the QKV chunk that starts at row r: at most kQKVRowsPerChunk rows,
+// never crossing the q/k/v matrix boundaries.
 __host__ __device__ inline int qkv_chunk_end(int r, int qb) {
-  int e = r + kRowsPerChunk1024;
+  int e = r + kQKVRowsPerChunk;
   const int bound = r < kQSize ? kQSize : (r < kQSize + kKVSize ? kQSize + kKVSize : kQKVRows);
   if (e > bound) e = bound;
   if (e > qb) e = qb;

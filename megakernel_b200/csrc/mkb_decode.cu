@@ -368,17 +368,18 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         const int r1 = pl.va + part(npre, kLmPreloadLayers, part_i + 1);
         pr.prefetch(p.lm_head + (size_t)r0 * kHidden, static_cast<uint32_t>(r1 - r0) * kHidden * 2u);
       }
-      // A: QKV rows
+      // A: QKV rows, one bulk copy per row into a padded row slot
       for (int r = pl.qa; r < pl.qb;) {
         const int e = qkv_chunk_end(r, pl.qb);
         const __nv_bfloat16* src = r < kQSize ? ldg_ptr(&lw->q_weight) + (size_t)r * kHidden
                                    : r < kQSize + kKVSize
                                        ? ldg_ptr(&lw->k_weight) + (size_t)(r - kQSize) * kHidden
                                        : ldg_ptr(&lw->v_weight) + (size_t)(r - kQSize - kKVSize) * kHidden;
-        const uint32_t bytes = static_cast<uint32_t>(e - r) * kHidden * 2u;
-        const int s = pr.begin(bytes);
+        const int s = pr.begin(static_cast<uint32_t>(e - r) * kHidden * 2u);
         if (s < 0) break;
-        if (pr.lane == 0) pr.copy(s, 0, src, bytes, pr.pol_w);
+        if (pr.lane < e - r)
+          pr.copy(s, static_cast<uint32_t>(pr.lane) * kRowStride, src + (size_t)pr.lane * kHidden, kHidden * 2u,
+                  pr.pol_w);
         pr.end();
         r = e;
       }
@@ -422,8 +423,8 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           const int s = pr.begin(static_cast<uint32_t>(o1 - o0) * 512u);
           if (s < 0) break;
           for (int row = o0 + pr.lane; row < o1; row += 32)
-            pr.copy(s, static_cast<uint32_t>(row - o0) * 512u, wo + (size_t)row * kQSize + pl.h * 2 * kHeadDim, 512u,
-                    pr.pol_w);
+            pr.copy(s, static_cast<uint32_t>(row - o0) * kORowStride, wo + (size_t)row * kQSize + pl.h * 2 * kHeadDim,
+                    512u, pr.pol_w);
           pr.end();
         }
       }
@@ -432,12 +433,14 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       const __nv_bfloat16* wu = ldg_ptr(&lw->up_proj_weight);
       for (int j0 = pl.ja; j0 < pl.jb; j0 += kGUPerChunk) {
         const int j1 = min(pl.jb, j0 + kGUPerChunk);
-        const uint32_t half = static_cast<uint32_t>(j1 - j0) * kHidden * 2u;
-        const int s = pr.begin(2u * half);
+        // gate rows to padded slots in the first half, up rows in the second
+        const int s = pr.begin(2u * static_cast<uint32_t>(j1 - j0) * kHidden * 2u);
         if (s < 0) break;
-        if (pr.lane == 0) {
-          pr.copy(s, 0, wg + (size_t)j0 * kHidden, half, pr.pol_w);
-          pr.copy(s, kSlotBytes / 2, wu + (size_t)j0 * kHidden, half, pr.pol_w);
+        if (pr.lane < 2 * (j1 - j0)) {
+          const int i = pr.lane % (j1 - j0);
+          const bool up = pr.lane >= (j1 - j0);
+          pr.copy(s, (up ? kSlotBytes / 2 : 0) + static_cast<uint32_t>(i) * kRowStride,
+                  (up ? wu : wg) + (size_t)(j0 + i) * kHidden, kHidden * 2u, pr.pol_w);
         }
         pr.end();
       }
@@ -478,6 +481,92 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 }
 
 // ---- consumers -----------------------------------------------------------------
+
+// ---- tensor-core GEMV over padded rows in a ring slot -------------------------
+// Warp w owns the reduction range k in [64w, 64w+64) of a 1024-wide row (four
+// 16-wide MMA k-steps); the 16 warps' partial sums are added through shared
+// memory. The activation x enters as B columns 0 (bf16 hi part) and 1 (bf16
+// remainder x - hi), so D[:,0] + D[:,1] carries ~16 mantissa bits of x.
+//
+// Norm weights for this lane's B-fragment entries (lanes 0-7 only), loaded ahead
+// of the transition that gates the norm.
+__device__ __forceinline__ void load_norm_k(const __nv_bfloat16* w, uint32_t nw2[4][2]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int st = 0; st < 4; ++st) {
+    const int k = 64 * warp + 16 * st + 2 * (lane & 3);
+    if (lane < 8 && w != nullptr) {
+      nw2[st][0] = __ldg(reinterpret_cast<const unsigned int*>(w + k));
+      nw2[st][1] = __ldg(reinterpret_cast<const unsigned int*>(w + k + 8));
+    } else {
+      nw2[st][0] = 0x3f803f80u;  // bf16 1.0 pair
+      nw2[st][1] = 0x3f803f80u;
+    }
+  }
+}
+// B fragments of x = v * rstd * w for this warp's k range (v in shared memory).
+__device__ __forceinline__ void build_bfrag(const float* v, float rstd, const uint32_t nw2[4][2], uint32_t bfr[4][2]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int st = 0; st < 4; ++st) {
+    bfr[st][0] = 0u;
+    bfr[st][1] = 0u;
+    if (lane < 8) {
+      const int k = 64 * warp + 16 * st + 2 * (lane & 3);
+      const float x0 = v[k] * rstd * bf_lo(nw2[st][0]);
+      const float x1 = v[k + 1] * rstd * bf_hi(nw2[st][0]);
+      const float x8 = v[k + 8] * rstd * bf_lo(nw2[st][1]);
+      const float x9 = v[k + 9] * rstd * bf_hi(nw2[st][1]);
+      const uint32_t h0 = pack_bf2(x0, x1), h1 = pack_bf2(x8, x9);
+      if (lane < 4) {
+        bfr[st][0] = h0;
+        bfr[st][1] = h1;
+      } else {
+        bfr[st][0] = pack_bf2(x0 - bf_lo(h0), x1 - bf_hi(h0));
+        bfr[st][1] = pack_bf2(x8 - bf_lo(h1), x9 - bf_hi(h1));
+      }
+    }
+  }
+}
+// One 16-row tile of padded 1024-wide rows at `base` (rows >= nrows read row 0).
+__device__ __forceinline__ void mma_tile_1024(uint32_t base, int nrows, const uint32_t bfr[4][2], float* d) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tr = lane & 15;
+  const uint32_t row = base + (tr < nrows ? tr : 0) * kRowStride + (lane >> 4) * 16 + warp * 128;
+#pragma unroll
+  for (int st = 0; st < 4; ++st) {
+    uint32_t a0, a1, a2, a3;
+    ldsm_x4(row + st * 32, a0, a1, a2, a3);
+    mma_bf16(d, a0, a1, a2, a3, bfr[st][0], bfr[st][1]);
+  }
+}
+// Gate/up tile: tile rows 0-6 are gate rows, 8-14 up rows (second slot half).
+__device__ __forceinline__ void mma_tile_gu(uint32_t base, int nrows, const uint32_t bfr[4][2], float* d) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tr = lane & 15, i = tr & 7;
+  const uint32_t row = base + (tr >= 8 ? kSlotBytes / 2 : 0) + (i < nrows ? i : 0) * kRowStride + (lane >> 4) * 16 +
+                       warp * 128;
+#pragma unroll
+  for (int st = 0; st < 4; ++st) {
+    uint32_t a0, a1, a2, a3;
+    ldsm_x4(row + st * 32, a0, a1, a2, a3);
+    mma_bf16(d, a0, a1, a2, a3, bfr[st][0], bfr[st][1]);
+  }
+}
+// Lanes holding D column pairs write this warp's row partials of tile t.
+__device__ __forceinline__ void stash_tile(float (*xred)[64], int t, const float* d) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if ((lane & 3) == 0) {
+    xred[warp][t * 16 + (lane >> 2)] = d[0] + d[1];
+    xred[warp][t * 16 + (lane >> 2) + 8] = d[2] + d[3];
+  }
+}
+__device__ __forceinline__ float sum_warps(float (*xred)[64], int idx) {
+  float v = 0.f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) v += xred[w][idx];
+  return v;
+}
 
 // Wait for `cnt` consecutive chunks from ring position n (all already issued by
 // the producer); their slot addresses go to sa[].
@@ -607,9 +696,10 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 
     for (int l = lb; l < le; ++l) {
       const LayerWeights* lw = p.layers + l;
-      uint4 nwv[4];
       // ================= A: RMSNorm + QKV rows (megakernel.cu:704-739, 633-701) ===
-      load_norm_w(ldg_ptr(&lw->norm_weight), nwv);
+      uint32_t nw2[4][2], bfr[4][2];
+      float(*xred)[64] = reinterpret_cast<float(*)[64]>(&sm.u.att[0][0][0]);
+      load_norm_k(ldg_ptr(&lw->norm_weight), nw2);
       if (l > lb) {
         transition_wait(c, tr, &ws->sync[l - 1][fused ? 2 : 3][0], tgtG, l, kStA, t);
         if (fused) {
@@ -633,10 +723,10 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       {
         const float tot = block_sumsq(r0, r1, sm.red, flip);
         tr.mark(kTrMark, kSubAInput, l, t);
-        xr_from(sm.r, rsqrtf(tot * (1.0f / kHidden) + kEps), nwv, xr);
+        build_bfrag(sm.r, rsqrtf(tot * (1.0f / kHidden) + kEps), nw2, bfr);
       }
       tr.mark(kTrMark, kSubANorm, l, t);
-      // rows of up to three chunks per pass, reductions interleaved
+      // QKV rows: up to three padded chunks (one 16-row MMA tile each) per pass
       for (int r = pl.qa; r < pl.qb;) {
         const int ra0 = r, ea0 = qkv_chunk_end(ra0, pl.qb);
         const int ra1 = ea0, ea1 = ra1 < pl.qb ? qkv_chunk_end(ra1, pl.qb) : ra1;
@@ -645,16 +735,21 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         r = ea2;
         uint32_t sa[3];
         ring_wait_all(c, n, na, sa, l, 0, t, &tr);
-        float v0 = ra0 + warp < ea0 ? dot_row1024(sa[0] + warp * 2048, xr, lane) : 0.f;
-        float v1 = ra1 + warp < ea1 ? dot_row1024(sa[1] + warp * 2048, xr, lane) : 0.f;
-        float v2 = ra2 + warp < ea2 ? dot_row1024(sa[2] + warp * 2048, xr, lane) : 0.f;
-        warp_sum3(v0, v1, v2);
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f}, d2[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_tile_1024(sa[0], ea0 - ra0, bfr, d0);
+        if (na > 1) mma_tile_1024(sa[1], ea1 - ra1, bfr, d1);
+        if (na > 2) mma_tile_1024(sa[2], ea2 - ra2, bfr, d2);
         ring_done_all(c, n, na);
-        if (lane < 3 && !(t == 0 && l == lb && c.cta == p.withhold_cta)) {
-          const int row = warp + (lane == 0 ? ra0 : (lane == 1 ? ra1 : ra2));
-          const int end = lane == 0 ? ea0 : (lane == 1 ? ea1 : ea2);
-          const float val = lane == 0 ? v0 : (lane == 1 ? v1 : v2);
-          if (row < end) {
+        stash_tile(xred, 0, d0);
+        stash_tile(xred, 1, d1);
+        stash_tile(xred, 2, d2);
+        consumer_sync(kConsumerThreads);
+        if (tid < 48 && !(t == 0 && l == lb && c.cta == p.withhold_cta)) {
+          const int i = tid >> 4;
+          const int row = (i == 0 ? ra0 : (i == 1 ? ra1 : ra2)) + (tid & 15);
+          const int end = i == 0 ? ea0 : (i == 1 ? ea1 : ea2);
+          if ((tid & 15) < 15 && row < end) {
+            const float val = sum_warps(xred, tid);
             st_tagged(&ws->qkv_tagged[l][row], val, tag);
             float* dst = row < kQSize ? p.q_out + row
                          : row < kQSize + kKVSize ? p.k_out + (row - kQSize)
@@ -662,6 +757,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             *dst = val;
           }
         }
+        consumer_sync(kConsumerThreads);
       }
       tr.mark(kTrPublish, kStA, l, t);
 
@@ -903,36 +999,42 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         // o_proj partial of this KV head's two Q heads (megakernel.cu:191-225)
         tr.mark(kTrMark, kSubBCComb, l, t);
         {
-          float xo[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) xo[e] = sm.attn[lane * 8 + e];
+          // K = 256 (two heads x 128): warp w owns the MMA k-step [16w, 16w+16);
+          // rows in padded 528-byte slots, four 16-row tiles per chunk.
+          uint32_t ob0 = 0u, ob1 = 0u;
+          if (lane < 8) {
+            const int k = 16 * warp + 2 * (lane & 3);
+            const float x0 = sm.attn[k], x1 = sm.attn[k + 1], x8 = sm.attn[k + 8], x9 = sm.attn[k + 9];
+            const uint32_t h0 = pack_bf2(x0, x1), h1 = pack_bf2(x8, x9);
+            ob0 = lane < 4 ? h0 : pack_bf2(x0 - bf_lo(h0), x1 - bf_hi(h0));
+            ob1 = lane < 4 ? h1 : pack_bf2(x8 - bf_lo(h1), x9 - bf_hi(h1));
+          }
           for (int o0 = pl.oa; o0 < pl.ob; o0 += kORowsPerChunk) {
-            const int o1 = min(pl.ob, o0 + kORowsPerChunk);
+            const int nrows = min(pl.ob, o0 + kORowsPerChunk) - o0;
             const uint32_t sa = ring_wait(c, n, l, 3, t, &tr);
-            float v[4];
+            float d[4][4] = {};
+            const int tr16 = lane & 15;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int row = o0 + warp * 4 + i;
-              v[i] = row < o1 ? dot8(lds128(sa + (row - o0) * 512 + lane * 16), xo) : 0.f;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
-            }
-            if (lane < 4) {
-              const int row = o0 + warp * 4 + lane;
-              const float val = lane == 0 ? v[0] : lane == 1 ? v[1] : lane == 2 ? v[2] : v[3];
-              if (row < o1) red_add_f32(&ws->acc_mid[l][row], val);
+            for (int tt = 0; tt < 4; ++tt) {
+              const int rr = tt * 16 + tr16;
+              const uint32_t row = sa + (rr < nrows ? rr : 0) * kORowStride + (lane >> 4) * 16 + warp * 32;
+              uint32_t a0, a1, a2, a3;
+              ldsm_x4(row, a0, a1, a2, a3);
+              mma_bf16(d[tt], a0, a1, a2, a3, ob0, ob1);
             }
             ring_done(c, n);
+#pragma unroll
+            for (int tt = 0; tt < 4; ++tt) stash_tile(xred, tt, d[tt]);
+            consumer_sync(kConsumerThreads);
+            if (tid < nrows) red_add_f32(&ws->acc_mid[l][o0 + tid], sum_warps(xred, tid));
+            consumer_sync(kConsumerThreads);
           }
         }
         transition_publish(tr, &ws->sync[l][1][0], l, kStBC, t);
       }
 
       // ================= DE: post norm, SwiGLU rows, down partial ===============
-      load_norm_w(ldg_ptr(&lw->post_attn_norm_weight), nwv);
+      load_norm_k(ldg_ptr(&lw->post_attn_norm_weight), nw2);
       transition_wait(c, tr, &ws->sync[l][1][0], tgtBC, l, kStDE, t);
       {
         const float m0 = sm.r[tid] + __ldcg(&ws->acc_mid[l][tid]);
@@ -940,30 +1042,32 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         sm.rmid[tid] = m0;
         sm.rmid[tid + kConsumerThreads] = m1;
         const float tot = block_sumsq(m0, m1, sm.red, flip);
-        xr_from(sm.rmid, rsqrtf(tot * (1.0f / kHidden) + kEps), nwv, xr);
+        build_bfrag(sm.rmid, rsqrtf(tot * (1.0f / kHidden) + kEps), nw2, bfr);
       }
       tr.mark(kTrMark, kSubDENorm, l, t);
       const int nj = pl.jb - pl.ja;
-      // gate rows (warps 0-7) and up rows (warps 8-15), three chunks per pass
-      // (megakernel.cu:100-142)
+      // gate and up rows (megakernel.cu:100-142): each padded chunk holds 7 of
+      // each and is one 16-row MMA tile; up to three chunks per pass
       for (int jb0 = 0; jb0 < nj; jb0 += 3 * kGUPerChunk) {
         const int ng = min(3, (nj - jb0 + kGUPerChunk - 1) / kGUPerChunk);
         uint32_t sa[3];
         ring_wait_all(c, n, ng, sa, l, 4, t, &tr);
-        const uint32_t half = warp >= 8 ? kSlotBytes / 2 : 0;
-        const int j0 = jb0 + (warp & 7);
-        float v0 = j0 < nj ? dot_row1024(sa[0] + half + (warp & 7) * 2048, xr, lane) : 0.f;
-        float v1 = (ng > 1 && j0 + kGUPerChunk < nj) ? dot_row1024(sa[1] + half + (warp & 7) * 2048, xr, lane) : 0.f;
-        float v2 = (ng > 2 && j0 + 2 * kGUPerChunk < nj) ? dot_row1024(sa[2] + half + (warp & 7) * 2048, xr, lane)
-                                                           : 0.f;
-        warp_sum3(v0, v1, v2);
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f}, d2[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_tile_gu(sa[0], min(kGUPerChunk, nj - jb0), bfr, d0);
+        if (ng > 1) mma_tile_gu(sa[1], min(kGUPerChunk, nj - jb0 - kGUPerChunk), bfr, d1);
+        if (ng > 2) mma_tile_gu(sa[2], min(kGUPerChunk, nj - jb0 - 2 * kGUPerChunk), bfr, d2);
         ring_done_all(c, n, ng);
-        if (lane < 3) {
-          const int jj = j0 + lane * kGUPerChunk;
-          if (jj < nj) sm.gu[warp >> 3][jj] = lane == 0 ? v0 : (lane == 1 ? v1 : v2);
+        stash_tile(xred, 0, d0);
+        stash_tile(xred, 1, d1);
+        stash_tile(xred, 2, d2);
+        consumer_sync(kConsumerThreads);
+        if (tid < 16 * ng) {
+          const int i = (tid & 15) & 7;
+          const int j = jb0 + (tid >> 4) * kGUPerChunk + i;
+          if (i < kGUPerChunk && j < nj) sm.gu[(tid & 15) >> 3][j] = sum_warps(xred, tid);
         }
+        consumer_sync(kConsumerThreads);
       }
-      consumer_sync(kConsumerThreads);
       tr.mark(kTrMark, kSubDEGU, l, t);
       if (tid < nj) {
         const float g = sm.gu[0][tid], u = sm.gu[1][tid];
