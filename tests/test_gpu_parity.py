@@ -5,7 +5,8 @@ Every call goes through the C ABI of libmkb200.so (``mkb_decode``,
 
 Tolerances:
 * stage level (same numerics as the restatement: BF16 cache, FP32 activations):
-  max-abs 2e-3 on the layer output, 1 BF16 ulp on the appended K/V;
+  raw QKV within 1e-4 of float64, max-abs 2e-3 on the layer output, 2 BF16 ulp
+  on the appended K/V;
 * model level, against HF Qwen3 FP32 on the CPU (the BASELINE oracle): per-step
   logits max-abs <= 2e-2 and cosine > 0.999, identical greedy tokens wherever
   HF's top-2 margin exceeds 0.05;
@@ -147,16 +148,26 @@ def test_single_layer_config1(fused, cuda_device):
     # restatement with identical numerics (BF16 cache, FP32 RoPE tables)
     kc, vc = k.clone(), v.clone()
     o = R.decode_layer(w1.layers[0], c1["hidden"].float(), 0, pos, pos + 1, kc, vc, cos, sin)
-    assert (q.cpu() - o["q"]).abs().max().item() < 1e-3
-    assert (kk.cpu() - o["k"]).abs().max().item() < 1e-3
-    assert (vv.cpu() - o["v"]).abs().max().item() < 1e-3
+    # raw QKV GEMV outputs against float64
+    x = R.rmsnorm(c1["hidden"].float(), w1.layers[0]["input_norm"]).double()
+    for name, got, wname in (("q", q, "q"), ("k", kk, "k"), ("v", vv, "v")):
+        ref64 = (w1.layers[0][wname].double() @ x).float()
+        err = (got.cpu() - ref64).abs().max().item()
+        assert err < 1e-4, f"{name}: max |err| {err:.3e} vs float64"
+    err_q = (q.cpu() - o["q"]).abs().max().item()
+    assert err_q < 1e-4, err_q
     got_k = kg[0, :, pos].float().cpu()
     got_v = vg[0, :, pos].float().cpu()
-    ulp = 2.0 ** -7
-    assert ((got_k - kc[0, :, pos].float()).abs() <= ulp * kc[0, :, pos].float().abs() + 1e-6).all()
-    assert ((got_v - vc[0, :, pos].float()).abs() <= ulp * vc[0, :, pos].float().abs() + 1e-6).all()
+    # both sides round an FP32 value to BF16; last-bit differences in the FP32
+    # sums may move a rounding by one BF16 ulp (2^-7..2^-8 relative)
+    ulp = 2.0 ** -6
+    dk = (got_k - kc[0, :, pos].float()).abs()
+    dv = (got_v - vc[0, :, pos].float()).abs()
+    assert (dk <= ulp * kc[0, :, pos].float().abs() + 1e-6).all(), f"k row: max {dk.max().item():.3e}"
+    assert (dv <= ulp * vc[0, :, pos].float().abs() + 1e-6).all(), f"v row: max {dv.max().item():.3e}"
     assert torch.equal(kg[0, :, :pos].cpu(), k[0, :, :pos])      # the prefix is untouched
-    assert (r_out.cpu() - o["r_out"]).abs().max().item() < 2e-3
+    err_r = (r_out.cpu() - o["r_out"]).abs().max().item()
+    assert err_r < 2e-3, err_r
     # against HF FP32 (new K/V kept in FP32 there)
     assert (r_out.cpu() - torch.from_numpy(g["out"])).abs().max().item() < 2e-2
 
