@@ -6,7 +6,7 @@ Every call goes through the C ABI of libmkb200.so (``mkb_decode``,
 Tolerances:
 * stage level (same numerics as the restatement: BF16 cache, FP32 activations):
   raw QKV within 1e-4 of float64, max-abs 2e-3 on the layer output, 2 BF16 ulp
-  on the appended K/V;
+  + 1e-4 on the appended K/V;
 * model level, against HF Qwen3 FP32 on the CPU (the BASELINE oracle): per-step
   logits max-abs <= 2e-2 and cosine > 0.999, identical greedy tokens wherever
   HF's top-2 margin exceeds 0.05;
@@ -158,13 +158,14 @@ def test_single_layer_config1(fused, cuda_device):
     assert err_q < 1e-4, err_q
     got_k = kg[0, :, pos].float().cpu()
     got_v = vg[0, :, pos].float().cpu()
-    # both sides round an FP32 value to BF16; last-bit differences in the FP32
-    # sums may move a rounding by one BF16 ulp (2^-7..2^-8 relative)
-    ulp = 2.0 ** -6
+    # both sides round an FP32 value to BF16: the FP32 inputs agree to ~1e-4
+    # absolute (O(1) values after the head norm), so allow that plus two BF16 ulps
     dk = (got_k - kc[0, :, pos].float()).abs()
     dv = (got_v - vc[0, :, pos].float()).abs()
-    assert (dk <= ulp * kc[0, :, pos].float().abs() + 1e-6).all(), f"k row: max {dk.max().item():.3e}"
-    assert (dv <= ulp * vc[0, :, pos].float().abs() + 1e-6).all(), f"v row: max {dv.max().item():.3e}"
+    bk = 2.0 ** -6 * kc[0, :, pos].float().abs() + 1e-4
+    bv = 2.0 ** -6 * vc[0, :, pos].float().abs() + 1e-4
+    assert (dk <= bk).all(), f"k row: max {dk.max().item():.3e}, worst excess {(dk - bk).max().item():.3e}"
+    assert (dv <= bv).all(), f"v row: max {dv.max().item():.3e}, worst excess {(dv - bv).max().item():.3e}"
     assert torch.equal(kg[0, :, :pos].cpu(), k[0, :, :pos])      # the prefix is untouched
     err_r = (r_out.cpu() - o["r_out"]).abs().max().item()
     assert err_r < 2e-3, err_r
