@@ -56,6 +56,10 @@ struct __align__(128) Smem {
   float red[32];
   float best_v[kConsumerWarps];
   int best_i[kConsumerWarps];
+  // Copy of the device LayerWeights table (+ the transposed down pointer) in
+  // shared memory: grid-transition acquires invalidate L1, and these pointers
+  // are needed on the critical path of every stage.
+  const __nv_bfloat16* lwp[kMaxLayers][12];
   int token;
   int is_last;
   int abort;
@@ -215,6 +219,12 @@ __device__ __forceinline__ float rope_at(const void* table, int fp32, size_t idx
               : __bfloat162float(static_cast<const __nv_bfloat16*>(table)[idx]);
 }
 
+// Field indices of the shared-memory layer table (LayerWeights order + down_t).
+enum LayerField : int {
+  kWNorm = 0, kWQ, kWK, kWV, kWQNorm, kWKNorm, kWO, kWPost, kWGate, kWUp, kWDown, kWDownT
+};
+__device__ __forceinline__ const __nv_bfloat16* lwt(const Ctl& c, int l, int f) { return c.sm->lwp[l][f]; }
+
 // Pointer field of a device-resident table, read through the read-only path.
 template <typename T>
 __device__ __forceinline__ const T* ldg_ptr(const T* const* field) {
@@ -306,15 +316,14 @@ struct Producer {
 // ring, so HBM keeps streaming while the consumers wait at grid transitions and
 // the ring refills from L2.
 __device__ void prefetch_layer(Producer& pr, const DecodeParams& p, const Plan& pl, int l, int cl, int splits) {
-  const LayerWeights* lw = p.layers + l;
   if (pr.lane == 0) {
     for (int r = pl.qa; r < pl.qb;) {
       int e = r < kQSize ? kQSize : (r < kQSize + kKVSize ? kQSize + kKVSize : kQKVRows);
       if (e > pl.qb) e = pl.qb;
-      const __nv_bfloat16* src = r < kQSize ? ldg_ptr(&lw->q_weight) + (size_t)r * kHidden
+      const __nv_bfloat16* src = r < kQSize ? lwt(pr.c, l, kWQ) + (size_t)r * kHidden
                                  : r < kQSize + kKVSize
-                                     ? ldg_ptr(&lw->k_weight) + (size_t)(r - kQSize) * kHidden
-                                     : ldg_ptr(&lw->v_weight) + (size_t)(r - kQSize - kKVSize) * kHidden;
+                                     ? lwt(pr.c, l, kWK) + (size_t)(r - kQSize) * kHidden
+                                     : lwt(pr.c, l, kWV) + (size_t)(r - kQSize - kKVSize) * kHidden;
       pr.prefetch(src, static_cast<uint32_t>(e - r) * kHidden * 2u);
       r = e;
     }
@@ -326,17 +335,17 @@ __device__ void prefetch_layer(Producer& pr, const DecodeParams& p, const Plan& 
       pr.prefetch(p.v_cache + head_off + (size_t)ka * kHeadDim, static_cast<uint32_t>(kb - ka) * kHeadDim * 2u);
     }
     const uint32_t gu = static_cast<uint32_t>(pl.jb - pl.ja) * kHidden * 2u;
-    pr.prefetch(ldg_ptr(&lw->gate_proj_weight) + (size_t)pl.ja * kHidden, gu);
-    pr.prefetch(ldg_ptr(&lw->up_proj_weight) + (size_t)pl.ja * kHidden, gu);
+    pr.prefetch(lwt(pr.c, l, kWGate) + (size_t)pl.ja * kHidden, gu);
+    pr.prefetch(lwt(pr.c, l, kWUp) + (size_t)pl.ja * kHidden, gu);
     if (p.down_t != nullptr) {
-      pr.prefetch(ldg_ptr(p.down_t + l) + (size_t)pl.ja * kHidden, gu);
+      pr.prefetch(lwt(pr.c, l, kWDownT) + (size_t)pl.ja * kHidden, gu);
     } else {
-      pr.prefetch(ldg_ptr(&lw->down_proj_weight) + (size_t)pl.da * kInter,
+      pr.prefetch(lwt(pr.c, l, kWDown) + (size_t)pl.da * kInter,
                   static_cast<uint32_t>(pl.db - pl.da) * kInter * 2u);
     }
   }
   if (pl.in_bc) {
-    const __nv_bfloat16* wo = ldg_ptr(&lw->o_proj_weight);
+    const __nv_bfloat16* wo = lwt(pr.c, l, kWO);
     for (int row = pl.oa + pr.lane; row < pl.ob; row += 32)
       pr.prefetch(wo + (size_t)row * kQSize + pl.h * 2 * kHeadDim, 512u);
   }
@@ -356,7 +365,6 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     const int pos = pos0 + t;
     const int cl = cl0 + t;
     for (int l = p.layer_begin; l < p.layer_end && !pr.stop; ++l) {
-      const LayerWeights* lw = p.layers + l;
       // L2 prefetch one layer ahead (the next token's first layer after the last)
       if (l == p.layer_begin && t == 0) prefetch_layer(pr, p, pl, l, cl, splits);
       if (l + 1 < p.layer_end) prefetch_layer(pr, p, pl, l + 1, cl, splits);
@@ -371,10 +379,10 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       // A: QKV rows, one bulk copy per row into a padded row slot
       for (int r = pl.qa; r < pl.qb;) {
         const int e = qkv_chunk_end(r, pl.qb);
-        const __nv_bfloat16* src = r < kQSize ? ldg_ptr(&lw->q_weight) + (size_t)r * kHidden
+        const __nv_bfloat16* src = r < kQSize ? lwt(pr.c, l, kWQ) + (size_t)r * kHidden
                                    : r < kQSize + kKVSize
-                                       ? ldg_ptr(&lw->k_weight) + (size_t)(r - kQSize) * kHidden
-                                       : ldg_ptr(&lw->v_weight) + (size_t)(r - kQSize - kKVSize) * kHidden;
+                                       ? lwt(pr.c, l, kWK) + (size_t)(r - kQSize) * kHidden
+                                       : lwt(pr.c, l, kWV) + (size_t)(r - kQSize - kKVSize) * kHidden;
         const int s = pr.begin(static_cast<uint32_t>(e - r) * kHidden * 2u);
         if (s < 0) break;
         if (pr.lane < e - r)
@@ -417,7 +425,7 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           }
           pr.end();
         }
-        const __nv_bfloat16* wo = ldg_ptr(&lw->o_proj_weight);
+        const __nv_bfloat16* wo = lwt(pr.c, l, kWO);
         for (int o0 = pl.oa; o0 < pl.ob; o0 += kORowsPerChunk) {
           const int o1 = min(pl.ob, o0 + kORowsPerChunk);
           const int s = pr.begin(static_cast<uint32_t>(o1 - o0) * 512u);
@@ -429,8 +437,8 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         }
       }
       // DE / D: gate and up rows
-      const __nv_bfloat16* wg = ldg_ptr(&lw->gate_proj_weight);
-      const __nv_bfloat16* wu = ldg_ptr(&lw->up_proj_weight);
+      const __nv_bfloat16* wg = lwt(pr.c, l, kWGate);
+      const __nv_bfloat16* wu = lwt(pr.c, l, kWUp);
       for (int j0 = pl.ja; j0 < pl.jb; j0 += kGUPerChunk) {
         const int j1 = min(pl.jb, j0 + kGUPerChunk);
         // gate rows to padded slots in the first half, up rows in the second
@@ -445,7 +453,7 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         pr.end();
       }
       if (fused) {
-        const __nv_bfloat16* wdt = ldg_ptr(p.down_t + l);
+        const __nv_bfloat16* wdt = lwt(pr.c, l, kWDownT);
         for (int j0 = pl.ja; j0 < pl.jb; j0 += kRowsPerChunk1024) {
           const int j1 = min(pl.jb, j0 + kRowsPerChunk1024);
           const uint32_t bytes = static_cast<uint32_t>(j1 - j0) * kHidden * 2u;
@@ -455,7 +463,7 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           pr.end();
         }
       } else {
-        const __nv_bfloat16* wd = ldg_ptr(&lw->down_proj_weight);
+        const __nv_bfloat16* wd = lwt(pr.c, l, kWDown);
         for (int d0 = pl.da; d0 < pl.db; d0 += kDownRowsPerChunk) {
           const int d1 = min(pl.db, d0 + kDownRowsPerChunk);
           const uint32_t bytes = static_cast<uint32_t>(d1 - d0) * kInter * 2u;
@@ -694,12 +702,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     float r1 = p.input_residual ? __ldcg(p.input_residual + tid + kConsumerThreads)
                                 : __bfloat162float(p.embed[(size_t)token * kHidden + tid + kConsumerThreads]);
 
+    uint32_t nwA[4][2], nwD[4][2];
+    if (le > lb) load_norm_k(lwt(c, lb, kWNorm), nwA);
     for (int l = lb; l < le; ++l) {
-      const LayerWeights* lw = p.layers + l;
       // ================= A: RMSNorm + QKV rows (megakernel.cu:704-739, 633-701) ===
-      uint32_t nw2[4][2], bfr[4][2];
+      uint32_t bfr[4][2];
       float(*xred)[64] = reinterpret_cast<float(*)[64]>(&sm.u.att[0][0][0]);
-      load_norm_k(ldg_ptr(&lw->norm_weight), nw2);
       if (l > lb) {
         transition_wait(c, tr, &ws->sync[l - 1][fused ? 2 : 3][0], tgtG, l, kStA, t);
         if (fused) {
@@ -723,7 +731,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       {
         const float tot = block_sumsq(r0, r1, sm.red, flip);
         tr.mark(kTrMark, kSubAInput, l, t);
-        build_bfrag(sm.r, rsqrtf(tot * (1.0f / kHidden) + kEps), nw2, bfr);
+        build_bfrag(sm.r, rsqrtf(tot * (1.0f / kHidden) + kEps), nwA, bfr);
       }
       tr.mark(kTrMark, kSubANorm, l, t);
       // QKV rows: up to three padded chunks (one 16-row MMA tile each) per pass
@@ -760,6 +768,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         consumer_sync(kConsumerThreads);
       }
       tr.mark(kTrPublish, kStA, l, t);
+      load_norm_k(lwt(c, l, kWPost), nwD);  // post-attention norm, one stage ahead
 
       // ================= BC: head norm + RoPE + KV append, attention, o_proj =====
       if (pl.in_bc) {
@@ -769,7 +778,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f, cs0 = 0.f, sn0 = 0.f, cs1 = 0.f, sn1 = 0.f;
         const int d0 = 2 * lane;
         if (warp < 3) {
-          const __nv_bfloat16* nw = warp < 2 ? ldg_ptr(&lw->q_norm_weight) : ldg_ptr(&lw->k_norm_weight);
+          const __nv_bfloat16* nw = lwt(c, l, warp < 2 ? kWQNorm : kWKNorm);
           w0 = __bfloat162float(nw[d0]);
           w1 = __bfloat162float(nw[d0 + 1]);
           w2 = __bfloat162float(nw[d0 + 64]);
@@ -1034,7 +1043,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       }
 
       // ================= DE: post norm, SwiGLU rows, down partial ===============
-      load_norm_k(ldg_ptr(&lw->post_attn_norm_weight), nw2);
+      // the next layer's input-norm weights, one stage ahead of their use
+      if (l + 1 < le) load_norm_k(lwt(c, l + 1, kWNorm), nwA);
       transition_wait(c, tr, &ws->sync[l][1][0], tgtBC, l, kStDE, t);
       {
         const float m0 = sm.r[tid] + __ldcg(&ws->acc_mid[l][tid]);
@@ -1042,7 +1052,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         sm.rmid[tid] = m0;
         sm.rmid[tid + kConsumerThreads] = m1;
         const float tot = block_sumsq(m0, m1, sm.red, flip);
-        build_bfrag(sm.rmid, rsqrtf(tot * (1.0f / kHidden) + kEps), nw2, bfr);
+        build_bfrag(sm.rmid, rsqrtf(tot * (1.0f / kHidden) + kEps), nwD, bfr);
       }
       tr.mark(kTrMark, kSubDENorm, l, t);
       const int nj = pl.jb - pl.ja;
@@ -1289,6 +1299,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     cl = pos + 1;
   }
 
+  for (int i = threadIdx.x; i < kMaxLayers * 12; i += blockDim.x) {
+    const int l = i / 12, f = i % 12;
+    const __nv_bfloat16* v = nullptr;
+    if (l >= p.layer_begin && l < p.layer_end) {
+      if (f < 11) v = reinterpret_cast<const __nv_bfloat16* const*>(p.layers + l)[f];
+      else if (p.down_t != nullptr) v = p.down_t[l];
+    }
+    sm->lwp[l][f] = v;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(&sm->full[s], 1);
