@@ -40,6 +40,24 @@ cudaError_t launch_decode_kernel(int token_id, const void* embed_weight, const v
                                  void* g_logits, void* g_q, void* g_k, void* g_v, int position, int cache_len,
                                  int max_seq_len, cudaStream_t stream);
 
+/* No counterpart in the reference. launch_decode_kernel with the same
+ * arguments and results, for callers that must not allocate device memory at
+ * any call: the synchronisation workspace lives in a file-scope device array of
+ * at most 2 MiB per device (a build whose workspace is larger returns
+ * cudaErrorInvalidValue). The first call on a device looks up that array's
+ * address (cudaGetSymbolAddress) and caches it; make that first call before
+ * any stream capture. Every call clears the workspace bytes with
+ * cudaMemsetAsync on `stream`, then launches. The array is shared by all calls
+ * on the device: calls that overlap in time race on it. */
+cudaError_t launch_decode_kernel_noalloc(int token_id, const void* embed_weight, const void* lm_head_weight,
+                                         const void* final_norm_weight, const void* layer_weights,
+                                         const void* cos_table, const void* sin_table, void* k_cache,
+                                         void* v_cache, void* hidden_buffer, void* g_residual,
+                                         void* g_activations, void* g_attn_output, void* g_normalized,
+                                         void* g_mlp_intermediate, void* g_logits, void* g_q, void* g_k,
+                                         void* g_v, int position, int cache_len, int max_seq_len,
+                                         cudaStream_t stream);
+
 /* ---- explicit-argument launch ----------------------------------------------
  * Generalises the reference launcher (megakernel.cu:898-994): layer range,
  * input residual instead of the embedding gather, optional LM head, several

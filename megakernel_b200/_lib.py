@@ -95,6 +95,10 @@ SIGNATURES = [
      [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
       c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
       c_void_p, c_int, c_int, c_int, c_void_p]),
+    ("launch_decode_kernel_noalloc", c_int,
+     [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+      c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+      c_void_p, c_int, c_int, c_int, c_void_p]),
     ("mkb_decode_args_init", None, [POINTER(DecodeArgs)]),
     ("mkb_decode", c_int, [POINTER(DecodeArgs), c_void_p]),
     ("mkb_workspace_bytes", c_size_t, []),

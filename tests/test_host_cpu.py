@@ -18,13 +18,14 @@ def declared_functions():
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
     names = re.findall(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(", src)
     skip = {"if", "for", "while", "sizeof", "return", "defined"}
-    return sorted({n for n in names if n not in skip and (n.startswith("mkb_") or n == "launch_decode_kernel")})
+    return sorted({n for n in names if n not in skip and (n.startswith("mkb_") or n.startswith("launch_decode_kernel"))})
 
 
 def test_library_exports_every_declared_symbol():
     lib = _lib.load()
     names = declared_functions()
     assert "launch_decode_kernel" in names and "mkb_engine_step" in names
+    assert "launch_decode_kernel_noalloc" in names
     for n in names:
         assert hasattr(lib, n), n
     assert {s[0] for s in _lib.SIGNATURES} == set(names)
