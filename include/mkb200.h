@@ -43,7 +43,7 @@ cudaError_t launch_decode_kernel(int token_id, const void* embed_weight, const v
 /* No counterpart in the reference. launch_decode_kernel with the same
  * arguments and results, for callers that must not allocate device memory at
  * any call: the synchronisation workspace lives in a file-scope device array of
- * at most 2 MiB per device (a build whose workspace is larger returns
+ * at most 4 MiB per device (a build whose workspace is larger returns
  * cudaErrorInvalidValue). The first call on a device looks up that array's
  * address (cudaGetSymbolAddress) and caches it; make that first call before
  * any stream capture. Every call clears the workspace bytes with

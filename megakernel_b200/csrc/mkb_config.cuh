@@ -3,6 +3,7 @@
 // the host-side schedule query used by the CPU tests.
 #pragma once
 
+#include <cstddef>
 #include <cstdint>
 #include <cuda_bf16.h>
 
@@ -21,8 +22,9 @@ constexpr int kVocab = 151936;
 constexpr int kMaxLayers = 28;
 constexpr float kEps = 1e-6f;
 
-// Execution shape: one CTA per SM, 16 consumer warps + 1 producer warp.
-constexpr int kConsumerWarps = 16;
+// Execution shape: one CTA per SM, 8 consumer warps + 1 producer warp (at most
+// 3 warps per scheduler, so up to 168 registers per thread).
+constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 // Shared-memory weight ring: kSlots slots of kSlotBytes, filled by cp.async.bulk.
@@ -50,7 +52,28 @@ enum ErrorCode : uint32_t {
   kErrTimeoutRing = 2,         // a shared-memory ring slot never filled / emptied
   kErrTimeoutToken = 3,        // the greedy token broadcast never arrived
   kErrBadArgs = 4,             // position / cache_len / token out of range
+  kErrRange = 5,               // a partial sum outside the counted fixed-point range
 };
+
+// Counted fixed-point accumulators. A grid-wide sum of per-CTA partials is kept
+// in one 64-bit word per element: bits 56-63 count the contributions, bits
+// 0-55 hold sum(round(x * 2^28) + 2^47). Every contribution is one
+// red.add.u64, so a reader that sees the expected count also sees the complete
+// sum -- no counter, no fence -- and integer addition makes the sum independent
+// of arrival order. |x| < 2^19 per contribution; up to 255 contributions (the
+// biased field of 255 terms stays below 2^56).
+constexpr int kAccShift = 28;
+constexpr uint64_t kAccBias = 1ull << 47;
+constexpr uint64_t kAccOne = 1ull << 56;
+constexpr uint64_t kAccLowMask = kAccOne - 1ull;
+// The down-projection partials of the kCluster CTAs of a thread-block cluster
+// are first summed in distributed shared memory (CTA rank r of the cluster owns
+// elements [1024 r / kCluster, 1024 (r + 1) / kCluster)); the owners add the
+// cluster sums into acc_down,
+// spread over kDownCopies copies (cluster k adds into copy k % kDownCopies) to
+// cut same-address atomic contention; readers add the copies.
+constexpr int kCluster = 2;  // 74 co-resident pairs use all 148 SMs
+constexpr int kDownCopies = 2;
 
 // Flags in DecodeParams::flags.
 enum : int {
@@ -94,8 +117,13 @@ struct alignas(128) Workspace {
   uint32_t tok_flag[32];                     // greedy token broadcast (multi-token launches)
   uint32_t error[32];                        // [0] code, [1] cta, [2] layer, [3] stage, [4] token
   uint32_t tag_base[32];                     // [0]: tag of the last token decoded (tagged words)
-  float acc_mid[kMaxLayers][kHidden];        // sum of o_proj partials per layer
-  float acc_down[kMaxLayers][kHidden];       // sum of down-proj partials per layer
+  // Per-layer sums as counted fixed-point words (see kAccShift): o_proj
+  // partials (one per KV head) and down-proj partials (one per CTA).
+  uint64_t acc_mid[kMaxLayers][kHidden];
+  uint64_t acc_down[kMaxLayers][kDownCopies][kHidden];
+  // K/V append of (layer, KV head) published for a later token of the same
+  // launch (two adds per token: the K and the V writer).
+  uint32_t kv_ready[kMaxLayers][kNKV][32];
   float att_part[kNKV][kMaxSplits][2][kHeadDim + 4];  // split attention (m, l, o[128])
   float qkv[kQKVRows];
   // Raw QKV outputs of every layer as tagged words (value | tag << 32); the tag
@@ -106,6 +134,11 @@ struct alignas(128) Workspace {
   float cand_val[kMaxGrid];
   int cand_idx[kMaxGrid];
 };
+
+// Fields read or cleared with 16-byte vector accesses.
+static_assert(offsetof(Workspace, acc_mid) % 16 == 0 && offsetof(Workspace, acc_down) % 16 == 0 &&
+                  offsetof(Workspace, resid) % 16 == 0 && offsetof(Workspace, qkv_tagged) % 16 == 0,
+              "workspace vector fields must be 16-byte aligned");
 
 // Launch parameters (passed by value; all pointers are device pointers).
 struct DecodeParams {
@@ -146,9 +179,14 @@ struct DecodeParams {
 };
 
 // Trace record: (code << 48) | (globaltimer ns & 0xffffffffffff). Row cta is
-// written by consumer thread 0 of that CTA, row grid + cta by its producer lane.
+// written by consumer thread 0 of that CTA (rows grid..2*grid-1 are reserved).
 // code = kind | stage << 2 | layer << 7 | token << 12.
 enum TraceKind : uint32_t { kTrWaitBegin = 0, kTrWaitEnd = 1, kTrPublish = 2, kTrMark = 3 };
+// Trace window: consumer stamps staged in shared memory for these layers.
+constexpr int kTraceLayerLo = 8;
+constexpr int kTraceLayers = 8;
+constexpr int kTraceSmem = 192;
+
 enum TraceStage : uint32_t {
   kStA = 0, kStBC = 1, kStDE = 2, kStE = 3, kStLM = 4, kStSplit = 5, kStToken = 6, kStEnd = 7,
   // sub-stage marks (kind kTrMark)

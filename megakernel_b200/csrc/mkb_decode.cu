@@ -8,15 +8,17 @@
 //     a grid transition (except a one-off acquire before re-reading KV rows in a
 //     multi-token launch), so HBM keeps streaming while the consumers wait.
 //   * warps 0-15 (consumers) run the stages of each layer and hand off between
-//     CTAs through gpu-scope release/acquire counters in the workspace:
-//        A  : input RMSNorm + QKV GEMV rows                        -> T_A
+//     CTAs through the workspace without grid barriers or fences:
+//        A  : input RMSNorm + QKV GEMV rows -> tagged words (value | tag)
 //        BC : q/k RMSNorm + RoPE + KV append, GQA decode attention,
-//             o_proj partial of this KV head (red.add into acc_mid) -> T_BC
+//             o_proj partial of this KV head -> counted fixed-point
+//             red.add into acc_mid (complete when 8 heads have added)
 //        DE : post RMSNorm + gate/up SwiGLU rows + down-proj partial
 //             over the same rows of the transposed down weight
-//             (red.add into acc_down)                               -> T_DE
-//        (reference-layout down weight: D writes the SwiGLU vector -> T_D,
-//         E computes whole down rows and writes the residual       -> T_E)
+//             -> counted red.add into acc_down (complete at G adds)
+//        (reference-layout down weight: D writes the SwiGLU vector and
+//         publishes a counter, E computes whole down rows and writes the
+//         residual, then publishes the next counter)
 //     then final RMSNorm + tied LM head + block/grid argmax.
 // Every wait is bounded by DecodeParams::timeout_ns; on expiry the kernel
 // records an error in Workspace::error, stops issuing copies, drains the ones in
@@ -26,6 +28,7 @@
 // calls (megakernel.cu:9-739); see the per-stage comments below.
 
 #include <cfloat>
+#include <cstddef>
 #include <climits>
 #include <cstdint>
 #include <cuda_bf16.h>
@@ -40,32 +43,42 @@ struct __align__(128) Smem {
   uint8_t ring[kSlots][kSlotBytes];
   uint64_t full[kSlots];
   uint64_t empty[kSlots];
-  float r[kHidden];      // residual entering the current layer
-  float rmid[kHidden];   // residual after attention + o_proj
-  union {
+  uint64_t rxbar;        // kCluster arrivals: the cluster's down partials have landed
+  alignas(16) float r[kHidden];      // residual entering the current layer
+  alignas(16) float rmid[kHidden];   // residual after attention + o_proj
+  alignas(16) union {
     float att[kConsumerWarps][2][kHeadDim + 4];  // per-warp attention partials
+    float xred[kConsumerWarps][64];              // per-warp GEMV row partials
     float x[kInter];                             // SwiGLU vector (reference-layout down)
   } u;
-  float q[2][kHeadDim];  // rotated, pre-scaled queries of this KV head's two Q heads
-  float knew[kHeadDim];  // rotated new key (BF16-rounded)
-  float vnew[kHeadDim];  // new value (BF16-rounded)
-  float attn[2 * kHeadDim];
-  float gu[2][32];
-  float m[32];
-  float dpart[8][4];
-  float red[32];
+  // Normalised activation of the current GEMV stage as BF16 high part and
+  // remainder (MMA B operand columns 0 and 1).
+  alignas(16) __nv_bfloat16 xh[kHidden];
+  alignas(16) __nv_bfloat16 xl[kHidden];
+  alignas(16) float q[2][kHeadDim];  // rotated, pre-scaled queries of this KV head's two Q heads
+  alignas(16) float knew[kHeadDim];  // rotated new key (BF16-rounded)
+  alignas(16) float vnew[kHeadDim];  // new value (BF16-rounded)
+  alignas(16) float attn[2 * kHeadDim];
+  alignas(16) float gu[2][32];
+  alignas(16) float m[32];
+  alignas(16) float pbuf[kConsumerWarps][16];  // attention weights exchanged within a warp
+  float red[2 * kConsumerWarps];
   float best_v[kConsumerWarps];
   int best_i[kConsumerWarps];
   // Copy of the device LayerWeights table (+ the transposed down pointer) in
   // shared memory: grid-transition acquires invalidate L1, and these pointers
   // are needed on the critical path of every stage.
   const __nv_bfloat16* lwp[kMaxLayers][12];
+  unsigned long long tbuf[kTraceSmem];  // trace staging (traced instantiation only)
   int token;
   int is_last;
   int abort;
 };
 
 constexpr size_t kSmemBytes = sizeof(Smem);
+static_assert(offsetof(Smem, r) % 16 == 0 && offsetof(Smem, rmid) % 16 == 0 && offsetof(Smem, u) % 16 == 0 &&
+                  offsetof(Smem, xh) % 16 == 0 && offsetof(Smem, q) % 16 == 0 && offsetof(Smem, pbuf) % 16 == 0,
+              "vector-accessed shared arrays must be 16-byte aligned");
 static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 
 // Upper bound on one hardware-suspended mbarrier wait; the enclosing loops
@@ -81,17 +94,32 @@ struct Ctl {
   int trace_cap;
 };
 
-// Stage time stamp (consumer thread 0 only; no-op without a trace buffer).
+// Stage time stamps of consumer thread 0, compiled in only for the traced
+// instantiation. Stamps go to a shared-memory buffer (a global store per stamp
+// would queue behind the bulk copies and slow the stage being measured) and are
+// written to the CTA's trace row at the end of each token. Stamps are kept for
+// layers [kTraceLayerLo, kTraceLayerLo + kTraceLayers) and the token-level marks.
+template <bool kOn>
 struct Tracer {
-  unsigned long long* row;
-  int cap;
-  int n;
-  int who;  // the one thread that records
+  unsigned long long* row;   // global trace row of this CTA (or null)
+  unsigned long long* sbuf;  // shared-memory staging buffer
+  int cap;                   // entries of `row`
+  int n;                     // entries staged in sbuf
+  int base;                  // entries already written to `row`
   __device__ __forceinline__ void mark(uint32_t kind, uint32_t stage, int layer, int tok) {
-    if (row != nullptr && static_cast<int>(threadIdx.x) == who && n < cap) {
+    if (kOn && row != nullptr && threadIdx.x == 0 && n < kTraceSmem &&
+        ((layer >= kTraceLayerLo && layer < kTraceLayerLo + kTraceLayers) || stage == kStLM ||
+         stage == kStToken || stage == kStEnd)) {
       const uint64_t code = kind | ((stage & 31u) << 2) | ((static_cast<uint32_t>(layer) & 31u) << 7) |
                             ((static_cast<uint32_t>(tok) & 15u) << 12);
-      row[n++] = (code << 48) | (global_ns() & 0xffffffffffffull);
+      sbuf[n++] = (code << 48) | (global_ns() & 0xffffffffffffull);
+    }
+  }
+  __device__ __forceinline__ void flush() {
+    if (kOn && row != nullptr && threadIdx.x == 0) {
+      for (int i = 0; i < n && base + i < cap; ++i) row[base + i] = sbuf[i];
+      base += n;
+      n = 0;
     }
   }
 };
@@ -100,7 +128,7 @@ __device__ __forceinline__ bool aborted(const Ctl& c) {
   return *reinterpret_cast<volatile int*>(&c.sm->abort) != 0;
 }
 
-__device__ void raise_error(const Ctl& c, uint32_t code, int layer, int stage, int tok) {
+__device__ __noinline__ void raise_error(const Ctl c, uint32_t code, int layer, int stage, int tok) {
   if (atomicCAS(&c.ws->error[0], 0u, code) == 0u) {
     c.ws->error[1] = static_cast<uint32_t>(c.cta);
     c.ws->error[2] = static_cast<uint32_t>(layer);
@@ -111,8 +139,8 @@ __device__ void raise_error(const Ctl& c, uint32_t code, int layer, int stage, i
 }
 
 // Bounded spin until *ctr >= target (wrap-safe). Single thread.
-__device__ void spin_geq(const Ctl& c, const uint32_t* ctr, uint32_t target, uint32_t code, int layer,
-                         int stage, int tok) {
+__device__ __noinline__ void spin_geq(const Ctl c, const uint32_t* ctr, uint32_t target, uint32_t code,
+                                      int layer, int stage, int tok) {
   if (aborted(c)) return;
   if (static_cast<int>(ld_acquire(ctr) - target) >= 0) return;
   const uint64_t t0 = global_ns();
@@ -133,7 +161,8 @@ __device__ void spin_geq(const Ctl& c, const uint32_t* ctr, uint32_t target, uin
 }
 
 // Consumer-side transition: thread 0 waits, then all consumers proceed.
-__device__ __forceinline__ void transition_wait(const Ctl& c, Tracer& tr, const uint32_t* ctr, uint32_t target,
+template <class TR>
+__device__ __forceinline__ void transition_wait(const Ctl& c, TR& tr, const uint32_t* ctr, uint32_t target,
                                                 int layer, int stage, int tok) {
   tr.mark(kTrWaitBegin, stage, layer, tok);
   if (threadIdx.x == 0) spin_geq(c, ctr, target, kErrTimeoutTransition, layer, stage, tok);
@@ -142,27 +171,36 @@ __device__ __forceinline__ void transition_wait(const Ctl& c, Tracer& tr, const 
 }
 
 // Consumer-side publish: every consumer's writes are ordered before the add.
-__device__ __forceinline__ void transition_publish(Tracer& tr, uint32_t* ctr, int layer, int stage, int tok) {
+template <class TR>
+__device__ __forceinline__ void transition_publish(TR& tr, uint32_t* ctr, int layer, int stage, int tok) {
   consumer_sync(kConsumerThreads);
   if (threadIdx.x == 0) release_add(ctr, 1u);
   tr.mark(kTrPublish, stage, layer, tok);
 }
 
 // ---- ring (consumer side) ----------------------------------------------------
+// Bounded hardware-suspended wait on an mbarrier phase (out of line: the
+// fast path is a single test at each call site).
+__device__ __noinline__ void mbar_wait_bounded(const Ctl c, uint64_t* bar, uint32_t ph, int layer, int stage,
+                                               int tok) {
+  const uint64_t t0 = global_ns();
+  while (!mbar_wait(bar, ph, kSuspendNs)) {
+    if (aborted(c)) break;
+    if (global_ns() - t0 > c.timeout) {
+      raise_error(c, kErrTimeoutRing, layer, stage, tok);
+      break;
+    }
+  }
+}
+
+template <class TR = Tracer<false>>
 __device__ __forceinline__ uint32_t ring_wait(const Ctl& c, uint32_t n, int layer, int stage, int tok,
-                                              Tracer* tr = nullptr) {
+                                              TR* tr = nullptr) {
   const int s = static_cast<int>(n % kSlots);
   const uint32_t ph = (n / kSlots) & 1u;
   if (!mbar_test(&c.sm->full[s], ph)) {
     if (tr) tr->mark(kTrWaitBegin, kStRing, layer, tok);
-    const uint64_t t0 = global_ns();
-    while (!mbar_wait(&c.sm->full[s], ph, kSuspendNs)) {
-      if (aborted(c)) break;
-      if (global_ns() - t0 > c.timeout) {
-        raise_error(c, kErrTimeoutRing, layer, stage, tok);
-        break;
-      }
-    }
+    mbar_wait_bounded(c, &c.sm->full[s], ph, layer, stage, tok);
     if (tr) tr->mark(kTrWaitEnd, kStRing, layer, tok);
   }
   return smem_addr(c.sm->ring[s]);
@@ -238,16 +276,11 @@ struct Producer {
   bool stop;
   uint64_t pol_w, pol_kv;
   int lane;
-  Tracer tr;  // row grid + cta of the trace buffer
 
   __device__ Producer(const Ctl& ctl) : c(ctl), n(0), stop(false) {
     lane = threadIdx.x & 31;
     pol_w = policy_evict_first();
     pol_kv = policy_evict_last();
-    // ctl.trace is this CTA's consumer row (base + cta * cap); its producer row
-    // is base + (grid + cta) * cap.
-    tr = Tracer{ctl.trace ? ctl.trace + (size_t)gridDim.x * ctl.trace_cap : nullptr, ctl.trace_cap, 0,
-                kConsumerThreads};
   }
 
   // Reserve the next slot for `bytes`; returns its index or -1 once stopped.
@@ -258,7 +291,6 @@ struct Producer {
     int ok = 1;
     if (lane == 0) {
       if (!mbar_test(&c.sm->empty[s], ph)) {
-        tr.mark(kTrWaitBegin, kStSlot, static_cast<int>(n & 31u), 0);
         const uint64_t t0 = global_ns();
         while (!mbar_wait(&c.sm->empty[s], ph, kSuspendNs)) {
           if (aborted(c)) { ok = 0; break; }
@@ -268,11 +300,9 @@ struct Producer {
             break;
           }
         }
-        tr.mark(kTrWaitEnd, kStSlot, static_cast<int>(n & 31u), 0);
       }
       if (ok && aborted(c)) ok = 0;
       if (ok) mbar_arrive_expect_tx(&c.sm->full[s], bytes);
-      tr.mark(kTrMark, kStIssue, static_cast<int>(n & 31u), 0);
     }
     ok = __shfl_sync(0xffffffffu, ok, 0);
     if (!ok) { stop = true; return -1; }
@@ -291,12 +321,6 @@ struct Producer {
     bulk_g2s(c.sm->ring[s] + off, src, bytes, &c.sm->full[s], pol);
   }
 
-  // L2 prefetch (16-byte aligned operands only; others are simply skipped).
-  __device__ void prefetch(const void* src, uint32_t bytes) {
-    if (bytes == 0 || ((reinterpret_cast<uintptr_t>(src) | bytes) & 15u) != 0u) return;
-    bulk_prefetch_l2(src, bytes, pol_kv);
-  }
-
   // Wait for every copy still in flight before the CTA exits.
   __device__ void drain() {
     if (lane != 0) return;
@@ -312,70 +336,14 @@ struct Producer {
   }
 };
 
-// Pull this CTA's bytes of layer `l` (cache length `cl`) into L2 ahead of the
-// ring, so HBM keeps streaming while the consumers wait at grid transitions and
-// the ring refills from L2.
-__device__ void prefetch_layer(Producer& pr, const DecodeParams& p, const Plan& pl, int l, int cl, int splits) {
-  if (pr.lane == 0) {
-    for (int r = pl.qa; r < pl.qb;) {
-      int e = r < kQSize ? kQSize : (r < kQSize + kKVSize ? kQSize + kKVSize : kQKVRows);
-      if (e > pl.qb) e = pl.qb;
-      const __nv_bfloat16* src = r < kQSize ? lwt(pr.c, l, kWQ) + (size_t)r * kHidden
-                                 : r < kQSize + kKVSize
-                                     ? lwt(pr.c, l, kWK) + (size_t)(r - kQSize) * kHidden
-                                     : lwt(pr.c, l, kWV) + (size_t)(r - kQSize - kKVSize) * kHidden;
-      pr.prefetch(src, static_cast<uint32_t>(e - r) * kHidden * 2u);
-      r = e;
-    }
-    if (pl.in_bc) {
-      int ka, kb;
-      key_range(cl, splits, pl.c, &ka, &kb);
-      const size_t head_off = ((size_t)l * kNKV + pl.h) * (size_t)p.max_seq * kHeadDim;
-      pr.prefetch(p.k_cache + head_off + (size_t)ka * kHeadDim, static_cast<uint32_t>(kb - ka) * kHeadDim * 2u);
-      pr.prefetch(p.v_cache + head_off + (size_t)ka * kHeadDim, static_cast<uint32_t>(kb - ka) * kHeadDim * 2u);
-    }
-    const uint32_t gu = static_cast<uint32_t>(pl.jb - pl.ja) * kHidden * 2u;
-    pr.prefetch(lwt(pr.c, l, kWGate) + (size_t)pl.ja * kHidden, gu);
-    pr.prefetch(lwt(pr.c, l, kWUp) + (size_t)pl.ja * kHidden, gu);
-    if (p.down_t != nullptr) {
-      pr.prefetch(lwt(pr.c, l, kWDownT) + (size_t)pl.ja * kHidden, gu);
-    } else {
-      pr.prefetch(lwt(pr.c, l, kWDown) + (size_t)pl.da * kInter,
-                  static_cast<uint32_t>(pl.db - pl.da) * kInter * 2u);
-    }
-  }
-  if (pl.in_bc) {
-    const __nv_bfloat16* wo = lwt(pr.c, l, kWO);
-    for (int row = pl.oa + pr.lane; row < pl.ob; row += 32)
-      pr.prefetch(wo + (size_t)row * kQSize + pl.h * 2 * kHeadDim, 512u);
-  }
-  __syncwarp();
-}
-
-// Percentage of each CTA's LM-head rows pulled into L2 during the last layers.
-constexpr int kLmPreloadPct = 15;
-constexpr int kLmPreloadLayers = 4;
-
+template <bool kFused, bool kTraced>
 __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int pos0, int cl0,
                              int splits) {
   Producer pr(c);
-  const bool fused = p.down_t != nullptr;
-  const int nbc = kNKV * p.group_size;
   for (int t = 0; t < p.n_tokens && !pr.stop; ++t) {
     const int pos = pos0 + t;
     const int cl = cl0 + t;
     for (int l = p.layer_begin; l < p.layer_end && !pr.stop; ++l) {
-      // L2 prefetch one layer ahead (the next token's first layer after the last)
-      if (l == p.layer_begin && t == 0) prefetch_layer(pr, p, pl, l, cl, splits);
-      if (l + 1 < p.layer_end) prefetch_layer(pr, p, pl, l + 1, cl, splits);
-      else if (t + 1 < p.n_tokens) prefetch_layer(pr, p, pl, p.layer_begin, cl + 1, splits);
-      if ((p.flags & kFlagLmHead) && l >= p.layer_end - kLmPreloadLayers && pr.lane == 0) {
-        const int npre = (pl.vb - pl.va) * kLmPreloadPct / 100;
-        const int part_i = l - (p.layer_end - kLmPreloadLayers);
-        const int r0 = pl.va + part(npre, kLmPreloadLayers, part_i);
-        const int r1 = pl.va + part(npre, kLmPreloadLayers, part_i + 1);
-        pr.prefetch(p.lm_head + (size_t)r0 * kHidden, static_cast<uint32_t>(r1 - r0) * kHidden * 2u);
-      }
       // A: QKV rows, one bulk copy per row into a padded row slot
       for (int r = pl.qa; r < pl.qb;) {
         const int e = qkv_chunk_end(r, pl.qb);
@@ -398,7 +366,7 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         if (t > 0 && kb > ka && pr.lane == 0) {
           // The previous token of this launch appended K/V at pos-1; make it
           // visible to the bulk-copy engine before re-reading those rows.
-          spin_geq(c, &p.ws->sync[l][1][0], static_cast<uint32_t>(nbc * t), kErrTimeoutTransition, l, 10, t);
+          spin_geq(c, &p.ws->kv_ready[l][pl.h][0], 2u * static_cast<uint32_t>(t), kErrTimeoutTransition, l, 10, t);
           fence_proxy_async_global();
         }
         const size_t head_off = ((size_t)l * kNKV + pl.h) * (size_t)p.max_seq * kHeadDim;
@@ -452,7 +420,7 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         }
         pr.end();
       }
-      if (fused) {
+      if constexpr (kFused) {
         const __nv_bfloat16* wdt = lwt(pr.c, l, kWDownT);
         for (int j0 = pl.ja; j0 < pl.jb; j0 += kRowsPerChunk1024) {
           const int j1 = min(pl.jb, j0 + kRowsPerChunk1024);
@@ -489,73 +457,73 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 }
 
 // ---- consumers -----------------------------------------------------------------
+//
+// Vector ownership: consumer thread i owns elements [kE*i, kE*i + kE) of every
+// 1024-vector (residual, accumulators, norm weights).
 
 // ---- tensor-core GEMV over padded rows in a ring slot -------------------------
-// Warp w owns the reduction range k in [64w, 64w+64) of a 1024-wide row (four
-// 16-wide MMA k-steps); the 16 warps' partial sums are added through shared
-// memory. The activation x enters as B columns 0 (bf16 hi part) and 1 (bf16
-// remainder x - hi), so D[:,0] + D[:,1] carries ~16 mantissa bits of x.
-//
-// Norm weights for this lane's B-fragment entries (lanes 0-7 only), loaded ahead
-// of the transition that gates the norm.
-__device__ __forceinline__ void load_norm_k(const __nv_bfloat16* w, uint32_t nw2[4][2]) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int st = 0; st < 4; ++st) {
-    const int k = 64 * warp + 16 * st + 2 * (lane & 3);
-    if (lane < 8 && w != nullptr) {
-      nw2[st][0] = __ldg(reinterpret_cast<const unsigned int*>(w + k));
-      nw2[st][1] = __ldg(reinterpret_cast<const unsigned int*>(w + k + 8));
-    } else {
-      nw2[st][0] = 0x3f803f80u;  // bf16 1.0 pair
-      nw2[st][1] = 0x3f803f80u;
-    }
-  }
+// Warp w owns the reduction range k in [kKPerWarp*w, kKPerWarp*(w+1)) of a
+// 1024-wide row (kKSteps 16-wide MMA k-steps); the warps' partial sums are added
+// through shared memory. The activation enters as B columns 0 (BF16 high part)
+// and 1 (BF16 remainder x - high), so D[:,0] + D[:,1] carries ~16 mantissa bits
+// of x. Both parts are written once per stage into sm.xh / sm.xl.
+constexpr int kE = kHidden / kConsumerThreads;       // elements per consumer thread
+constexpr int kKPerWarp = kHidden / kConsumerWarps;  // GEMV k range per warp
+constexpr int kKSteps = kKPerWarp / 16;
+constexpr int kKeysPerWarp = kKeysPerChunk / kConsumerWarps;  // attention keys per warp and chunk
+constexpr int kOSteps = 2 * kHeadDim / 16 / kConsumerWarps;   // o_proj k-steps per warp
+static_assert(kE == 4, "the vector helpers below move 4 elements per thread");
+static_assert(kKeysPerWarp == 8, "the attention butterfly reduces 2 x 8 scores per warp");
+static_assert(kOSteps >= 1 && kKSteps >= 1, "warp count");
+
+// This thread's 4 norm-weight elements (8 bytes, read-only path); issued a stage
+// ahead of use.
+__device__ __forceinline__ uint2 load_w4(const __nv_bfloat16* w) {
+  if (w == nullptr) return make_uint2(0x3f803f80u, 0x3f803f80u);  // bf16 1.0 pairs
+  return __ldg(reinterpret_cast<const uint2*>(w) + threadIdx.x);
 }
-// B fragments of x = v * rstd * w for this warp's k range (v in shared memory).
-__device__ __forceinline__ void build_bfrag(const float* v, float rstd, const uint32_t nw2[4][2], uint32_t bfr[4][2]) {
+// x = v * rstd * w for this thread's 4 elements, written as BF16 high part and
+// remainder into sm.xh / sm.xl (8 bytes each).
+__device__ __forceinline__ void store_x(Smem& sm, const float v[4], float rstd, uint2 w) {
+  const float x0 = v[0] * rstd * bf_lo(w.x), x1 = v[1] * rstd * bf_hi(w.x);
+  const float x2 = v[2] * rstd * bf_lo(w.y), x3 = v[3] * rstd * bf_hi(w.y);
+  const uint32_t h01 = pack_bf2(x0, x1), h23 = pack_bf2(x2, x3);
+  const uint32_t l01 = pack_bf2(x0 - bf_lo(h01), x1 - bf_hi(h01));
+  const uint32_t l23 = pack_bf2(x2 - bf_lo(h23), x3 - bf_hi(h23));
+  const int e = threadIdx.x * kE;
+  *reinterpret_cast<uint2*>(&sm.xh[e]) = make_uint2(h01, h23);
+  *reinterpret_cast<uint2*>(&sm.xl[e]) = make_uint2(l01, l23);
+}
+// B fragments of this warp's k-steps (lanes 0-3: high part, 4-7: remainder).
+__device__ __forceinline__ void load_bfrag(const Smem& sm, uint32_t bfr[kKSteps][2]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t base = smem_addr(lane < 4 ? sm.xh : sm.xl) + (kKPerWarp * warp + 2 * (lane & 3)) * 2;
 #pragma unroll
-  for (int st = 0; st < 4; ++st) {
-    bfr[st][0] = 0u;
-    bfr[st][1] = 0u;
-    if (lane < 8) {
-      const int k = 64 * warp + 16 * st + 2 * (lane & 3);
-      const float x0 = v[k] * rstd * bf_lo(nw2[st][0]);
-      const float x1 = v[k + 1] * rstd * bf_hi(nw2[st][0]);
-      const float x8 = v[k + 8] * rstd * bf_lo(nw2[st][1]);
-      const float x9 = v[k + 9] * rstd * bf_hi(nw2[st][1]);
-      const uint32_t h0 = pack_bf2(x0, x1), h1 = pack_bf2(x8, x9);
-      if (lane < 4) {
-        bfr[st][0] = h0;
-        bfr[st][1] = h1;
-      } else {
-        bfr[st][0] = pack_bf2(x0 - bf_lo(h0), x1 - bf_hi(h0));
-        bfr[st][1] = pack_bf2(x8 - bf_lo(h1), x9 - bf_hi(h1));
-      }
-    }
+  for (int st = 0; st < kKSteps; ++st) {
+    bfr[st][0] = lane < 8 ? lds32(base + st * 32) : 0u;
+    bfr[st][1] = lane < 8 ? lds32(base + st * 32 + 16) : 0u;
   }
 }
 // One 16-row tile of padded 1024-wide rows at `base` (rows >= nrows read row 0).
-__device__ __forceinline__ void mma_tile_1024(uint32_t base, int nrows, const uint32_t bfr[4][2], float* d) {
+__device__ __forceinline__ void mma_tile_1024(uint32_t base, int nrows, const uint32_t bfr[kKSteps][2], float* d) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int tr = lane & 15;
-  const uint32_t row = base + (tr < nrows ? tr : 0) * kRowStride + (lane >> 4) * 16 + warp * 128;
+  const uint32_t row = base + (tr < nrows ? tr : 0) * kRowStride + (lane >> 4) * 16 + warp * (kKPerWarp * 2);
 #pragma unroll
-  for (int st = 0; st < 4; ++st) {
+  for (int st = 0; st < kKSteps; ++st) {
     uint32_t a0, a1, a2, a3;
     ldsm_x4(row + st * 32, a0, a1, a2, a3);
     mma_bf16(d, a0, a1, a2, a3, bfr[st][0], bfr[st][1]);
   }
 }
 // Gate/up tile: tile rows 0-6 are gate rows, 8-14 up rows (second slot half).
-__device__ __forceinline__ void mma_tile_gu(uint32_t base, int nrows, const uint32_t bfr[4][2], float* d) {
+__device__ __forceinline__ void mma_tile_gu(uint32_t base, int nrows, const uint32_t bfr[kKSteps][2], float* d) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int tr = lane & 15, i = tr & 7;
   const uint32_t row = base + (tr >= 8 ? kSlotBytes / 2 : 0) + (i < nrows ? i : 0) * kRowStride + (lane >> 4) * 16 +
-                       warp * 128;
+                       warp * (kKPerWarp * 2);
 #pragma unroll
-  for (int st = 0; st < 4; ++st) {
+  for (int st = 0; st < kKSteps; ++st) {
     uint32_t a0, a1, a2, a3;
     ldsm_x4(row + st * 32, a0, a1, a2, a3);
     mma_bf16(d, a0, a1, a2, a3, bfr[st][0], bfr[st][1]);
@@ -578,8 +546,9 @@ __device__ __forceinline__ float sum_warps(float (*xred)[64], int idx) {
 
 // Wait for `cnt` consecutive chunks from ring position n (all already issued by
 // the producer); their slot addresses go to sa[].
+template <class TR>
 __device__ __forceinline__ void ring_wait_all(const Ctl& c, uint32_t n, int cnt, uint32_t* sa, int layer, int stage,
-                                              int tok, Tracer* tr) {
+                                              int tok, TR* tr) {
 #pragma unroll
   for (int i = 0; i < 3; ++i)
     if (i < cnt) sa[i] = ring_wait(c, n + i, layer, stage, tok, tr);
@@ -591,10 +560,10 @@ __device__ __forceinline__ void ring_done_all(const Ctl& c, uint32_t& n, int cnt
   n += cnt;
 }
 
-// Block-wide sum of a*a + b*b over the consumer threads (one named barrier;
-// s_red alternates between two halves so no trailing barrier is needed).
-__device__ __forceinline__ float block_sumsq(float a, float b, float* s_red, int& flip) {
-  const float ss = warp_sum(a * a + b * b);
+// Block-wide sum over the consumer threads of `v` (one named barrier; s_red
+// alternates between two halves so no trailing barrier is needed).
+__device__ __forceinline__ float block_sum(float v, float* s_red, int& flip) {
+  const float ss = warp_sum(v);
   float* buf = s_red + (flip ? kConsumerWarps : 0);
   flip ^= 1;
   if ((threadIdx.x & 31) == 0) buf[threadIdx.x >> 5] = ss;
@@ -625,43 +594,151 @@ __device__ __forceinline__ void xr_from(const float* v, float rstd, const uint4 
   }
 }
 
-// Butterfly sums of three per-lane partials at once (independent shuffle chains).
-__device__ __forceinline__ void warp_sum3(float& a, float& b, float& d) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a += __shfl_xor_sync(0xffffffffu, a, o);
-    b += __shfl_xor_sync(0xffffffffu, b, o);
-    d += __shfl_xor_sync(0xffffffffu, d, o);
-  }
-}
-
 // Bounded poll of two tagged words (16 bytes) until both carry `tag`.
+__device__ __noinline__ ulonglong2 poll_tagged2_slow(const Ctl c, const uint64_t* p, uint32_t tag, int layer,
+                                                    int tok) {
+  uint64_t a = 0, b = 0;
+  const uint64_t t0 = global_ns();
+  uint32_t it = 0;
+  while (true) {
+    ld_tagged2(p, a, b);
+    if (static_cast<uint32_t>(a >> 32) == tag && static_cast<uint32_t>(b >> 32) == tag) break;
+    if ((++it & 15u) == 0u) {
+      if (aborted(c) || ld_relaxed(&c.ws->error[0]) != 0u) {
+        *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
+        break;
+      }
+      if (global_ns() - t0 > c.timeout) {
+        raise_error(c, kErrTimeoutTransition, layer, kStBC, tok);
+        break;
+      }
+    }
+  }
+  return make_ulonglong2(a, b);
+}
 __device__ __forceinline__ void poll_tagged2(const Ctl& c, const uint64_t* p, uint32_t tag, float& v0, float& v1,
                                              int layer, int tok) {
   uint64_t a, b;
   ld_tagged2(p, a, b);
   if (static_cast<uint32_t>(a >> 32) != tag || static_cast<uint32_t>(b >> 32) != tag) {
-    const uint64_t t0 = global_ns();
-    uint32_t it = 0;
-    while (true) {
-      ld_tagged2(p, a, b);
-      if (static_cast<uint32_t>(a >> 32) == tag && static_cast<uint32_t>(b >> 32) == tag) break;
-      if ((++it & 15u) == 0u) {
-        if (aborted(c) || ld_relaxed(&c.ws->error[0]) != 0u) {
-          *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
-          break;
-        }
-        if (global_ns() - t0 > c.timeout) {
-          raise_error(c, kErrTimeoutTransition, layer, kStBC, tok);
-          break;
-        }
-      }
-    }
+    const ulonglong2 w = poll_tagged2_slow(c, p, tag, layer, tok);
+    a = w.x;
+    b = w.y;
   }
   v0 = __uint_as_float(static_cast<uint32_t>(a));
   v1 = __uint_as_float(static_cast<uint32_t>(b));
 }
 
+// ---- counted fixed-point accumulators (layout in mkb_config.cuh) ---------------
+// One contribution x: kAccOne + round(x * 2^28) + kAccBias. |x| >= 2^19 (or
+// NaN) is clamped and flags `bad`.
+__device__ __forceinline__ uint64_t acc_term(float x, bool& bad) {
+  float s = x * 268435456.0f;
+  constexpr float kLim = 140737488355000.0f;  // just below 2^47
+  if (!(fabsf(s) < kLim)) {
+    bad = true;
+    s = s > 0.f ? kLim : -kLim;  // NaN clamps to the negative limit
+  }
+  return kAccOne + static_cast<uint64_t>(__float2ll_rn(s) + static_cast<long long>(kAccBias));
+}
+__device__ __forceinline__ float acc_decode(uint64_t low, uint64_t cnt) {
+  const long long fixed = static_cast<long long>(low) - static_cast<long long>(cnt * kAccBias);
+  return __ll2float_rn(fixed) * (1.0f / 268435456.0f);
+}
+// Sum carried by `copies` words at stride kHidden; `count` receives the number
+// of contributions.
+__device__ __forceinline__ float acc_value(const uint64_t* w, int copies, uint32_t& count) {
+  uint64_t low = 0, cnt = 0;
+  for (int q = 0; q < copies; ++q) {
+    const uint64_t v = ld_relaxed_u64(w + q * kHidden);
+    cnt += v >> 56;
+    low += v & kAccLowMask;
+  }
+  count = static_cast<uint32_t>(cnt);
+  return acc_decode(low, cnt);
+}
+// Bounded poll of one element until it holds `expect` contributions.
+__device__ __noinline__ float acc_wait_slow(const Ctl c, const uint64_t* w, int copies, uint32_t expect, int layer,
+                                            int stage, int tok) {
+  const uint64_t t0 = global_ns();
+  uint32_t it = 0, cnt = 0;
+  float v = 0.f;
+  while (true) {
+    v = acc_value(w, copies, cnt);
+    if (cnt == expect) break;
+    if ((++it & 15u) == 0u) {
+      if (aborted(c) || ld_relaxed(&c.ws->error[0]) != 0u) {
+        *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
+        break;
+      }
+      if (global_ns() - t0 > c.timeout) {
+        raise_error(c, kErrTimeoutTransition, layer, stage, tok);
+        break;
+      }
+    }
+  }
+  return v;
+}
+// This thread's 4 elements of a [copies][kHidden] accumulator row, each
+// complete with `expect` contributions. Lane 0 polls first, so a warp that
+// arrives early generates one poll stream instead of 32.
+__device__ __forceinline__ void acc_wait4(const Ctl& c, const uint64_t* row, int copies, uint32_t expect, float v[4],
+                                          int layer, int stage, int tok) {
+  const uint64_t* w = row + threadIdx.x * kE;
+  uint32_t cnt = 0;
+  if ((threadIdx.x & 31) == 0) {
+    acc_value(w, copies, cnt);
+    if (cnt != expect) acc_wait_slow(c, w, copies, expect, layer, stage, tok);
+  }
+  __syncwarp();
+  uint64_t low[4] = {0, 0, 0, 0}, cn[4] = {0, 0, 0, 0};
+  for (int q = 0; q < copies; ++q) {
+    uint64_t a, b, x, y;
+    ld_tagged2(w + q * kHidden, a, b);
+    ld_tagged2(w + q * kHidden + 2, x, y);
+    cn[0] += a >> 56; low[0] += a & kAccLowMask;
+    cn[1] += b >> 56; low[1] += b & kAccLowMask;
+    cn[2] += x >> 56; low[2] += x & kAccLowMask;
+    cn[3] += y >> 56; low[3] += y & kAccLowMask;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[i] = acc_decode(low[i], cn[i]);
+    if (cn[i] != expect) v[i] = acc_wait_slow(c, w + i, copies, expect, layer, stage, tok);
+  }
+}
+// Clear this thread's 4 elements of an accumulator row.
+__device__ __forceinline__ void acc_clear4(uint64_t* row) {
+  uint64_t* w = row + threadIdx.x * kE;
+  *reinterpret_cast<ulonglong2*>(w) = make_ulonglong2(0ull, 0ull);
+  *reinterpret_cast<ulonglong2*>(w + 2) = make_ulonglong2(0ull, 0ull);
+}
+
+// Receive buffer of the cluster pre-reduction: [kCluster senders][kSlice] floats in
+// the union after the GEMV partials. It overlaps the attention partials, which
+// are never live at the same time: a sender writes layer l's slice only after
+// acc_mid[l] is complete (every owner has left its attention of layer l), and
+// writes layer l+1's only after acc_down[l] is complete (every owner has read
+// layer l's slices).
+constexpr int kSlice = kHidden / kCluster;  // accumulator elements owned per cluster rank
+__device__ __forceinline__ float (*cluster_rx(Smem& sm))[kSlice] {
+  return reinterpret_cast<float(*)[kSlice]>(&sm.u.x[512]);
+}
+__device__ __noinline__ void cluster_rx_wait_slow(const Ctl c, uint32_t ph, int layer, int tok) {
+  const uint64_t t0 = global_ns();
+  while (!mbar_wait_cluster(&c.sm->rxbar, ph, kSuspendNs)) {
+    if (aborted(c)) break;
+    if (global_ns() - t0 > c.timeout) {
+      raise_error(c, kErrTimeoutTransition, layer, kStDE, tok);
+      break;
+    }
+  }
+}
+__device__ __forceinline__ void cluster_rx_wait(const Ctl& c, uint32_t ph, int layer, int tok) {
+  if (!mbar_wait_cluster(&c.sm->rxbar, ph, 0u)) cluster_rx_wait_slow(c, ph, layer, tok);
+}
+
+template <bool kFused, bool kTraced>
 __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int token0, int pos0, int cl0,
                              int splits, uint32_t tag0) {
   Smem& sm = *c.sm;
@@ -669,22 +746,23 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const bool fused = p.down_t != nullptr;
+  const int e0 = tid * kE;  // first element owned by this thread
+  constexpr bool fused = kFused;
   const int G = p.grid;
-  const int nbc = kNKV * p.group_size;
   const int lb = p.layer_begin, le = p.layer_end;
   const int zero_cta = G - 1;
   uint32_t n = 0;
+  uint32_t xph = 0;  // phase of sm.rxbar for the next cluster exchange
   int flip = 0;
   float xr[32];
-  Tracer tr{c.trace, c.trace_cap, 0, 0};
+  Tracer<kTraced> tr{c.trace, sm.tbuf, c.trace_cap, 0, 0};
+  float(*xred)[64] = sm.u.xred;
 
   int token = token0;
   for (int t = 0; t < p.n_tokens; ++t) {
     const int pos = pos0 + t;
     const int cl = cl0 + t;
     const uint32_t tgtG = static_cast<uint32_t>(G * (t + 1));
-    const uint32_t tgtBC = static_cast<uint32_t>(nbc * (t + 1));
     const uint32_t tag = tag0 + static_cast<uint32_t>(t) + 1u;
     tr.mark(kTrMark, kStToken, 0, t);
 
@@ -697,50 +775,57 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       token = sm.token;
     }
     token = min(max(token, 0), kVocab - 1);
-    float r0 = p.input_residual ? __ldcg(p.input_residual + tid)
-                                : __bfloat162float(p.embed[(size_t)token * kHidden + tid]);
-    float r1 = p.input_residual ? __ldcg(p.input_residual + tid + kConsumerThreads)
-                                : __bfloat162float(p.embed[(size_t)token * kHidden + tid + kConsumerThreads]);
+    float r[4];
+    if (p.input_residual) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(p.input_residual) + tid);
+      r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+    } else {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(p.embed + (size_t)token * kHidden) + tid);
+      r[0] = bf_lo(u.x); r[1] = bf_hi(u.x); r[2] = bf_lo(u.y); r[3] = bf_hi(u.y);
+    }
 
-    uint32_t nwA[4][2], nwD[4][2];
-    if (le > lb) load_norm_k(lwt(c, lb, kWNorm), nwA);
+    uint2 wA = make_uint2(0u, 0u), wD = make_uint2(0u, 0u);
+    if (le > lb) wA = load_w4(lwt(c, lb, kWNorm));
     for (int l = lb; l < le; ++l) {
       // ================= A: RMSNorm + QKV rows (megakernel.cu:704-739, 633-701) ===
-      uint32_t bfr[4][2];
-      float(*xred)[64] = reinterpret_cast<float(*)[64]>(&sm.u.att[0][0][0]);
       if (l > lb) {
-        transition_wait(c, tr, &ws->sync[l - 1][fused ? 2 : 3][0], tgtG, l, kStA, t);
-        if (fused) {
-          r0 = sm.rmid[tid] + __ldcg(&ws->acc_down[l - 1][tid]);
-          r1 = sm.rmid[tid + kConsumerThreads] + __ldcg(&ws->acc_down[l - 1][tid + kConsumerThreads]);
+        if constexpr (fused) {
+          tr.mark(kTrWaitBegin, kStA, l, t);
+          float d[4];
+          acc_wait4(c, &ws->acc_down[l - 1][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster), d, l, kStA, t);
+          tr.mark(kTrWaitEnd, kStA, l, t);
+          const float4 rm = *reinterpret_cast<const float4*>(&sm.rmid[e0]);
+          r[0] = rm.x + d[0]; r[1] = rm.y + d[1]; r[2] = rm.z + d[2]; r[3] = rm.w + d[3];
         } else {
-          r0 = __ldcg(&ws->resid[tid]);
-          r1 = __ldcg(&ws->resid[tid + kConsumerThreads]);
+          transition_wait(c, tr, &ws->sync[l - 1][3][0], tgtG, l, kStA, t);
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(ws->resid) + tid);
+          r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
         }
         // Every CTA has finished layer l-1 (and so read the accumulators of
         // layer l-2): clear those for the next token.
         if (c.cta == zero_cta && l >= lb + 2) {
-          ws->acc_mid[l - 2][tid] = 0.f;
-          ws->acc_mid[l - 2][tid + kConsumerThreads] = 0.f;
-          ws->acc_down[l - 2][tid] = 0.f;
-          ws->acc_down[l - 2][tid + kConsumerThreads] = 0.f;
+          acc_clear4(&ws->acc_mid[l - 2][0]);
+#pragma unroll
+          for (int q = 0; q < kDownCopies; ++q) acc_clear4(&ws->acc_down[l - 2][q][0]);
         }
       }
-      sm.r[tid] = r0;
-      sm.r[tid + kConsumerThreads] = r1;
+      *reinterpret_cast<float4*>(&sm.r[e0]) = make_float4(r[0], r[1], r[2], r[3]);
+      uint32_t bfr[kKSteps][2];
       {
-        const float tot = block_sumsq(r0, r1, sm.red, flip);
+        const float tot = block_sum(r[0] * r[0] + r[1] * r[1] + r[2] * r[2] + r[3] * r[3], sm.red, flip);
         tr.mark(kTrMark, kSubAInput, l, t);
-        build_bfrag(sm.r, rsqrtf(tot * (1.0f / kHidden) + kEps), nwA, bfr);
+        store_x(sm, r, rsqrtf(tot * (1.0f / kHidden) + kEps), wA);
+        consumer_sync(kConsumerThreads);
+        load_bfrag(sm, bfr);
       }
       tr.mark(kTrMark, kSubANorm, l, t);
       // QKV rows: up to three padded chunks (one 16-row MMA tile each) per pass
-      for (int r = pl.qa; r < pl.qb;) {
-        const int ra0 = r, ea0 = qkv_chunk_end(ra0, pl.qb);
+      for (int rr = pl.qa; rr < pl.qb;) {
+        const int ra0 = rr, ea0 = qkv_chunk_end(ra0, pl.qb);
         const int ra1 = ea0, ea1 = ra1 < pl.qb ? qkv_chunk_end(ra1, pl.qb) : ra1;
         const int ra2 = ea1, ea2 = ra2 < pl.qb ? qkv_chunk_end(ra2, pl.qb) : ra2;
         const int na = 1 + (ea1 > ra1) + (ea2 > ra2);
-        r = ea2;
+        rr = ea2;
         uint32_t sa[3];
         ring_wait_all(c, n, na, sa, l, 0, t, &tr);
         float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f}, d2[4] = {0.f, 0.f, 0.f, 0.f};
@@ -759,16 +844,18 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           if ((tid & 15) < 15 && row < end) {
             const float val = sum_warps(xred, tid);
             st_tagged(&ws->qkv_tagged[l][row], val, tag);
-            float* dst = row < kQSize ? p.q_out + row
-                         : row < kQSize + kKVSize ? p.k_out + (row - kQSize)
-                                                  : p.v_out + (row - kQSize - kKVSize);
-            *dst = val;
+            if (l == le - 1) {  // raw QKV outputs are reported for the last layer only
+              float* dst = row < kQSize ? p.q_out + row
+                           : row < kQSize + kKVSize ? p.k_out + (row - kQSize)
+                                                    : p.v_out + (row - kQSize - kKVSize);
+              *dst = val;
+            }
           }
         }
         consumer_sync(kConsumerThreads);
       }
       tr.mark(kTrPublish, kStA, l, t);
-      load_norm_k(lwt(c, l, kWPost), nwD);  // post-attention norm, one stage ahead
+      wD = load_w4(lwt(c, l, kWPost));  // post-attention norm, one stage ahead
 
       // ================= BC: head norm + RoPE + KV append, attention, o_proj =====
       if (pl.in_bc) {
@@ -779,10 +866,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         const int d0 = 2 * lane;
         if (warp < 3) {
           const __nv_bfloat16* nw = lwt(c, l, warp < 2 ? kWQNorm : kWKNorm);
-          w0 = __bfloat162float(nw[d0]);
-          w1 = __bfloat162float(nw[d0 + 1]);
-          w2 = __bfloat162float(nw[d0 + 64]);
-          w3 = __bfloat162float(nw[d0 + 65]);
+          const uint32_t wa = __ldg(reinterpret_cast<const unsigned int*>(nw + d0));
+          const uint32_t wb = __ldg(reinterpret_cast<const unsigned int*>(nw + d0 + 64));
+          w0 = bf_lo(wa); w1 = bf_hi(wa); w2 = bf_lo(wb); w3 = bf_hi(wb);
           const size_t rb = (size_t)pos * kHeadDim;
           cs0 = rope_at(p.cos_table, p.rope_fp32, rb + d0);
           sn0 = rope_at(p.sin_table, p.rope_fp32, rb + d0);
@@ -840,124 +926,124 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         consumer_sync(kConsumerThreads);
         tr.mark(kTrWaitEnd, kStBC, l, t);
         tr.mark(kTrMark, kSubBCPrep, l, t);
-        // GQA decode attention over keys [ka, kb) (megakernel.cu:228-370),
-        // per-warp online softmax in the exp2 domain, then a 16-warp combine.
+        // GQA decode attention over keys [ka, kb) (megakernel.cu:228-370): per
+        // 64-key chunk warp w takes keys [8w, 8w+8) for both Q heads; lane holds
+        // dims [4 lane, 4 lane + 4). The 16 dot products are summed over the
+        // warp by a reduce-scatter butterfly (16 shuffles), after which lane L
+        // holds score j = (L >> 1) & 15 (head j >> 3, key j & 7). Online softmax
+        // per warp in the exp2 domain, then a combine over the warps.
         int ka, kb;
         key_range(cl, splits, pl.c, &ka, &kb);
         if (kb > ka) {
           float q0[4], q1[4];
-#pragma unroll
-          for (int d = 0; d < 4; ++d) {
-            q0[d] = sm.q[0][lane * 4 + d];
-            q1[d] = sm.q[1][lane * 4 + d];
+          {
+            const float4 a = *reinterpret_cast<const float4*>(&sm.q[0][lane * 4]);
+            const float4 b = *reinterpret_cast<const float4*>(&sm.q[1][lane * 4]);
+            q0[0] = a.x; q0[1] = a.y; q0[2] = a.z; q0[3] = a.w;
+            q1[0] = b.x; q1[1] = b.y; q1[2] = b.z; q1[3] = b.w;
           }
-          float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+          const int jm = (lane >> 1) & 15;   // score held after the butterfly
+          const int my_key = jm & 7;
+          const bool my_head1 = jm >= 8;
+          float m = -INFINITY, lsum = 0.f;   // this lane's head: running max and sum
           float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
           for (int k0 = ka; k0 < kb; k0 += kKeysPerChunk) {
             const int k1 = min(kb, k0 + kKeysPerChunk);
+            const int kw = k0 + warp * kKeysPerWarp;  // this warp's first key
             const uint32_t sa = ring_wait(c, n, l, 1, t, &tr);
-            float s0[4], s1[4];
+            float v[16];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int kk = k0 + warp * 4 + i;
+            for (int i = 0; i < kKeysPerWarp; ++i) {
+              const int kk = kw + i;
               float kx0 = 0.f, kx1 = 0.f, kx2 = 0.f, kx3 = 0.f;
               if (kk < k1) {
                 if (kk == pos) {
-                  kx0 = sm.knew[lane * 4 + 0];
-                  kx1 = sm.knew[lane * 4 + 1];
-                  kx2 = sm.knew[lane * 4 + 2];
-                  kx3 = sm.knew[lane * 4 + 3];
+                  const float4 kn = *reinterpret_cast<const float4*>(&sm.knew[lane * 4]);
+                  kx0 = kn.x; kx1 = kn.y; kx2 = kn.z; kx3 = kn.w;
                 } else {
                   const uint2 u = lds64(sa + (kk - k0) * (kHeadDim * 2) + lane * 8);
-                  kx0 = bf_lo(u.x);
-                  kx1 = bf_hi(u.x);
-                  kx2 = bf_lo(u.y);
-                  kx3 = bf_hi(u.y);
+                  kx0 = bf_lo(u.x); kx1 = bf_hi(u.x); kx2 = bf_lo(u.y); kx3 = bf_hi(u.y);
                 }
               }
-              s0[i] = fmaf(q0[3], kx3, fmaf(q0[2], kx2, fmaf(q0[1], kx1, q0[0] * kx0)));
-              s1[i] = fmaf(q1[3], kx3, fmaf(q1[2], kx2, fmaf(q1[1], kx1, q1[0] * kx0)));
+              v[i] = fmaf(q0[3], kx3, fmaf(q0[2], kx2, fmaf(q0[1], kx1, q0[0] * kx0)));
+              v[8 + i] = fmaf(q1[3], kx3, fmaf(q1[2], kx2, fmaf(q1[1], kx1, q1[0] * kx0)));
             }
+            // reduce-scatter butterfly: 16 -> 8 -> 4 -> 2 -> 1 values, then the last lane bit
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
+            for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
+              const bool up = (lane & bit) != 0;
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                s0[i] += __shfl_xor_sync(0xffffffffu, s0[i], o);
-                s1[i] += __shfl_xor_sync(0xffffffffu, s1[i], o);
+              for (int j = 0; j < half; ++j) {
+                const float send = up ? v[j] : v[j + half];
+                const float keep = up ? v[j + half] : v[j];
+                v[j] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
               }
             }
-            float mx0 = m0, mx1 = m1;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              if (k0 + warp * 4 + i >= k1) {
-                s0[i] = -INFINITY;
-                s1[i] = -INFINITY;
-              }
-              mx0 = fmaxf(mx0, s0[i]);
-              mx1 = fmaxf(mx1, s1[i]);
+            float s = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+            if (kw + my_key >= k1) s = -INFINITY;
+            // online softmax for this lane's head over the warp's 8 keys
+            float mx = s;
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            const float mnew = fmaxf(m, mx);
+            float sc = 1.f, pk = 0.f;
+            if (mnew > -INFINITY) {
+              sc = exp2f(m - mnew);
+              pk = s > -INFINITY ? exp2f(s - mnew) : 0.f;
             }
-            float p0[4] = {0.f, 0.f, 0.f, 0.f}, p1[4] = {0.f, 0.f, 0.f, 0.f};
-            if (mx0 > -INFINITY) {
-              const float sc = exp2f(m0 - mx0);
-              float ps = 0.f;
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                p0[i] = exp2f(s0[i] - mx0);
-                ps += p0[i];
-              }
-              l0 = l0 * sc + ps;
-#pragma unroll
-              for (int d = 0; d < 4; ++d) a0[d] *= sc;
-              m0 = mx0;
+            float ps = pk;
+            ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+            lsum = lsum * sc + ps;
+            m = mnew;
+            // both heads' rescale factors and the 16 weights for the value rows
+            const float sco = __shfl_xor_sync(0xffffffffu, sc, 16);
+            const float sc0 = my_head1 ? sco : sc, sc1 = my_head1 ? sc : sco;
+            if ((lane & 1) == 0) sm.pbuf[warp][jm] = pk;
+            __syncwarp();
+            float p0[8], p1[8];
+            {
+              const float4 x = *reinterpret_cast<const float4*>(&sm.pbuf[warp][0]);
+              const float4 y = *reinterpret_cast<const float4*>(&sm.pbuf[warp][4]);
+              const float4 z = *reinterpret_cast<const float4*>(&sm.pbuf[warp][8]);
+              const float4 w = *reinterpret_cast<const float4*>(&sm.pbuf[warp][12]);
+              p0[0] = x.x; p0[1] = x.y; p0[2] = x.z; p0[3] = x.w; p0[4] = y.x; p0[5] = y.y; p0[6] = y.z; p0[7] = y.w;
+              p1[0] = z.x; p1[1] = z.y; p1[2] = z.z; p1[3] = z.w; p1[4] = w.x; p1[5] = w.y; p1[6] = w.z; p1[7] = w.w;
             }
-            if (mx1 > -INFINITY) {
-              const float sc = exp2f(m1 - mx1);
-              float ps = 0.f;
+            __syncwarp();
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                p1[i] = exp2f(s1[i] - mx1);
-                ps += p1[i];
-              }
-              l1 = l1 * sc + ps;
-#pragma unroll
-              for (int d = 0; d < 4; ++d) a1[d] *= sc;
-              m1 = mx1;
+            for (int d = 0; d < 4; ++d) {
+              a0[d] *= sc0;
+              a1[d] *= sc1;
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int kk = k0 + warp * 4 + i;
+            for (int i = 0; i < kKeysPerWarp; ++i) {
+              const int kk = kw + i;
               if (kk < k1) {
-                float vx[4];
+                float vx0, vx1, vx2, vx3;
                 if (kk == pos) {
-#pragma unroll
-                  for (int d = 0; d < 4; ++d) vx[d] = sm.vnew[lane * 4 + d];
+                  const float4 vn = *reinterpret_cast<const float4*>(&sm.vnew[lane * 4]);
+                  vx0 = vn.x; vx1 = vn.y; vx2 = vn.z; vx3 = vn.w;
                 } else {
                   const uint2 u = lds64(sa + kSlotBytes / 2 + (kk - k0) * (kHeadDim * 2) + lane * 8);
-                  vx[0] = bf_lo(u.x);
-                  vx[1] = bf_hi(u.x);
-                  vx[2] = bf_lo(u.y);
-                  vx[3] = bf_hi(u.y);
+                  vx0 = bf_lo(u.x); vx1 = bf_hi(u.x); vx2 = bf_lo(u.y); vx3 = bf_hi(u.y);
                 }
-#pragma unroll
-                for (int d = 0; d < 4; ++d) {
-                  a0[d] = fmaf(p0[i], vx[d], a0[d]);
-                  a1[d] = fmaf(p1[i], vx[d], a1[d]);
-                }
+                a0[0] = fmaf(p0[i], vx0, a0[0]); a0[1] = fmaf(p0[i], vx1, a0[1]);
+                a0[2] = fmaf(p0[i], vx2, a0[2]); a0[3] = fmaf(p0[i], vx3, a0[3]);
+                a1[0] = fmaf(p1[i], vx0, a1[0]); a1[1] = fmaf(p1[i], vx1, a1[1]);
+                a1[2] = fmaf(p1[i], vx2, a1[2]); a1[3] = fmaf(p1[i], vx3, a1[3]);
               }
             }
             ring_done(c, n);
           }
           tr.mark(kTrMark, kSubBCAttn, l, t);
-#pragma unroll
-          for (int d = 0; d < 4; ++d) {
-            sm.u.att[warp][0][lane * 4 + d] = a0[d];
-            sm.u.att[warp][1][lane * 4 + d] = a1[d];
-          }
-          if (lane == 0) {
-            sm.u.att[warp][0][kHeadDim] = m0;
-            sm.u.att[warp][0][kHeadDim + 1] = l0;
-            sm.u.att[warp][1][kHeadDim] = m1;
-            sm.u.att[warp][1][kHeadDim + 1] = l1;
+          *reinterpret_cast<float4*>(&sm.u.att[warp][0][lane * 4]) = make_float4(a0[0], a0[1], a0[2], a0[3]);
+          *reinterpret_cast<float4*>(&sm.u.att[warp][1][lane * 4]) = make_float4(a1[0], a1[1], a1[2], a1[3]);
+          if (lane == 0 || lane == 16) {
+            sm.u.att[warp][lane >> 4][kHeadDim] = m;
+            sm.u.att[warp][lane >> 4][kHeadDim + 1] = lsum;
           }
           consumer_sync(kConsumerThreads);
           if (tid < 2 * kHeadDim) {
@@ -1008,15 +1094,20 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         // o_proj partial of this KV head's two Q heads (megakernel.cu:191-225)
         tr.mark(kTrMark, kSubBCComb, l, t);
         {
-          // K = 256 (two heads x 128): warp w owns the MMA k-step [16w, 16w+16);
-          // rows in padded 528-byte slots, four 16-row tiles per chunk.
-          uint32_t ob0 = 0u, ob1 = 0u;
-          if (lane < 8) {
-            const int k = 16 * warp + 2 * (lane & 3);
-            const float x0 = sm.attn[k], x1 = sm.attn[k + 1], x8 = sm.attn[k + 8], x9 = sm.attn[k + 9];
-            const uint32_t h0 = pack_bf2(x0, x1), h1 = pack_bf2(x8, x9);
-            ob0 = lane < 4 ? h0 : pack_bf2(x0 - bf_lo(h0), x1 - bf_hi(h0));
-            ob1 = lane < 4 ? h1 : pack_bf2(x8 - bf_lo(h1), x9 - bf_hi(h1));
+          // K = 256 (two heads x 128): warp w owns kOSteps MMA k-steps from
+          // 16*kOSteps*w; rows in padded 528-byte slots, four 16-row tiles per chunk.
+          uint32_t ob[kOSteps][2];
+#pragma unroll
+          for (int st = 0; st < kOSteps; ++st) {
+            ob[st][0] = 0u;
+            ob[st][1] = 0u;
+            if (lane < 8) {
+              const int k = 16 * (kOSteps * warp + st) + 2 * (lane & 3);
+              const float x0 = sm.attn[k], x1 = sm.attn[k + 1], x8 = sm.attn[k + 8], x9 = sm.attn[k + 9];
+              const uint32_t h0 = pack_bf2(x0, x1), h1 = pack_bf2(x8, x9);
+              ob[st][0] = lane < 4 ? h0 : pack_bf2(x0 - bf_lo(h0), x1 - bf_hi(h0));
+              ob[st][1] = lane < 4 ? h1 : pack_bf2(x8 - bf_lo(h1), x9 - bf_hi(h1));
+            }
           }
           for (int o0 = pl.oa; o0 < pl.ob; o0 += kORowsPerChunk) {
             const int nrows = min(pl.ob, o0 + kORowsPerChunk) - o0;
@@ -1026,33 +1117,52 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 #pragma unroll
             for (int tt = 0; tt < 4; ++tt) {
               const int rr = tt * 16 + tr16;
-              const uint32_t row = sa + (rr < nrows ? rr : 0) * kORowStride + (lane >> 4) * 16 + warp * 32;
-              uint32_t a0, a1, a2, a3;
-              ldsm_x4(row, a0, a1, a2, a3);
-              mma_bf16(d[tt], a0, a1, a2, a3, ob0, ob1);
+              const uint32_t row = sa + (rr < nrows ? rr : 0) * kORowStride + (lane >> 4) * 16 +
+                                   warp * (kOSteps * 32);
+#pragma unroll
+              for (int st = 0; st < kOSteps; ++st) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(row + st * 32, a0, a1, a2, a3);
+                mma_bf16(d[tt], a0, a1, a2, a3, ob[st][0], ob[st][1]);
+              }
             }
             ring_done(c, n);
 #pragma unroll
             for (int tt = 0; tt < 4; ++tt) stash_tile(xred, tt, d[tt]);
             consumer_sync(kConsumerThreads);
-            if (tid < nrows) red_add_f32(&ws->acc_mid[l][o0 + tid], sum_warps(xred, tid));
+            if (tid < nrows) {
+              bool bad = false;
+              red_add_u64(&ws->acc_mid[l][o0 + tid], acc_term(sum_warps(xred, tid), bad));
+              if (bad) raise_error(c, kErrRange, l, kStBC, t);
+            }
             consumer_sync(kConsumerThreads);
           }
         }
-        transition_publish(tr, &ws->sync[l][1][0], l, kStBC, t);
+        tr.mark(kTrPublish, kStBC, l, t);
+        // A later token of this launch re-reads this head's K/V rows through the
+        // bulk-copy engine: publish the append (K writer and V writer).
+        if (p.n_tokens > 1 && pl.c == 0 && (warp == 2 || warp == 3)) {
+          __syncwarp();
+          if (lane == 0) release_add(&ws->kv_ready[l][h][0], 1u);
+        }
       }
 
       // ================= DE: post norm, SwiGLU rows, down partial ===============
       // the next layer's input-norm weights, one stage ahead of their use
-      if (l + 1 < le) load_norm_k(lwt(c, l + 1, kWNorm), nwA);
-      transition_wait(c, tr, &ws->sync[l][1][0], tgtBC, l, kStDE, t);
+      if (l + 1 < le) wA = load_w4(lwt(c, l + 1, kWNorm));
+      tr.mark(kTrWaitBegin, kStDE, l, t);
       {
-        const float m0 = sm.r[tid] + __ldcg(&ws->acc_mid[l][tid]);
-        const float m1 = sm.r[tid + kConsumerThreads] + __ldcg(&ws->acc_mid[l][tid + kConsumerThreads]);
-        sm.rmid[tid] = m0;
-        sm.rmid[tid + kConsumerThreads] = m1;
-        const float tot = block_sumsq(m0, m1, sm.red, flip);
-        build_bfrag(sm.rmid, rsqrtf(tot * (1.0f / kHidden) + kEps), nwD, bfr);
+        float a[4];
+        acc_wait4(c, &ws->acc_mid[l][0], 1, static_cast<uint32_t>(kNKV), a, l, kStDE, t);
+        tr.mark(kTrWaitEnd, kStDE, l, t);
+        const float4 rv = *reinterpret_cast<const float4*>(&sm.r[e0]);
+        float mres[4] = {rv.x + a[0], rv.y + a[1], rv.z + a[2], rv.w + a[3]};
+        *reinterpret_cast<float4*>(&sm.rmid[e0]) = make_float4(mres[0], mres[1], mres[2], mres[3]);
+        const float tot = block_sum(mres[0] * mres[0] + mres[1] * mres[1] + mres[2] * mres[2] + mres[3] * mres[3],
+                                    sm.red, flip);
+        store_x(sm, mres, rsqrtf(tot * (1.0f / kHidden) + kEps), wD);
+        consumer_sync(kConsumerThreads);
+        load_bfrag(sm, bfr);
       }
       tr.mark(kTrMark, kSubDENorm, l, t);
       const int nj = pl.jb - pl.ja;
@@ -1084,11 +1194,10 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         sm.m[tid] = g / (1.0f + expf(-g)) * u;  // silu (config.cuh:177-179) * up
       }
       consumer_sync(kConsumerThreads);
-      if (fused) {
-        // down-proj partial over this CTA's intermediate rows: warp w owns
-        // outputs [64w, 64w+64), two per lane (megakernel.cu:53-90, split by K)
-        const int col = warp * 64 + lane * 2;
-        float pa = 0.f, pb = 0.f;
+      if constexpr (fused) {
+        // down-proj partial over this CTA's intermediate rows: thread i owns
+        // output columns [4i, 4i+4) (megakernel.cu:53-90, split by K)
+        float pa[4] = {0.f, 0.f, 0.f, 0.f};
         for (int jb0 = 0; jb0 < nj; jb0 += 3 * kRowsPerChunk1024) {
           const int nd = min(3, (nj - jb0 + kRowsPerChunk1024 - 1) / kRowsPerChunk1024);
           uint32_t sa[3];
@@ -1097,20 +1206,45 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             const int js = jb0 + i * kRowsPerChunk1024;
             const int j1 = min(nj, js + kRowsPerChunk1024);
             for (int jj = js; jj < j1; ++jj) {
-              const uint32_t w = lds32(sa[i] + (jj - js) * 2048 + col * 2);
+              const uint2 w = lds64(sa[i] + (jj - js) * 2048 + e0 * 2);
               const float mj = sm.m[jj];
-              pa = fmaf(bf_lo(w), mj, pa);
-              pb = fmaf(bf_hi(w), mj, pb);
+              pa[0] = fmaf(bf_lo(w.x), mj, pa[0]);
+              pa[1] = fmaf(bf_hi(w.x), mj, pa[1]);
+              pa[2] = fmaf(bf_lo(w.y), mj, pa[2]);
+              pa[3] = fmaf(bf_hi(w.y), mj, pa[3]);
             }
           }
           ring_done_all(c, n, nd);
         }
         tr.mark(kTrMark, kSubDEDown, l, t);
-        red_add_v2_f32(&ws->acc_down[l][col], pa, pb);
-        transition_publish(tr, &ws->sync[l][2][0], l, kStDE, t);
+        {
+          // cluster pre-reduction: slice [kSlice r, kSlice (r + 1)) of every
+          // CTA's partial goes to cluster rank r (distributed shared memory),
+          // which adds the kCluster slices into acc_down (kCluster-fold fewer
+          // atomics).
+          const uint32_t rank = cluster_ctarank();
+          float(*rx)[kSlice] = cluster_rx(sm);
+          st_cluster_v4(mapa_shared(smem_addr(&rx[rank][e0 % kSlice]), static_cast<uint32_t>(e0 / kSlice)), pa[0],
+                        pa[1], pa[2], pa[3]);
+          consumer_sync(kConsumerThreads);
+          if (tid < kCluster) mbar_arrive_cluster(mapa_shared(smem_addr(&sm.rxbar), static_cast<uint32_t>(tid)));
+          cluster_rx_wait(c, xph, l, t);
+          xph ^= 1u;
+          bool bad = false;
+          uint64_t* dst = &ws->acc_down[l][(c.cta / kCluster) % kDownCopies][rank * kSlice];
+#pragma unroll
+          for (int i = tid; i < kSlice; i += kConsumerThreads) {
+            float v = 0.f;
+#pragma unroll
+            for (int q = 0; q < kCluster; ++q) v += rx[q][i];
+            red_add_u64(dst + i, acc_term(v, bad));
+          }
+          if (bad) raise_error(c, kErrRange, l, kStDE, t);
+        }
+        tr.mark(kTrPublish, kStDE, l, t);
       } else {
         // reference layout: publish the SwiGLU vector, then whole down rows
-        for (int j = tid; j < nj; j += kConsumerThreads) p.mlp_out[pl.ja + j] = sm.m[j];
+        if (tid < nj) p.mlp_out[pl.ja + tid] = sm.m[tid];
         transition_publish(tr, &ws->sync[l][2][0], l, kStDE, t);
         transition_wait(c, tr, &ws->sync[l][2][0], tgtG, l, kStE, t);
         for (int i = tid; i < kInter; i += kConsumerThreads) sm.u.x[i] = __ldcg(p.mlp_out + i);
@@ -1118,25 +1252,21 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         for (int d0 = pl.da; d0 < pl.db; d0 += kDownRowsPerChunk) {
           const int d1 = min(pl.db, d0 + kDownRowsPerChunk);
           const uint32_t sa = ring_wait(c, n, l, 6, t, &tr);
-          const int row = warp / 3, third = warp % 3;
-          if (warp < 15 && d0 + row < d1) {
+          for (int row = warp; row < d1 - d0; row += kConsumerWarps) {
             float acc = 0.f;
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              const int e = third * kHidden + lane * 8 + g * 256;
+#pragma unroll 4
+            for (int g = 0; g < kInter / 256; ++g) {
+              const int e = lane * 8 + g * 256;
               const uint4 w = lds128(sa + row * (kInter * 2) + e * 2);
               acc += dot8(w, sm.u.x + e);
             }
             acc = warp_sum(acc);
-            if (lane == 0) sm.dpart[row][third] = acc;
+            if (lane == 0) {
+              const int d = d0 + row;
+              ws->resid[d] = sm.rmid[d] + acc;
+            }
           }
           ring_done(c, n);
-          consumer_sync(kConsumerThreads);
-          if (tid < d1 - d0) {
-            const int d = d0 + tid;
-            ws->resid[d] = sm.rmid[d] + (sm.dpart[tid][0] + sm.dpart[tid][1] + sm.dpart[tid][2]);
-          }
-          consumer_sync(kConsumerThreads);
         }
         transition_publish(tr, &ws->sync[l][3][0], l, kStE, t);
       }
@@ -1146,37 +1276,42 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     uint4 fwv[4];
     load_norm_w((p.flags & kFlagSkipFinalNorm) ? nullptr : p.final_norm, fwv);
     if (le > lb) {
-      transition_wait(c, tr, &ws->sync[le - 1][fused ? 2 : 3][0], tgtG, le - 1, kStLM, t);
-      if (fused) {
-        r0 = sm.rmid[tid] + __ldcg(&ws->acc_down[le - 1][tid]);
-        r1 = sm.rmid[tid + kConsumerThreads] + __ldcg(&ws->acc_down[le - 1][tid + kConsumerThreads]);
+      if constexpr (fused) {
+        tr.mark(kTrWaitBegin, kStLM, le - 1, t);
+        float d[4];
+        acc_wait4(c, &ws->acc_down[le - 1][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster), d, le - 1, kStLM,
+                  t);
+        tr.mark(kTrWaitEnd, kStLM, le - 1, t);
+        const float4 rm = *reinterpret_cast<const float4*>(&sm.rmid[e0]);
+        r[0] = rm.x + d[0]; r[1] = rm.y + d[1]; r[2] = rm.z + d[2]; r[3] = rm.w + d[3];
       } else {
-        r0 = __ldcg(&ws->resid[tid]);
-        r1 = __ldcg(&ws->resid[tid + kConsumerThreads]);
+        transition_wait(c, tr, &ws->sync[le - 1][3][0], tgtG, le - 1, kStLM, t);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(ws->resid) + tid);
+        r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
       }
     }
-    sm.r[tid] = r0;
-    sm.r[tid + kConsumerThreads] = r1;
-    if (c.cta == 0 && p.residual_out != nullptr && t == p.n_tokens - 1) {
-      p.residual_out[tid] = r0;
-      p.residual_out[tid + kConsumerThreads] = r1;
-    }
+    *reinterpret_cast<float4*>(&sm.r[e0]) = make_float4(r[0], r[1], r[2], r[3]);
+    if (c.cta == 0 && p.residual_out != nullptr && t == p.n_tokens - 1)
+      *reinterpret_cast<float4*>(p.residual_out + e0) = make_float4(r[0], r[1], r[2], r[3]);
     float bv = -INFINITY;
     int bi = INT_MAX;
     if (p.flags & kFlagLmHead) {
-      const float tot = block_sumsq(r0, r1, sm.red, flip);
+      const float tot = block_sum(r[0] * r[0] + r[1] * r[1] + r[2] * r[2] + r[3] * r[3], sm.red, flip);
       const float rstd = (p.flags & kFlagSkipFinalNorm) ? 1.0f : rsqrtf(tot * (1.0f / kHidden) + kEps);
       xr_from(sm.r, rstd, fwv, xr);
       for (int v0 = pl.va; v0 < pl.vb; v0 += kRowsPerChunk1024) {
         const int v1 = min(pl.vb, v0 + kRowsPerChunk1024);
         const uint32_t sa = ring_wait(c, n, -1, 8, t, &tr);
-        const int row = v0 + warp;
-        if (row < v1) {
-          const float v = warp_sum(dot_row1024(sa + warp * 2048, xr, lane));
-          if (lane == 0 && p.logits != nullptr) p.logits[row] = v;
-          if (better(v, row, bv, bi)) {
-            bv = v;
-            bi = row;
+#pragma unroll
+        for (int i = 0; i < kRowsPerChunk1024 / kConsumerWarps; ++i) {
+          const int row = v0 + warp + i * kConsumerWarps;
+          if (row < v1) {
+            const float v = warp_sum(dot_row1024(sa + (warp + i * kConsumerWarps) * 2048, xr, lane));
+            if (lane == 0 && p.logits != nullptr) p.logits[row] = v;
+            if (better(v, row, bv, bi)) {
+              bv = v;
+              bi = row;
+            }
           }
         }
         ring_done(c, n);
@@ -1213,15 +1348,20 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     const int last_state = sm.is_last;
     consumer_sync(kConsumerThreads);
     tr.mark(kTrMark, kStEnd, 0, t);
+    tr.flush();
     if (last_state < 0) return;
     if (last_state) {
       int best = -1;
       if (p.flags & kFlagLmHead) {
         float v = -INFINITY;
         int i = INT_MAX;
-        if (tid < G) {
-          v = __ldcg(&ws->cand_val[tid]);
-          i = __ldcg(&ws->cand_idx[tid]);
+        for (int k = tid; k < G; k += kConsumerThreads) {
+          const float cv = __ldcg(&ws->cand_val[k]);
+          const int ci = __ldcg(&ws->cand_idx[k]);
+          if (better(cv, ci, v, i)) {
+            v = cv;
+            i = ci;
+          }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -1249,15 +1389,14 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         }
       }
       // the last two layers' accumulators (earlier ones were cleared on the way)
-      for (int i = tid; i < kHidden; i += kConsumerThreads) {
-        for (int l = max(lb, le - 2); l < le; ++l) {
-          ws->acc_mid[l][i] = 0.f;
-          ws->acc_down[l][i] = 0.f;
-        }
+      for (int l = max(lb, le - 2); l < le; ++l) {
+        acc_clear4(&ws->acc_mid[l][0]);
+        for (int q = 0; q < kDownCopies; ++q) acc_clear4(&ws->acc_down[l][q][0]);
       }
       const bool last_tok = t == p.n_tokens - 1;
       if (last_tok) {
         for (int i = tid; i < kMaxLayers * 4; i += kConsumerThreads) ws->sync[i >> 2][i & 3][0] = 0u;
+        for (int i = tid; i < kMaxLayers * kNKV; i += kConsumerThreads) ws->kv_ready[i / kNKV][i % kNKV][0] = 0u;
         for (int i = tid; i < kMaxLayers * kNKV; i += kConsumerThreads) ws->att_sync[i / kNKV][i % kNKV][0] = 0u;
       }
       consumer_sync(kConsumerThreads);
@@ -1285,6 +1424,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 }
 
 
+template <bool kFused, bool kTraced>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem* sm = reinterpret_cast<Smem*>(smem_raw);
@@ -1299,6 +1439,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     cl = pos + 1;
   }
 
+  int misaligned = 0;
   for (int i = threadIdx.x; i < kMaxLayers * 12; i += blockDim.x) {
     const int l = i / 12, f = i % 12;
     const __nv_bfloat16* v = nullptr;
@@ -1306,13 +1447,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
       if (f < 11) v = reinterpret_cast<const __nv_bfloat16* const*>(p.layers + l)[f];
       else if (p.down_t != nullptr) v = p.down_t[l];
     }
+    misaligned |= (reinterpret_cast<uintptr_t>(v) & 15u) != 0u;
     sm->lwp[l][f] = v;
   }
+  // every weight and vector is read with vector loads or bulk copies: 16-byte alignment
+  misaligned |= ((reinterpret_cast<uintptr_t>(p.final_norm) | reinterpret_cast<uintptr_t>(p.input_residual) |
+                  reinterpret_cast<uintptr_t>(p.residual_out)) & 15u) != 0u;
+  misaligned = __syncthreads_or(misaligned);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(&sm->full[s], 1);
       mbar_init(&sm->empty[s], kConsumerWarps);
     }
+    mbar_init(&sm->rxbar, kCluster);
     sm->abort = 0;
     sm->is_last = 0;
     fence_mbar_init();
@@ -1326,30 +1473,43 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
   // Argument guard (uniform over the grid, before any wait).
   if (token < 0 || token >= kVocab || pos < 0 || pos + p.n_tokens > p.max_seq || cl < 1 ||
       last_cl > p.max_seq || p.grid != static_cast<int>(gridDim.x) || p.grid > kMaxGrid ||
-      p.group_size * kNKV > p.grid || splits < 1 || splits > kMaxSplits ||
-      (splits > 1 && splits > p.group_size)) {
+      p.group_size * kNKV > p.grid || p.grid % kCluster != 0 || splits < 1 || splits > kMaxSplits ||
+      (splits > 1 && splits > p.group_size) || misaligned) {
     if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(c, kErrBadArgs, -1, -1, -1);
     return;
   }
 
+  // Every CTA of the cluster has initialised its barriers before any remote
+  // arrival, and none exits while a peer may still write into its shared memory.
+  cluster_sync_all();
   const Plan pl = make_plan(blockIdx.x, p.grid, p.group_size, kVocab);
   if (threadIdx.x >= kConsumerThreads) {
-    producer_run(p, pl, c, pos, cl, splits);
+    producer_run<kFused, kTraced>(p, pl, c, pos, cl, splits);
   } else {
-    consumer_run(p, pl, c, token, pos, cl, splits, tag0);
+    consumer_run<kFused, kTraced>(p, pl, c, token, pos, cl, splits, tag0);
   }
+  cluster_sync_all();
 }
 
 // ---- host-side launch ----------------------------------------------------------
+// The four instantiations: transposed-down (fused) or reference-layout
+// schedule, with or without trace stamps.
+template <bool kFused, bool kTraced>
+cudaError_t set_smem_attr() {
+  return cudaFuncSetAttribute(decode_kernel<kFused, kTraced>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kSmemBytes));
+}
+
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream) {
   static int configured[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 64 && !configured[dev]) {
-    e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) return e;
+    if ((e = set_smem_attr<true, false>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<false, false>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<true, true>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<false, true>()) != cudaSuccess) return e;
     configured[dev] = 1;
   }
   cudaLaunchConfig_t cfg = {};
@@ -1357,12 +1517,22 @@ cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream) {
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = kCluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_kernel, p);
+  cfg.numAttrs = 2;
+  const bool fused = p.down_t != nullptr, traced = p.trace != nullptr;
+  if (fused) {
+    return traced ? cudaLaunchKernelEx(&cfg, decode_kernel<true, true>, p)
+                  : cudaLaunchKernelEx(&cfg, decode_kernel<true, false>, p);
+  }
+  return traced ? cudaLaunchKernelEx(&cfg, decode_kernel<false, true>, p)
+                : cudaLaunchKernelEx(&cfg, decode_kernel<false, false>, p);
 }
 
 size_t decode_smem_bytes() { return kSmemBytes; }

@@ -2,7 +2,7 @@
 // workspace in a file-scope device array instead of a lazily cudaMalloc'd
 // buffer, for callers that must not allocate device memory at any call.
 //
-//  * capacity: kNoAllocScratchBytes (2 MiB) per device; a build whose
+//  * capacity: kNoAllocScratchBytes (4 MiB) per device; a build whose
 //    Workspace is larger is rejected at the call (cudaErrorInvalidValue and
 //    one line on stderr naming both sizes);
 //  * set-up, once per device on the first call: cudaGetSymbolAddress of the
@@ -24,7 +24,7 @@
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

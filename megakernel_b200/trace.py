@@ -1,9 +1,11 @@
 """Stage timeline of the decode kernel from its in-kernel ``%globaltimer`` stamps.
 
-With a trace buffer, consumer thread 0 of every CTA stamps each grid-transition
-wait (begin/end), each publish and the token start/LM-head end/token end
-(codes in ``mkb_decode_args.trace``). This module launches the kernel with such a
-buffer and reduces the stamps to per-stage wait and compute times.
+With a trace buffer, consumer thread 0 of every CTA stamps each cross-CTA wait
+(begin/end), each publish, the sub-stage boundaries and the token start/LM-head
+end/token end (codes in ``mkb_decode_args.trace``). Stamps are staged in shared
+memory and cover layers 8-15 plus the token-level marks. This module launches
+the kernel with such a buffer and reduces the stamps to per-stage wait and
+compute times.
 
     python -m megakernel_b200.trace [--tokens N] [--position P] [--reference-layout]
 
@@ -136,6 +138,22 @@ def summarize(per_cta) -> dict:
             name = STAGE_NAMES.get(cur[1], f"mark{cur[1]}")
             label = f"{KIND_NAMES[cur[0]]}:{name}" if cur[0] != 3 else name
             seg[label].append(cur[4] - prev[4])
+    # exchange latency: last publish of a stage over all CTAs -> each CTA's end of
+    # the wait on that stage (DE of layer l feeds A of l+1 and the LM head; BC
+    # feeds DE of the same layer)
+    last_pub = defaultdict(int)
+    for recs in per_cta:
+        for kind, st, layer, tok, t in recs:
+            if kind == 2 and st in (1, 2):
+                last_pub[(st, layer, tok)] = max(last_pub[(st, layer, tok)], t)
+    xlat = defaultdict(list)
+    for recs in per_cta:
+        for kind, st, layer, tok, t in recs:
+            if kind != 1:
+                continue
+            src = (2, layer - 1, tok) if st == 0 else (1, layer, tok) if st == 2 else (2, layer, tok) if st == 4 else None
+            if src in last_pub:
+                xlat[st].append(t - last_pub[src])
     med = lambda xs: statistics.median(xs) / 1000.0 if xs else None  # noqa: E731
     mean = lambda xs: statistics.fmean(xs) / 1000.0 if xs else None  # noqa: E731
     span = max(r[-1][4] for r in per_cta if r) - t0
@@ -144,6 +162,7 @@ def summarize(per_cta) -> dict:
         "token_us_max": max(token_ns) / 1000.0 if token_ns else None,
         "layer_period_us_median": med(layer_period),
         "lm_head_us_median": med(lm_ns),
+        "exchange_us_median": {STAGE_NAMES[k]: med(v) for k, v in xlat.items()},
         "segments": {k: {"mean_us": statistics.fmean(v) / 1000.0, "median_us": statistics.median(v) / 1000.0,
                          "count": len(v)} for k, v in seg.items()},
         "stages": {STAGE_NAMES[s]: {"wait_us_mean": mean(waits[s]), "wait_us_median": med(waits[s]),
@@ -161,6 +180,9 @@ def format_summary(s: dict) -> str:
         f = lambda v: f"{v:10.3f}" if v is not None else f"{'-':>10s}"  # noqa: E731
         lines.append(f"{name:16s} {f(d['wait_us_mean'])} {f(d['wait_us_median'])} "
                      f"{f(d['compute_us_mean']):>13s} {f(d['compute_us_median']):>12s}")
+    if s.get("exchange_us_median"):
+        lines.append("exchange latency (last publish over all CTAs -> wait end), median: " +
+                     ", ".join(f"{k} {v:.3f} us" for k, v in s["exchange_us_median"].items() if v is not None))
     lines.append("segments (time since the CTA's previous stamp, labelled by the later stamp):")
     for k, d in sorted(s.get("segments", {}).items(), key=lambda kv: -kv[1]["mean_us"] * kv[1]["count"]):
         lines.append(f"  {k:28s} mean {d['mean_us']:8.3f} us  median {d['median_us']:8.3f} us  n={d['count']}")
@@ -198,7 +220,7 @@ def main():
         print("plain launches done")
         return
     prod = getattr(td, "producer_records", None)
-    if prod:
+    if prod and any(prod):
         waits = []
         issues = []
         for recs in prod:
