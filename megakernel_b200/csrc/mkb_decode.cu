@@ -951,23 +951,36 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             const int k1 = min(kb, k0 + kKeysPerChunk);
             const int kw = k0 + warp * kKeysPerWarp;  // this warp's first key
             const uint32_t sa = ring_wait(c, n, l, 1, t, &tr);
+            // The producer skips row `pos` (the key appended this step): the warp
+            // that owns it writes the rotated K and the V row into the slot, so
+            // that every key is read the same way.
+            if (pos >= kw && pos < kw + kKeysPerWarp && pos < k1) {
+              const float4 kn = *reinterpret_cast<const float4*>(&sm.knew[lane * 4]);
+              const float4 vn = *reinterpret_cast<const float4*>(&sm.vnew[lane * 4]);
+              const uint32_t row = sa + (pos - k0) * (kHeadDim * 2) + lane * 8;
+              asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(row), "r"(pack_bf2(kn.x, kn.y)),
+                           "r"(pack_bf2(kn.z, kn.w)) : "memory");
+              asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(row + kSlotBytes / 2), "r"(pack_bf2(vn.x, vn.y)),
+                           "r"(pack_bf2(vn.z, vn.w)) : "memory");
+              fence_proxy_async_shared();  // before the slot is handed back to the bulk-copy engine
+              __syncwarp();
+            }
+            // all eight key rows of this warp (rows past k1 are in the slot but masked)
+            uint2 kr[kKeysPerWarp];
+#pragma unroll
+            for (int i = 0; i < kKeysPerWarp; ++i) kr[i] = lds64(sa + (kw + i - k0) * (kHeadDim * 2) + lane * 8);
             float v[16];
 #pragma unroll
             for (int i = 0; i < kKeysPerWarp; ++i) {
-              const int kk = kw + i;
-              float kx0 = 0.f, kx1 = 0.f, kx2 = 0.f, kx3 = 0.f;
-              if (kk < k1) {
-                if (kk == pos) {
-                  const float4 kn = *reinterpret_cast<const float4*>(&sm.knew[lane * 4]);
-                  kx0 = kn.x; kx1 = kn.y; kx2 = kn.z; kx3 = kn.w;
-                } else {
-                  const uint2 u = lds64(sa + (kk - k0) * (kHeadDim * 2) + lane * 8);
-                  kx0 = bf_lo(u.x); kx1 = bf_hi(u.x); kx2 = bf_lo(u.y); kx3 = bf_hi(u.y);
-                }
-              }
+              const float kx0 = bf_lo(kr[i].x), kx1 = bf_hi(kr[i].x), kx2 = bf_lo(kr[i].y), kx3 = bf_hi(kr[i].y);
               v[i] = fmaf(q0[3], kx3, fmaf(q0[2], kx2, fmaf(q0[1], kx1, q0[0] * kx0)));
               v[8 + i] = fmaf(q1[3], kx3, fmaf(q1[2], kx2, fmaf(q1[1], kx1, q1[0] * kx0)));
             }
+            // value rows, loaded while the scores are reduced
+            uint2 vr[kKeysPerWarp];
+#pragma unroll
+            for (int i = 0; i < kKeysPerWarp; ++i)
+              vr[i] = lds64(sa + kSlotBytes / 2 + (kw + i - k0) * (kHeadDim * 2) + lane * 8);
             // reduce-scatter butterfly: 16 -> 8 -> 4 -> 2 -> 1 values, then the last lane bit
 #pragma unroll
             for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
@@ -989,8 +1002,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             const float mnew = fmaxf(m, mx);
             float sc = 1.f, pk = 0.f;
             if (mnew > -INFINITY) {
-              sc = exp2f(m - mnew);
-              pk = s > -INFINITY ? exp2f(s - mnew) : 0.f;
+              sc = ex2_approx(m - mnew);
+              pk = s > -INFINITY ? ex2_approx(s - mnew) : 0.f;
             }
             float ps = pk;
             ps += __shfl_xor_sync(0xffffffffu, ps, 2);
@@ -1020,21 +1033,14 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             }
 #pragma unroll
             for (int i = 0; i < kKeysPerWarp; ++i) {
-              const int kk = kw + i;
-              if (kk < k1) {
-                float vx0, vx1, vx2, vx3;
-                if (kk == pos) {
-                  const float4 vn = *reinterpret_cast<const float4*>(&sm.vnew[lane * 4]);
-                  vx0 = vn.x; vx1 = vn.y; vx2 = vn.z; vx3 = vn.w;
-                } else {
-                  const uint2 u = lds64(sa + kSlotBytes / 2 + (kk - k0) * (kHeadDim * 2) + lane * 8);
-                  vx0 = bf_lo(u.x); vx1 = bf_hi(u.x); vx2 = bf_lo(u.y); vx3 = bf_hi(u.y);
-                }
-                a0[0] = fmaf(p0[i], vx0, a0[0]); a0[1] = fmaf(p0[i], vx1, a0[1]);
-                a0[2] = fmaf(p0[i], vx2, a0[2]); a0[3] = fmaf(p0[i], vx3, a0[3]);
-                a1[0] = fmaf(p1[i], vx0, a1[0]); a1[1] = fmaf(p1[i], vx1, a1[1]);
-                a1[2] = fmaf(p1[i], vx2, a1[2]); a1[3] = fmaf(p1[i], vx3, a1[3]);
-              }
+              // rows past k1 carry weight 0; select so that stale slot contents never reach the sums
+              const bool ok = kw + i < k1;
+              const float vx0 = ok ? bf_lo(vr[i].x) : 0.f, vx1 = ok ? bf_hi(vr[i].x) : 0.f;
+              const float vx2 = ok ? bf_lo(vr[i].y) : 0.f, vx3 = ok ? bf_hi(vr[i].y) : 0.f;
+              a0[0] = fmaf(p0[i], vx0, a0[0]); a0[1] = fmaf(p0[i], vx1, a0[1]);
+              a0[2] = fmaf(p0[i], vx2, a0[2]); a0[3] = fmaf(p0[i], vx3, a0[3]);
+              a1[0] = fmaf(p1[i], vx0, a1[0]); a1[1] = fmaf(p1[i], vx1, a1[1]);
+              a1[2] = fmaf(p1[i], vx2, a1[2]); a1[3] = fmaf(p1[i], vx3, a1[3]);
             }
             ring_done(c, n);
           }
@@ -1055,7 +1061,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) {
               const float mw = sm.u.att[w][hh][kHeadDim];
-              const float f = mw > -INFINITY ? exp2f(mw - M) : 0.f;
+              const float f = mw > -INFINITY ? ex2_approx(mw - M) : 0.f;
               L = fmaf(sm.u.att[w][hh][kHeadDim + 1], f, L);
               O = fmaf(sm.u.att[w][hh][d], f, O);
             }
@@ -1082,7 +1088,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             float L = 0.f, O = 0.f;
             for (int s = 0; s < splits; ++s) {
               const float ms = __ldcg(&ws->att_part[h][s][hh][kHeadDim]);
-              const float f = ms > -INFINITY ? exp2f(ms - M) : 0.f;
+              const float f = ms > -INFINITY ? ex2_approx(ms - M) : 0.f;
               L = fmaf(__ldcg(&ws->att_part[h][s][hh][kHeadDim + 1]), f, L);
               O = fmaf(__ldcg(&ws->att_part[h][s][hh][d]), f, O);
             }
