@@ -1506,32 +1506,63 @@ cudaError_t set_smem_attr() {
                               static_cast<int>(kSmemBytes));
 }
 
+// Largest grid of kCluster-CTA clusters that can be resident at once (each CTA
+// holds a whole SM's shared memory).
+template <bool kFused, bool kTraced>
+cudaError_t resident_ctas(int grid, int* out) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, decode_kernel<kFused, kTraced>, &cfg);
+  *out = clusters * kCluster;
+  return e;
+}
+
+// The CTAs wait on one another, so the whole grid must be resident: checked
+// once per device against the cluster occupancy (the launch is refused with
+// cudaErrorCooperativeLaunchTooLarge otherwise, as a cooperative launch would be).
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream) {
   static int configured[64] = {0};
+  static int resident[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 64 && !configured[dev]) {
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
     if ((e = set_smem_attr<true, false>()) != cudaSuccess) return e;
     if ((e = set_smem_attr<false, false>()) != cudaSuccess) return e;
     if ((e = set_smem_attr<true, true>()) != cudaSuccess) return e;
     if ((e = set_smem_attr<false, true>()) != cudaSuccess) return e;
+    int r[4];
+    if ((e = resident_ctas<true, false>(p.grid, &r[0])) != cudaSuccess) return e;
+    if ((e = resident_ctas<false, false>(p.grid, &r[1])) != cudaSuccess) return e;
+    if ((e = resident_ctas<true, true>(p.grid, &r[2])) != cudaSuccess) return e;
+    if ((e = resident_ctas<false, true>(p.grid, &r[3])) != cudaSuccess) return e;
+    resident[dev] = min(min(r[0], r[1]), min(r[2], r[3]));
     configured[dev] = 1;
   }
+  if (p.grid > resident[dev]) return cudaErrorCooperativeLaunchTooLarge;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = kCluster;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 1;
   const bool fused = p.down_t != nullptr, traced = p.trace != nullptr;
   if (fused) {
     return traced ? cudaLaunchKernelEx(&cfg, decode_kernel<true, true>, p)
