@@ -81,33 +81,71 @@ def synthetic_weights(seed: int, device):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during a region."""
-
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, power and clock-event reasons sampled every 5 ms (NVML, read only)
+    while the timed region runs; falls back to nvidia-smi at 200 ms without NVML."""
 
     def __init__(self, index: int):
         self.index = index
+        self.samples = []   # (sm_mhz, max_mhz, power_w, reasons)
+        self.stop = threading.Event()
+        self.thread = None
         self.proc = None
         self.lines = []
 
     def __enter__(self):
         try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            names = {pynvml.nvmlClocksEventReasonHwSlowdown: "hw_slowdown",
+                     pynvml.nvmlClocksEventReasonHwThermalSlowdown: "hw_thermal_slowdown",
+                     pynvml.nvmlClocksEventReasonSwThermalSlowdown: "sw_thermal_slowdown",
+                     pynvml.nvmlClocksEventReasonSwPowerCap: "sw_power_cap"}
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def run():
+                while not self.stop.is_set():
+                    try:
+                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                        bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((sm, mx, pw, [n for b, n in names.items() if bits & b]))
+                    except Exception:
+                        pass
+                    time.sleep(0.005)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            pass
+        try:
+            fields = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                      "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                      "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
         except Exception:
             self.proc = None
         return self
 
     def _read(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                self.samples.append((float(p[1]), float(p[2]), float(p[3]),
+                                     [n for n, v in zip(names, p[5:9]) if v.lower() == "active"]))
+            except ValueError:
+                continue
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -115,26 +153,16 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            p = [x.strip() for x in ln.split(",")]
-            if len(p) < 9:
-                continue
-            try:
-                sm.append(float(p[1]))
-                mx.append(float(p[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, p[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = sorted({r for s in self.samples for r in s[3]})
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples),
+                "power_w_max": max(s[2] for s in self.samples), "reasons": reasons, "samples": len(self.samples)}
 
 
 def measured_peak():
@@ -145,11 +173,13 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def ncu_traffic_per_token():
-    """DRAM bytes per token of decode_kernel from the committed ncu summary, if any."""
+def ncu_traffic():
+    """DRAM bytes of one decode_kernel token from the committed ncu capture:
+    (bytes at the captured cache length, that length, KV bytes per extra position)."""
     try:
         with open(os.path.join(ROOT, "profiles", "decode_kernel_traffic.json")) as f:
-            return float(json.load(f)["dram_bytes_per_token"])
+            d = json.load(f)
+        return float(d["dram_bytes_per_token"]), int(d["cache_len"]), float(d["kv_bytes_per_position"])
     except Exception:
         return None
 
@@ -303,8 +333,13 @@ def main():
     per_launch_s = dev_ms / 1000.0 / launches
     peak, peak_kind = measured_peak()
     achieved = per_launch_bytes / per_launch_s / 1e9
-    traffic_tok = ncu_traffic_per_token()
     toks_per_launch = steps / launches
+    # ncu traffic of one captured token, scaled to this launch's cache lengths
+    traffic = None
+    tr = ncu_traffic()
+    if tr is not None:
+        tok_bytes, cl0, per_pos = tr
+        traffic = sum(tok_bytes + per_pos * (PROMPT + (i % span) + 1 - cl0) for i in range(steps)) / launches
     if rank == 0:
         line = {
             "metric": METRIC, "value": world * steps / (dev_ms / 1000.0), "unit": "tok/s", "n_gpus": world,
@@ -321,7 +356,7 @@ def main():
                     "api": "mkb_engine_step (graph replay, host token in/out)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
-                         "traffic": (traffic_tok * toks_per_launch) if traffic_tok else None,
+                         "traffic": traffic,
                          "kernel": "decode_kernel", "algorithmic_bytes_per_launch": per_launch_bytes},
             "gpu_launches": launches,
             "clocks": clk.summary(),
