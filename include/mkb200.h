@@ -74,8 +74,8 @@ typedef struct mkb_decode_args {
   const void* lm_head;         /* device [vocab, 1024] (tied: == embed) */
   const void* final_norm;      /* device [1024] */
   const void* layers;          /* device LayerWeights[n_layers] */
-  const void* down_t;          /* device array of n_layers pointers to [3072, 1024]
-                                  transposed down weights, or NULL */
+  const void* down_t;          /* device array of n_layers pointers to [2][3072][512]
+                                  transposed down weights (mkb_transpose_down), or NULL */
   const void* cos_table;       /* device [max_seq, 128] */
   const void* sin_table;
   int rope_fp32;               /* 1: FP32 tables, 0: BF16 */
@@ -129,7 +129,9 @@ cudaError_t mkb_default_workspace(int device, void** out);
 const char* mkb_error_name(uint32_t code);
 
 /* ---- layout helper -------------------------------------------------------------
- * down [1024, 3072] -> down_t [3072, 1024] (BF16), used by the engine. */
+ * down [1024, 3072] -> down_t [2][3072][512] (BF16): the transpose with its
+ * 1024 output columns split into two contiguous 512-column blocks (one per CTA
+ * of a cluster pair), the layout mkb_decode_args.down_t expects. */
 cudaError_t mkb_transpose_down(const void* down, void* down_t, cudaStream_t stream);
 
 /* ---- resident engine -------------------------------------------------------------

@@ -66,13 +66,14 @@ constexpr int kAccShift = 28;
 constexpr uint64_t kAccBias = 1ull << 47;
 constexpr uint64_t kAccOne = 1ull << 56;
 constexpr uint64_t kAccLowMask = kAccOne - 1ull;
-// The down-projection partials of the kCluster CTAs of a thread-block cluster
-// are first summed in distributed shared memory (CTA rank r of the cluster owns
-// elements [1024 r / kCluster, 1024 (r + 1) / kCluster)); the owners add the
-// cluster sums into acc_down,
+// The down projection is split by output columns within a cluster pair: rank r
+// reduces columns [kSlice r, kSlice (r + 1)) over both CTAs' intermediate rows
+// (the partner's SwiGLU values arrive through distributed shared memory) and adds
+// them into acc_down,
 // spread over kDownCopies copies (cluster k adds into copy k % kDownCopies) to
 // cut same-address atomic contention; readers add the copies.
 constexpr int kCluster = 2;  // 74 co-resident pairs use all 148 SMs
+constexpr int kSlice = 1024 / kCluster;  // output columns of the down projection per cluster rank
 constexpr int kDownCopies = 2;
 
 // Flags in DecodeParams::flags.

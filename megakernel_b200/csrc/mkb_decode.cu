@@ -43,7 +43,7 @@ struct __align__(128) Smem {
   uint8_t ring[kSlots][kSlotBytes];
   uint64_t full[kSlots];
   uint64_t empty[kSlots];
-  uint64_t rxbar;        // kCluster arrivals: the cluster's down partials have landed
+  uint64_t rxbar;        // one arrival: the cluster partner's SwiGLU values have landed
   alignas(16) float r[kHidden];      // residual entering the current layer
   alignas(16) float rmid[kHidden];   // residual after attention + o_proj
   alignas(16) union {
@@ -61,6 +61,7 @@ struct __align__(128) Smem {
   alignas(16) float attn[2 * kHeadDim];
   alignas(16) float gu[2][32];
   alignas(16) float m[32];
+  alignas(16) float mrx[32];  // the cluster partner's SwiGLU values (down projection)
   alignas(16) float pbuf[kConsumerWarps][16];  // attention weights exchanged within a warp
   float red[2 * kConsumerWarps];
   float best_v[kConsumerWarps];
@@ -421,13 +422,17 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         pr.end();
       }
       if constexpr (kFused) {
-        const __nv_bfloat16* wdt = lwt(pr.c, l, kWDownT);
-        for (int j0 = pl.ja; j0 < pl.jb; j0 += kRowsPerChunk1024) {
-          const int j1 = min(pl.jb, j0 + kRowsPerChunk1024);
-          const uint32_t bytes = static_cast<uint32_t>(j1 - j0) * kHidden * 2u;
+        // this CTA's column block of the transposed down weight: its own rows,
+        // then its cluster partner's rows (one slot each)
+        const uint32_t rank = cluster_ctarank();
+        const __nv_bfloat16* wdt = lwt(pr.c, l, kWDownT) + (size_t)rank * kInter * kSlice;
+        const int partner = static_cast<int>(blockIdx.x ^ 1u);
+        const int rows[2][2] = {{pl.ja, pl.jb}, {part(kInter, p.grid, partner), part(kInter, p.grid, partner + 1)}};
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t bytes = static_cast<uint32_t>(rows[q][1] - rows[q][0]) * kSlice * 2u;
           const int s = pr.begin(bytes);
           if (s < 0) break;
-          if (pr.lane == 0) pr.copy(s, 0, wdt + (size_t)j0 * kHidden, bytes, pr.pol_w);
+          if (pr.lane == 0) pr.copy(s, 0, wdt + (size_t)rows[q][0] * kSlice, bytes, pr.pol_w);
           pr.end();
         }
       } else {
@@ -714,16 +719,9 @@ __device__ __forceinline__ void acc_clear4(uint64_t* row) {
   *reinterpret_cast<ulonglong2*>(w + 2) = make_ulonglong2(0ull, 0ull);
 }
 
-// Receive buffer of the cluster pre-reduction: [kCluster senders][kSlice] floats in
-// the union after the GEMV partials. It overlaps the attention partials, which
-// are never live at the same time: a sender writes layer l's slice only after
-// acc_mid[l] is complete (every owner has left its attention of layer l), and
-// writes layer l+1's only after acc_down[l] is complete (every owner has read
-// layer l's slices).
-constexpr int kSlice = kHidden / kCluster;  // accumulator elements owned per cluster rank
-__device__ __forceinline__ float (*cluster_rx(Smem& sm))[kSlice] {
-  return reinterpret_cast<float(*)[kSlice]>(&sm.u.x[512]);
-}
+static_assert(kCluster == 2 && kSlice == 2 * kConsumerThreads, "down projection: two columns per thread");
+
+// Bounded wait for the cluster partner's SwiGLU values of this layer.
 __device__ __noinline__ void cluster_rx_wait_slow(const Ctl c, uint32_t ph, int layer, int tok) {
   const uint64_t t0 = global_ns();
   while (!mbar_wait_cluster(&c.sm->rxbar, ph, kSuspendNs)) {
@@ -1197,54 +1195,54 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       tr.mark(kTrMark, kSubDEGU, l, t);
       if (tid < nj) {
         const float g = sm.gu[0][tid], u = sm.gu[1][tid];
-        sm.m[tid] = g / (1.0f + expf(-g)) * u;  // silu (config.cuh:177-179) * up
+        const float mv = g / (1.0f + expf(-g)) * u;  // silu (config.cuh:177-179) * up
+        sm.m[tid] = mv;
+        // the cluster partner reduces the other column block over these rows too
+        if constexpr (fused) st_cluster_f32(mapa_shared(smem_addr(&sm.mrx[tid]), cluster_ctarank() ^ 1u), mv);
       }
       consumer_sync(kConsumerThreads);
       if constexpr (fused) {
-        // down-proj partial over this CTA's intermediate rows: thread i owns
-        // output columns [4i, 4i+4) (megakernel.cu:53-90, split by K)
-        float pa[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int jb0 = 0; jb0 < nj; jb0 += 3 * kRowsPerChunk1024) {
-          const int nd = min(3, (nj - jb0 + kRowsPerChunk1024 - 1) / kRowsPerChunk1024);
-          uint32_t sa[3];
-          ring_wait_all(c, n, nd, sa, l, 5, t, &tr);
-          for (int i = 0; i < nd; ++i) {
-            const int js = jb0 + i * kRowsPerChunk1024;
-            const int j1 = min(nj, js + kRowsPerChunk1024);
-            for (int jj = js; jj < j1; ++jj) {
-              const uint2 w = lds64(sa[i] + (jj - js) * 2048 + e0 * 2);
-              const float mj = sm.m[jj];
-              pa[0] = fmaf(bf_lo(w.x), mj, pa[0]);
-              pa[1] = fmaf(bf_hi(w.x), mj, pa[1]);
-              pa[2] = fmaf(bf_lo(w.y), mj, pa[2]);
-              pa[3] = fmaf(bf_hi(w.y), mj, pa[3]);
-            }
+        if (tid == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&sm.rxbar), cluster_ctarank() ^ 1u));
+      }
+      if constexpr (fused) {
+        // Down projection split by output columns within the cluster pair: rank r
+        // reduces columns [kSlice r, kSlice (r + 1)) over both CTAs' intermediate
+        // rows (megakernel.cu:53-90, split by K across pairs); thread i owns two
+        // columns. Own rows first, then the partner's once its SwiGLU values land.
+        const uint32_t rank = cluster_ctarank();
+        const int pc = c.cta ^ 1;  // cluster partner
+        const int nj2 = part(kInter, G, pc + 1) - part(kInter, G, pc);
+        float pa0 = 0.f, pa1 = 0.f;
+        {
+          uint32_t sa[1];
+          ring_wait_all(c, n, 1, sa, l, 5, t, &tr);
+          for (int jj = 0; jj < nj; ++jj) {
+            const uint32_t w = lds32(sa[0] + jj * (kSlice * 2) + tid * 4);
+            const float mj = sm.m[jj];
+            pa0 = fmaf(bf_lo(w), mj, pa0);
+            pa1 = fmaf(bf_hi(w), mj, pa1);
           }
-          ring_done_all(c, n, nd);
+          ring_done_all(c, n, 1);
+        }
+        cluster_rx_wait(c, xph, l, t);
+        xph ^= 1u;
+        {
+          uint32_t sa[1];
+          ring_wait_all(c, n, 1, sa, l, 5, t, &tr);
+          for (int jj = 0; jj < nj2; ++jj) {
+            const uint32_t w = lds32(sa[0] + jj * (kSlice * 2) + tid * 4);
+            const float mj = sm.mrx[jj];
+            pa0 = fmaf(bf_lo(w), mj, pa0);
+            pa1 = fmaf(bf_hi(w), mj, pa1);
+          }
+          ring_done_all(c, n, 1);
         }
         tr.mark(kTrMark, kSubDEDown, l, t);
         {
-          // cluster pre-reduction: slice [kSlice r, kSlice (r + 1)) of every
-          // CTA's partial goes to cluster rank r (distributed shared memory),
-          // which adds the kCluster slices into acc_down (kCluster-fold fewer
-          // atomics).
-          const uint32_t rank = cluster_ctarank();
-          float(*rx)[kSlice] = cluster_rx(sm);
-          st_cluster_v4(mapa_shared(smem_addr(&rx[rank][e0 % kSlice]), static_cast<uint32_t>(e0 / kSlice)), pa[0],
-                        pa[1], pa[2], pa[3]);
-          consumer_sync(kConsumerThreads);
-          if (tid < kCluster) mbar_arrive_cluster(mapa_shared(smem_addr(&sm.rxbar), static_cast<uint32_t>(tid)));
-          cluster_rx_wait(c, xph, l, t);
-          xph ^= 1u;
           bool bad = false;
-          uint64_t* dst = &ws->acc_down[l][(c.cta / kCluster) % kDownCopies][rank * kSlice];
-#pragma unroll
-          for (int i = tid; i < kSlice; i += kConsumerThreads) {
-            float v = 0.f;
-#pragma unroll
-            for (int q = 0; q < kCluster; ++q) v += rx[q][i];
-            red_add_u64(dst + i, acc_term(v, bad));
-          }
+          uint64_t* dst = &ws->acc_down[l][(c.cta / kCluster) % kDownCopies][rank * kSlice + 2 * tid];
+          red_add_u64(dst, acc_term(pa0, bad));
+          red_add_u64(dst + 1, acc_term(pa1, bad));
           if (bad) raise_error(c, kErrRange, l, kStDE, t);
         }
         tr.mark(kTrPublish, kStDE, l, t);
@@ -1465,7 +1463,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
       mbar_init(&sm->full[s], 1);
       mbar_init(&sm->empty[s], kConsumerWarps);
     }
-    mbar_init(&sm->rxbar, kCluster);
+    mbar_init(&sm->rxbar, 1);
     sm->abort = 0;
     sm->is_last = 0;
     fence_mbar_init();

@@ -141,15 +141,19 @@ cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p) {
   return cudaSuccess;
 }
 
-// [1024, 3072] -> [3072, 1024] BF16 transpose through 32x32 shared tiles.
+// down [1024, 3072] -> down_t [kCluster][3072][1024 / kCluster] BF16: the
+// transpose with its 1024 output columns split into kCluster contiguous column
+// blocks (block r = the columns cluster rank r reduces), through 32x32 tiles.
 __global__ void transpose_down_kernel(const __nv_bfloat16* __restrict__ src, __nv_bfloat16* __restrict__ dst) {
   __shared__ __nv_bfloat16 tile[32][33];
-  const int bx = blockIdx.x * 32, by = blockIdx.y * 32;  // bx over 3072 cols, by over 1024 rows
+  const int bx = blockIdx.x * 32, by = blockIdx.y * 32;  // bx over 3072 (j), by over 1024 (output column)
   for (int i = threadIdx.y; i < 32; i += blockDim.y)
     tile[i][threadIdx.x] = src[(size_t)(by + i) * kInter + bx + threadIdx.x];
   __syncthreads();
+  constexpr int kHalf = kHidden / kCluster;
+  const int col = by + threadIdx.x;
   for (int i = threadIdx.y; i < 32; i += blockDim.y)
-    dst[(size_t)(bx + i) * kHidden + by + threadIdx.x] = tile[threadIdx.x][i];
+    dst[((size_t)(col / kHalf) * kInter + bx + i) * kHalf + col % kHalf] = tile[threadIdx.x][i];
 }
 
 }  // namespace

@@ -154,6 +154,18 @@ def summarize(per_cta) -> dict:
             src = (2, layer - 1, tok) if st == 0 else (1, layer, tok) if st == 2 else (2, layer, tok) if st == 4 else None
             if src in last_pub:
                 xlat[st].append(t - last_pub[src])
+    # stragglers: per (stage, layer, token) the publishing CTAs' spread and who is last
+    pubs = defaultdict(list)
+    for cta, recs in enumerate(per_cta):
+        for kind, st, layer, tok, t in recs:
+            if kind == 2 and st in (0, 1, 2):
+                pubs[(st, layer, tok)].append((t, cta))
+    spread = defaultdict(list)
+    last_cta = defaultdict(lambda: defaultdict(int))
+    for (st, layer, tok), v in pubs.items():
+        ts = sorted(x[0] for x in v)
+        spread[st].append(ts[-1] - ts[len(ts) // 2])
+        last_cta[st][max(v)[1]] += 1
     med = lambda xs: statistics.median(xs) / 1000.0 if xs else None  # noqa: E731
     mean = lambda xs: statistics.fmean(xs) / 1000.0 if xs else None  # noqa: E731
     span = max(r[-1][4] for r in per_cta if r) - t0
@@ -163,6 +175,8 @@ def summarize(per_cta) -> dict:
         "layer_period_us_median": med(layer_period),
         "lm_head_us_median": med(lm_ns),
         "exchange_us_median": {STAGE_NAMES[k]: med(v) for k, v in xlat.items()},
+        "publish_spread_us_median": {STAGE_NAMES[k]: med(v) for k, v in spread.items()},
+        "last_publishers": {STAGE_NAMES[k]: sorted(v.items(), key=lambda kv: -kv[1])[:6] for k, v in last_cta.items()},
         "segments": {k: {"mean_us": statistics.fmean(v) / 1000.0, "median_us": statistics.median(v) / 1000.0,
                          "count": len(v)} for k, v in seg.items()},
         "stages": {STAGE_NAMES[s]: {"wait_us_mean": mean(waits[s]), "wait_us_median": med(waits[s]),
@@ -183,6 +197,11 @@ def format_summary(s: dict) -> str:
     if s.get("exchange_us_median"):
         lines.append("exchange latency (last publish over all CTAs -> wait end), median: " +
                      ", ".join(f"{k} {v:.3f} us" for k, v in s["exchange_us_median"].items() if v is not None))
+    if s.get("publish_spread_us_median"):
+        lines.append("publish spread (last CTA - median CTA), median over layers: " +
+                     ", ".join(f"{k} {v:.3f} us" for k, v in s["publish_spread_us_median"].items() if v is not None))
+        for k, v in s["last_publishers"].items():
+            lines.append(f"  last {k} publishers (cta: layers): " + ", ".join(f"{c}: {n}" for c, n in v))
     lines.append("segments (time since the CTA's previous stamp, labelled by the later stamp):")
     for k, d in sorted(s.get("segments", {}).items(), key=lambda kv: -kv[1]["mean_us"] * kv[1]["count"]):
         lines.append(f"  {k:28s} mean {d['mean_us']:8.3f} us  median {d['median_us']:8.3f} us  n={d['count']}")

@@ -62,9 +62,12 @@ def down_t_table(layers_gpu):
 
 
 def test_transpose_down(w_gpu):
+    """[1024, 3072] -> [2][3072][512]: the transpose with its output columns in
+    two contiguous blocks, one per CTA of a cluster pair."""
     bufs, _ = down_t_table(w_gpu.layers[:1])
     torch.cuda.synchronize()
-    assert torch.equal(bufs[0], w_gpu.layers[0]["down"].t().contiguous())
+    want = w_gpu.layers[0]["down"].t().reshape(3072, 2, 512).permute(1, 0, 2).contiguous()
+    assert torch.equal(bufs[0].reshape(2, 3072, 512), want)
 
 
 # ---------------------------------------------------------------- config 2
