@@ -356,6 +356,41 @@ def test_withheld_arrival_times_out_with_status(w_gpu):
     assert torch.isfinite(logits).all()
 
 
+def test_misaligned_weight_is_rejected_on_the_device(w_gpu):
+    """A weight pointer that is not 16-byte aligned (here the first layer's input
+    norm, offset by one element) is caught by the kernel's prologue before any
+    load: the launch returns, the status is kErrBadArgs, and nothing was read."""
+    k = torch.zeros((28, 8, 64, 128), dtype=torch.bfloat16, device=DEV)
+    cos, sin = mk.rope_tables(64, DEV)
+    layers = w_gpu.flat_layer_list()
+    shifted = torch.ones(1024 + 8, dtype=torch.bfloat16, device=DEV)
+    bad = list(layers)
+    bad[0] = shifted[1:1025]
+    table = build_layer_table(bad, DEV)
+    ws = torch.zeros(_lib.load().mkb_workspace_bytes(), dtype=torch.uint8, device=DEV)
+    logits = torch.full((151936,), 7.0, dtype=torch.float32, device=DEV)
+    _lib.check(decode_call(embed=w_gpu.embed, lm_head=w_gpu.embed, final_norm=w_gpu.final_norm, layers=table,
+                           cos_table=cos, sin_table=sin, rope_fp32=1, k_cache=k, v_cache=k.clone(), max_seq=64,
+                           layer_begin=0, layer_end=28, token=5, position=0, cache_len=1,
+                           flags=_lib.MKB_FLAG_LM_HEAD, logits=logits, workspace=ws), "mkb_decode")
+    torch.cuda.synchronize()
+    assert _lib.workspace_status(ws.data_ptr())[0] == 4  # kErrBadArgs
+    assert bool((logits == 7.0).all())
+    assert bool((k == 0).all())
+
+
+def test_grid_that_cannot_form_cluster_pairs_is_refused(w_gpu):
+    """The grid is launched as CTA pairs: an odd grid is refused on the host."""
+    k = torch.zeros((28, 8, 64, 128), dtype=torch.bfloat16, device=DEV)
+    cos, sin = mk.rope_tables(64, DEV)
+    table = build_layer_table(w_gpu.flat_layer_list(), DEV)
+    code = decode_call(embed=w_gpu.embed, lm_head=w_gpu.embed, final_norm=w_gpu.final_norm, layers=table,
+                       cos_table=cos, sin_table=sin, rope_fp32=1, k_cache=k, v_cache=k.clone(), max_seq=64,
+                       layer_begin=0, layer_end=28, token=5, position=0, cache_len=1, flags=_lib.MKB_FLAG_LM_HEAD,
+                       grid=147)
+    assert code == 9  # cudaErrorInvalidConfiguration
+
+
 # ---------------------------------------------------------------- the reference kernel itself
 def test_reference_kernel_agrees(w_gpu, hf_model, config0_hf):
     """The reference megakernel (built from its own sources for sm_100a) and the
