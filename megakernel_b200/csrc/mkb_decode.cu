@@ -514,12 +514,15 @@ __device__ __forceinline__ void mma_tile_1024(uint32_t base, int nrows, const ui
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int tr = lane & 15;
   const uint32_t row = base + (tr < nrows ? tr : 0) * kRowStride + (lane >> 4) * 16 + warp * (kKPerWarp * 2);
+  float e[4] = {0.f, 0.f, 0.f, 0.f};  // second accumulator: two independent MMA chains
 #pragma unroll
   for (int st = 0; st < kKSteps; ++st) {
     uint32_t a0, a1, a2, a3;
     ldsm_x4(row + st * 32, a0, a1, a2, a3);
-    mma_bf16(d, a0, a1, a2, a3, bfr[st][0], bfr[st][1]);
+    mma_bf16((st & 1) ? e : d, a0, a1, a2, a3, bfr[st][0], bfr[st][1]);
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] += e[i];
 }
 // Gate/up tile: tile rows 0-6 are gate rows, 8-14 up rows (second slot half).
 __device__ __forceinline__ void mma_tile_gu(uint32_t base, int nrows, const uint32_t bfr[kKSteps][2], float* d) {
@@ -527,12 +530,15 @@ __device__ __forceinline__ void mma_tile_gu(uint32_t base, int nrows, const uint
   const int tr = lane & 15, i = tr & 7;
   const uint32_t row = base + (tr >= 8 ? kSlotBytes / 2 : 0) + (i < nrows ? i : 0) * kRowStride + (lane >> 4) * 16 +
                        warp * (kKPerWarp * 2);
+  float e[4] = {0.f, 0.f, 0.f, 0.f};  // second accumulator: two independent MMA chains
 #pragma unroll
   for (int st = 0; st < kKSteps; ++st) {
     uint32_t a0, a1, a2, a3;
     ldsm_x4(row + st * 32, a0, a1, a2, a3);
-    mma_bf16(d, a0, a1, a2, a3, bfr[st][0], bfr[st][1]);
+    mma_bf16((st & 1) ? e : d, a0, a1, a2, a3, bfr[st][0], bfr[st][1]);
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] += e[i];
 }
 // Lanes holding D column pairs write this warp's row partials of tile t.
 __device__ __forceinline__ void stash_tile(float (*xred)[64], int t, const float* d) {
