@@ -74,7 +74,10 @@ constexpr uint64_t kAccLowMask = kAccOne - 1ull;
 // cut same-address atomic contention; readers add the copies.
 constexpr int kCluster = 2;  // 74 co-resident pairs use all 148 SMs
 constexpr int kSlice = 1024 / kCluster;  // output columns of the down projection per cluster rank
-constexpr int kDownCopies = 2;
+#ifndef MKB_DOWN_COPIES
+#define MKB_DOWN_COPIES 2
+#endif
+constexpr int kDownCopies = MKB_DOWN_COPIES;
 
 // Flags in DecodeParams::flags.
 enum : int {

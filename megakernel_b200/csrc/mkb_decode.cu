@@ -690,18 +690,42 @@ __device__ __noinline__ float acc_wait_slow(const Ctl c, const uint64_t* w, int 
   }
   return v;
 }
-// This thread's 4 elements of a [copies][kHidden] accumulator row, each
-// complete with `expect` contributions. Lane 0 polls first, so a warp that
-// arrives early generates one poll stream instead of 32.
-__device__ __forceinline__ void acc_wait4(const Ctl& c, const uint64_t* row, int copies, uint32_t expect, float v[4],
-                                          int layer, int stage, int tok) {
-  const uint64_t* w = row + threadIdx.x * kE;
-  uint32_t cnt = 0;
-  if ((threadIdx.x & 31) == 0) {
-    acc_value(w, copies, cnt);
-    if (cnt != expect) acc_wait_slow(c, w, copies, expect, layer, stage, tok);
+// Bounded poll by one thread until elements e0 and e1 of an accumulator row
+// (e1 < 0: e0 only) both hold `expect` contributions; both are loaded in every
+// round, so the second costs no extra round trip.
+__device__ __noinline__ void acc_wait_pair(const Ctl c, const uint64_t* row, int copies, uint32_t expect, int e0,
+                                           int e1, int layer, int stage, int tok) {
+  const uint64_t t0 = global_ns();
+  uint32_t it = 0;
+  while (true) {
+    uint32_t n0 = 0, n1 = expect;
+    acc_value(row + e0, copies, n0);
+    if (e1 >= 0) acc_value(row + e1, copies, n1);
+    if (n0 == expect && n1 == expect) break;
+    if ((++it & 15u) == 0u) {
+      if (aborted(c) || ld_relaxed(&c.ws->error[0]) != 0u) {
+        *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
+        break;
+      }
+      if (global_ns() - t0 > c.timeout) {
+        raise_error(c, kErrTimeoutTransition, layer, stage, tok);
+        break;
+      }
+    }
   }
-  __syncwarp();
+}
+// This thread's 4 elements of a [copies][kHidden] accumulator row, each
+// complete with `expect` contributions in total. One thread of the CTA polls a
+// sentinel element of copy 0 only (complete at `expect0` contributions) and
+// the others wait at a barrier: every poll competes with the atomics landing on
+// the same L2 lines, so the fewer poll loads the faster the exchange
+// (measured). Elements still incomplete after the barrier are polled by their
+// owners.
+__device__ __forceinline__ void acc_wait4(const Ctl& c, const uint64_t* row, int copies, uint32_t expect,
+                                          uint32_t expect0, int s0, float v[4], int layer, int stage, int tok) {
+  const uint64_t* w = row + threadIdx.x * kE;
+  if (threadIdx.x == 0) acc_wait_pair(c, row, 1, expect0, s0, -1, layer, stage, tok);
+  consumer_sync(kConsumerThreads);
   uint64_t low[4] = {0, 0, 0, 0}, cn[4] = {0, 0, 0, 0};
   for (int q = 0; q < copies; ++q) {
     uint64_t a, b, x, y;
@@ -726,6 +750,7 @@ __device__ __forceinline__ void acc_clear4(uint64_t* row) {
 }
 
 static_assert(kCluster == 2 && kSlice == 2 * kConsumerThreads, "down projection: two columns per thread");
+
 
 // Bounded wait for the cluster partner's SwiGLU values of this layer.
 __device__ __noinline__ void cluster_rx_wait_slow(const Ctl c, uint32_t ph, int layer, int tok) {
@@ -755,6 +780,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   const int G = p.grid;
   const int lb = p.layer_begin, le = p.layer_end;
   const int zero_cta = G - 1;
+  // contributions that land in copy 0 of a down row: clusters k with k % kDownCopies == 0
+  const int down_copy0 = (G / kCluster + kDownCopies - 1) / kDownCopies;
   uint32_t n = 0;
   uint32_t xph = 0;  // phase of sm.rxbar for the next cluster exchange
   int flip = 0;
@@ -796,7 +823,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         if constexpr (fused) {
           tr.mark(kTrWaitBegin, kStA, l, t);
           float d[4];
-          acc_wait4(c, &ws->acc_down[l - 1][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster), d, l, kStA, t);
+          acc_wait4(c, &ws->acc_down[l - 1][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster),
+                    static_cast<uint32_t>(down_copy0), 0, d, l, kStA, t);
           tr.mark(kTrWaitEnd, kStA, l, t);
           const float4 rm = *reinterpret_cast<const float4*>(&sm.rmid[e0]);
           r[0] = rm.x + d[0]; r[1] = rm.y + d[1]; r[2] = rm.z + d[2]; r[3] = rm.w + d[3];
@@ -884,6 +912,13 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           const int base = warp < 2 ? (2 * h + warp) * kHeadDim
                                     : (warp == 2 ? kQSize + h * kHeadDim : kQSize + kKVSize + h * kHeadDim);
           float x0, x1, x2, x3;  // dims d0, d0+1, d0+64, d0+65
+          // lane 0 polls the end of the range first, then every lane reads its
+          // words (few pollers; stragglers are polled by their readers)
+          if (lane == 0) {
+            float y0, y1;
+            poll_tagged2(c, &ws->qkv_tagged[l][base + kHeadDim - 2], tag, y0, y1, l, t);
+          }
+          __syncwarp();
           poll_tagged2(c, &ws->qkv_tagged[l][base + d0], tag, x0, x1, l, t);
           poll_tagged2(c, &ws->qkv_tagged[l][base + d0 + 64], tag, x2, x3, l, t);
           if (warp < 3) {
@@ -1163,7 +1198,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       tr.mark(kTrWaitBegin, kStDE, l, t);
       {
         float a[4];
-        acc_wait4(c, &ws->acc_mid[l][0], 1, static_cast<uint32_t>(kNKV), a, l, kStDE, t);
+        acc_wait4(c, &ws->acc_mid[l][0], 1, static_cast<uint32_t>(kNKV), static_cast<uint32_t>(kNKV), 0, a, l, kStDE,
+                  t);
         tr.mark(kTrWaitEnd, kStDE, l, t);
         const float4 rv = *reinterpret_cast<const float4*>(&sm.r[e0]);
         float mres[4] = {rv.x + a[0], rv.y + a[1], rv.z + a[2], rv.w + a[3]};
@@ -1289,8 +1325,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       if constexpr (fused) {
         tr.mark(kTrWaitBegin, kStLM, le - 1, t);
         float d[4];
-        acc_wait4(c, &ws->acc_down[le - 1][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster), d, le - 1, kStLM,
-                  t);
+        acc_wait4(c, &ws->acc_down[le - 1][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster),
+                  static_cast<uint32_t>(down_copy0), 0, d, le - 1, kStLM, t);
         tr.mark(kTrWaitEnd, kStLM, le - 1, t);
         const float4 rm = *reinterpret_cast<const float4*>(&sm.rmid[e0]);
         r[0] = rm.x + d[0]; r[1] = rm.y + d[1]; r[2] = rm.z + d[2]; r[3] = rm.w + d[3];
