@@ -43,7 +43,9 @@ struct __align__(128) Smem {
   uint8_t ring[kSlots][kSlotBytes];
   uint64_t full[kSlots];
   uint64_t empty[kSlots];
-  uint64_t rxbar;        // one arrival: the cluster partner's SwiGLU values have landed
+  // One phase per layer: this CTA's own arrival (with the expected byte count)
+  // plus the cluster partner's SwiGLU values, each landing with complete_tx.
+  uint64_t rxbar;
   alignas(16) float r[kHidden];      // residual entering the current layer
   alignas(16) float rmid[kHidden];   // residual after attention + o_proj
   alignas(16) union {
@@ -74,6 +76,7 @@ struct __align__(128) Smem {
   int token;
   int is_last;
   int abort;
+  int peer_gone;  // set by the cluster partner when it leaves the token loop early
 };
 
 constexpr size_t kSmemBytes = sizeof(Smem);
@@ -752,19 +755,24 @@ __device__ __forceinline__ void acc_clear4(uint64_t* row) {
 static_assert(kCluster == 2 && kSlice == 2 * kConsumerThreads, "down projection: two columns per thread");
 
 
-// Bounded wait for the cluster partner's SwiGLU values of this layer.
-__device__ __noinline__ void cluster_rx_wait_slow(const Ctl c, uint32_t ph, int layer, int tok) {
+// Bounded wait for the cluster partner's SwiGLU values of this layer; true once
+// they have landed. Unlike the other waits it does not give up on an abort:
+// an aborted partner still sends every layer until it leaves the token loop
+// (and then says so through peer_gone), and each value must have landed before
+// this CTA re-arms rxbar or exits.
+__device__ __noinline__ bool cluster_rx_wait_slow(const Ctl c, uint32_t ph, int layer, int tok) {
   const uint64_t t0 = global_ns();
   while (!mbar_wait_cluster(&c.sm->rxbar, ph, kSuspendNs)) {
-    if (aborted(c)) break;
+    if (*reinterpret_cast<volatile int*>(&c.sm->peer_gone) != 0) return false;
     if (global_ns() - t0 > c.timeout) {
       raise_error(c, kErrTimeoutTransition, layer, kStDE, tok);
-      break;
+      return false;
     }
   }
+  return true;
 }
-__device__ __forceinline__ void cluster_rx_wait(const Ctl& c, uint32_t ph, int layer, int tok) {
-  if (!mbar_wait_cluster(&c.sm->rxbar, ph, 0u)) cluster_rx_wait_slow(c, ph, layer, tok);
+__device__ __forceinline__ bool cluster_rx_wait(const Ctl& c, uint32_t ph, int layer, int tok) {
+  return mbar_wait_cluster(&c.sm->rxbar, ph, 0u) || cluster_rx_wait_slow(c, ph, layer, tok);
 }
 
 template <bool kFused, bool kTraced>
@@ -783,7 +791,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   // contributions that land in copy 0 of a down row: clusters k with k % kDownCopies == 0
   const int down_copy0 = (G / kCluster + kDownCopies - 1) / kDownCopies;
   uint32_t n = 0;
-  uint32_t xph = 0;  // phase of sm.rxbar for the next cluster exchange
+  uint32_t xph = 0;     // phase of sm.rxbar for the next cluster exchange
+  bool rx_live = true;  // every earlier phase of sm.rxbar was seen to complete
   int flip = 0;
   float xr[32];
   Tracer<kTraced> tr{c.trace, sm.tbuf, c.trace_cap, 0, 0};
@@ -1185,7 +1194,10 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         }
         tr.mark(kTrPublish, kStBC, l, t);
         // A later token of this launch re-reads this head's K/V rows through the
-        // bulk-copy engine: publish the append (K writer and V writer).
+        // bulk-copy engine: publish the append (K writer and V writer). Moving
+        // this gpu-scope release off the consumer warps (to the end of the
+        // layer, to the producer once per token, to a tenth warp, or having
+        // every attention CTA append and wait locally) measured slower.
         if (p.n_tokens > 1 && pl.c == 0 && (warp == 2 || warp == 3)) {
           __syncwarp();
           if (lane == 0) release_add(&ws->kv_ready[l][h][0], 1u);
@@ -1239,13 +1251,17 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         const float g = sm.gu[0][tid], u = sm.gu[1][tid];
         const float mv = g / (1.0f + expf(-g)) * u;  // silu (config.cuh:177-179) * up
         sm.m[tid] = mv;
-        // the cluster partner reduces the other column block over these rows too
-        if constexpr (fused) st_cluster_f32(mapa_shared(smem_addr(&sm.mrx[tid]), cluster_ctarank() ^ 1u), mv);
+        // The cluster partner reduces the other column block over these rows too:
+        // each value lands in its shared memory with 4 bytes of complete_tx on its
+        // rxbar, so no thread here waits on a release.
+        if constexpr (fused) {
+          if (*reinterpret_cast<volatile int*>(&sm.peer_gone) == 0) {
+            const uint32_t pr = cluster_ctarank() ^ 1u;
+            st_async_f32(mapa_shared(smem_addr(&sm.mrx[tid]), pr), mv, mapa_shared(smem_addr(&sm.rxbar), pr));
+          }
+        }
       }
       consumer_sync(kConsumerThreads);
-      if constexpr (fused) {
-        if (tid == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&sm.rxbar), cluster_ctarank() ^ 1u));
-      }
       if constexpr (fused) {
         // Down projection split by output columns within the cluster pair: rank r
         // reduces columns [kSlice r, kSlice (r + 1)) over both CTAs' intermediate
@@ -1266,7 +1282,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           }
           ring_done_all(c, n, 1);
         }
-        cluster_rx_wait(c, xph, l, t);
+        if (rx_live) rx_live = cluster_rx_wait(c, xph, l, t);
         xph ^= 1u;
         {
           uint32_t sa[1];
@@ -1288,6 +1304,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           if (bad) raise_error(c, kErrRange, l, kStDE, t);
         }
         tr.mark(kTrPublish, kStDE, l, t);
+        // Arm the next phase of rxbar, now that this one is seen complete (one
+        // arrival per phase; the partner's bytes may land before or after it).
+        if (rx_live && tid == kConsumerThreads - 32) mbar_arrive_expect_tx(&sm.rxbar, static_cast<uint32_t>(nj2) * 4u);
       } else {
         // reference layout: publish the SwiGLU vector, then whole down rows
         if (tid < nj) p.mlp_out[pl.ja + tid] = sm.m[tid];
@@ -1395,7 +1414,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     consumer_sync(kConsumerThreads);
     tr.mark(kTrMark, kStEnd, 0, t);
     tr.flush();
-    if (last_state < 0) return;
+    if (last_state < 0) {
+      // leaving early: the cluster partner must not wait for (or send) more
+      // SwiGLU values; this store is ordered before the final cluster barrier
+      if (kFused && tid == 0) st_cluster_u32(mapa_shared(smem_addr(&sm.peer_gone), cluster_ctarank() ^ 1u), 1u);
+      return;
+    }
     if (last_state) {
       int best = -1;
       if (p.flags & kFlagLmHead) {
@@ -1506,7 +1530,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
       mbar_init(&sm->empty[s], kConsumerWarps);
     }
     mbar_init(&sm->rxbar, 1);
+    if (kFused) {  // the first layer's phase: one arrival plus the partner's SwiGLU bytes
+      const int pc = static_cast<int>(blockIdx.x) ^ 1;
+      mbar_arrive_expect_tx(&sm->rxbar, static_cast<uint32_t>(part(kInter, p.grid, pc + 1) - part(kInter, p.grid, pc)) * 4u);
+    }
     sm->abort = 0;
+    sm->peer_gone = 0;
     sm->is_last = 0;
     fence_mbar_init();
   }

@@ -158,20 +158,22 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
   return r;
 }
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+// Plain store into another CTA's shared memory (ordered by a later cluster
+// barrier's release).
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+// Non-blocking store of one float into another CTA's shared memory whose
+// arrival is counted (4 bytes of complete_tx) on that CTA's mbarrier: the
+// receiver's wait on the barrier covers the data, and the sender carries on at
+// once (no release fence on its side).
+__device__ __forceinline__ void st_async_f32(uint32_t remote_addr, float v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(remote_addr),
+               "f"(v), "r"(remote_bar)
                : "memory");
 }
-// Arrive on an mbarrier of another CTA of the cluster; orders this thread's
-// earlier (and, through a preceding CTA barrier, its CTA's) shared::cluster
-// writes before the arrival.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
-}
-// As mbar_wait, with cluster-scope acquire (pairs with mbar_arrive_cluster).
+// As mbar_wait, with cluster-scope acquire (pairs with the release of the
+// complete_tx that st_async_f32 performs on this barrier).
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
   uint32_t ok;
   asm volatile(

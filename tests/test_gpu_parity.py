@@ -266,32 +266,57 @@ def test_c_abi_launcher_matches_extension(w_gpu, hf_model, config0_hf):
     assert (lg - kept[0]).abs().max().item() <= 2e-2 and cosine(lg, kept[0]) > 0.999
 
 
-def test_generate_matches_stepwise(w_gpu, hf_model, config0_hf):
-    """One persistent launch of n greedy tokens == n single-token launches."""
-    g, fed, _ = config0_hf
-    ids = torch.from_numpy(g["prompt"])
-    _, _, kg, vg = prefill_to_gpu(hf_model, ids, 512)
+def _generate_vs_stepwise(eng, kg, vg, first, pos0, n):
+    """Greedy tokens of n single-token launches and of one n-token launch from
+    the same cache; checks the tokens (up to a near-tie) and the K/V rows the
+    launch appended, which later tokens of the same launch re-read."""
     k0, v0 = kg.clone(), vg.clone()
-    eng = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), kg, vg)
-    n = 24
     steps, margins = [], []
-    tok = fed[0]
+    tok = first
     for i in range(n):
-        tok = eng.step(tok, 32 + i)
-        lg = eng.logits
-        t2 = torch.topk(lg, 2).values
+        tok = eng.step(tok, pos0 + i)
+        t2 = torch.topk(eng.logits, 2).values
         margins.append(float(t2[0] - t2[1]))
         steps.append(tok)
+    ks, vs = kg[:, :, pos0:pos0 + n].clone(), vg[:, :, pos0:pos0 + n].clone()
     kg.copy_(k0)
     vg.copy_(v0)
-    out = eng.generate(fed[0], 32, n)
+    out = eng.generate(first, pos0, n)
     torch.cuda.synchronize()
     gen = out.cpu().tolist()
+    same = n
     for i in range(n):
         if gen[i] != steps[i]:
             assert margins[i] < 1e-3, f"token {i} differs with margin {margins[i]}"
+            same = i
             break
     assert eng.status()[0] == 0
+    # row pos0 + i is appended from the token fed at step i: equal inputs up to
+    # the first differing token; within 2 BF16 ulp (a stale or missing row
+    # differs by O(1))
+    m = min(same + 1, n)
+    for got, ref in ((kg[:, :, pos0:pos0 + m], ks[:, :, :m]), (vg[:, :, pos0:pos0 + m], vs[:, :, :m])):
+        torch.testing.assert_close(got.float(), ref.float(), rtol=1.6e-2, atol=1e-3)
+
+
+def test_generate_matches_stepwise(w_gpu, hf_model, config0_hf):
+    """One persistent launch of n greedy tokens == n single-token launches."""
+    g, fed, _ = config0_hf
+    _, _, kg, vg = prefill_to_gpu(hf_model, torch.from_numpy(g["prompt"]), 512)
+    eng = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), kg, vg)
+    _generate_vs_stepwise(eng, kg, vg, fed[0], 32, 24)
+    eng.close()
+
+
+def test_generate_matches_stepwise_split_attention(w_gpu):
+    """As above on a 1024-slot cache of seeded random K/V at positions 1000..:
+    attention is split across the head's CTAs, and every token after the first
+    re-reads rows appended earlier in the same launch."""
+    gen = torch.Generator(device=DEV).manual_seed(7)
+    kg = torch.randn((28, 8, 1024, 128), generator=gen, device=DEV).to(torch.bfloat16)
+    vg = torch.randn((28, 8, 1024, 128), generator=gen, device=DEV).to(torch.bfloat16)
+    eng = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), kg, vg)
+    _generate_vs_stepwise(eng, kg, vg, 1234, 1000, 8)
     eng.close()
 
 
