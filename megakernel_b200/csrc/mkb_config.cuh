@@ -31,6 +31,9 @@ constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kSlotBytes = 32768;
 constexpr int kSlots = 6;
 constexpr int kMaxGrid = 256;
+constexpr int kMinGrid = 128;
+// SwiGLU rows per CTA are at most kMaxJ (kInter split over at least kMinGrid CTAs).
+constexpr int kMaxJ = (kInter + kMinGrid - 1) / kMinGrid;
 constexpr int kMaxSplits = 32;
 
 // Chunk geometry (rows per ring slot) for each streamed matrix. Rows read by

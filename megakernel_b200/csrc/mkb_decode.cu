@@ -543,6 +543,40 @@ __device__ __forceinline__ void mma_tile_gu(uint32_t base, int nrows, const uint
 #pragma unroll
   for (int i = 0; i < 4; ++i) d[i] += e[i];
 }
+// Down projection over the SwiGLU rows j < nj of one slot (row j at
+// j * kSlice * 2 bytes, this thread's two columns at 4 * tid), weighted by m[j]:
+// unrolled over the static bound kMaxJ so the shared loads issue back to back
+// ahead of the FMAs, with two accumulator chains per column. m[j] is zero for
+// j >= nj and the weight word is masked there, so stale slot bytes never enter.
+__device__ __forceinline__ void down_rows(uint32_t slot, const float* m, int nj, float& a0, float& a1) {
+  const uint32_t col = slot + (threadIdx.x & (kConsumerThreads - 1)) * 4;
+  float b0 = 0.f, b1 = 0.f;
+#pragma unroll
+  for (int jj = 0; jj < kMaxJ; jj += 4) {
+    const float4 mv = *reinterpret_cast<const float4*>(m + jj);
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      // unconditional load (rows up to kMaxJ lie inside the slot), then mask:
+      // a conditional asm load would become a branch per row
+      const uint32_t v = lds32(col + (jj + q) * (kSlice * 2));
+      w[q] = jj + q < nj ? v : 0u;
+    }
+    a0 = fmaf(bf_lo(w[0]), mv.x, a0);
+    a1 = fmaf(bf_hi(w[0]), mv.x, a1);
+    b0 = fmaf(bf_lo(w[1]), mv.y, b0);
+    b1 = fmaf(bf_hi(w[1]), mv.y, b1);
+    a0 = fmaf(bf_lo(w[2]), mv.z, a0);
+    a1 = fmaf(bf_hi(w[2]), mv.z, a1);
+    b0 = fmaf(bf_lo(w[3]), mv.w, b0);
+    b1 = fmaf(bf_hi(w[3]), mv.w, b1);
+  }
+  a0 += b0;
+  a1 += b1;
+}
+static_assert(kMaxJ % 4 == 0 && kMaxJ <= 32 && kMaxJ * kSlice * 2 <= kSlotBytes,
+              "down_rows reads m[0, kMaxJ) as float4 and kMaxJ rows of a slot");
+
 // Lanes holding D column pairs write this warp's row partials of tile t.
 __device__ __forceinline__ void stash_tile(float (*xred)[64], int t, const float* d) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -793,6 +827,15 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   uint32_t n = 0;
   uint32_t xph = 0;     // phase of sm.rxbar for the next cluster exchange
   bool rx_live = true;  // every earlier phase of sm.rxbar was seen to complete
+  // Cluster-pair constants of the down projection, fixed for the launch (each
+  // costs a dependent chain of long-latency instructions if formed per layer):
+  // this CTA's rank, the partner's SwiGLU row count, the partner's mrx slot and
+  // rxbar for this thread's value, and this pair's copy of the down accumulators.
+  const uint32_t crank = cluster_ctarank();
+  const int nj2 = part(kInter, G, (c.cta ^ 1) + 1) - part(kInter, G, c.cta ^ 1);
+  const uint32_t rx_bar_peer = mapa_shared(smem_addr(&sm.rxbar), crank ^ 1u);
+  const uint32_t rx_m_peer = mapa_shared(smem_addr(&sm.mrx[tid & 31]), crank ^ 1u);
+  const int down_copy = (c.cta / kCluster) % kDownCopies;
   int flip = 0;
   float xr[32];
   Tracer<kTraced> tr{c.trace, sm.tbuf, c.trace_cap, 0, 0};
@@ -1255,10 +1298,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         // each value lands in its shared memory with 4 bytes of complete_tx on its
         // rxbar, so no thread here waits on a release.
         if constexpr (fused) {
-          if (*reinterpret_cast<volatile int*>(&sm.peer_gone) == 0) {
-            const uint32_t pr = cluster_ctarank() ^ 1u;
-            st_async_f32(mapa_shared(smem_addr(&sm.mrx[tid]), pr), mv, mapa_shared(smem_addr(&sm.rxbar), pr));
-          }
+          if (*reinterpret_cast<volatile int*>(&sm.peer_gone) == 0) st_async_f32(rx_m_peer, mv, rx_bar_peer);
         }
       }
       consumer_sync(kConsumerThreads);
@@ -1267,19 +1307,11 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         // reduces columns [kSlice r, kSlice (r + 1)) over both CTAs' intermediate
         // rows (megakernel.cu:53-90, split by K across pairs); thread i owns two
         // columns. Own rows first, then the partner's once its SwiGLU values land.
-        const uint32_t rank = cluster_ctarank();
-        const int pc = c.cta ^ 1;  // cluster partner
-        const int nj2 = part(kInter, G, pc + 1) - part(kInter, G, pc);
         float pa0 = 0.f, pa1 = 0.f;
         {
           uint32_t sa[1];
           ring_wait_all(c, n, 1, sa, l, 5, t, &tr);
-          for (int jj = 0; jj < nj; ++jj) {
-            const uint32_t w = lds32(sa[0] + jj * (kSlice * 2) + tid * 4);
-            const float mj = sm.m[jj];
-            pa0 = fmaf(bf_lo(w), mj, pa0);
-            pa1 = fmaf(bf_hi(w), mj, pa1);
-          }
+          down_rows(sa[0], sm.m, nj, pa0, pa1);
           ring_done_all(c, n, 1);
         }
         if (rx_live) rx_live = cluster_rx_wait(c, xph, l, t);
@@ -1287,18 +1319,13 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         {
           uint32_t sa[1];
           ring_wait_all(c, n, 1, sa, l, 5, t, &tr);
-          for (int jj = 0; jj < nj2; ++jj) {
-            const uint32_t w = lds32(sa[0] + jj * (kSlice * 2) + tid * 4);
-            const float mj = sm.mrx[jj];
-            pa0 = fmaf(bf_lo(w), mj, pa0);
-            pa1 = fmaf(bf_hi(w), mj, pa1);
-          }
+          down_rows(sa[0], sm.mrx, nj2, pa0, pa1);
           ring_done_all(c, n, 1);
         }
         tr.mark(kTrMark, kSubDEDown, l, t);
         {
           bool bad = false;
-          uint64_t* dst = &ws->acc_down[l][(c.cta / kCluster) % kDownCopies][rank * kSlice + 2 * tid];
+          uint64_t* dst = &ws->acc_down[l][down_copy][crank * kSlice + 2 * tid];
           red_add_u64(dst, acc_term(pa0, bad));
           red_add_u64(dst + 1, acc_term(pa1, bad));
           if (bad) raise_error(c, kErrRange, l, kStDE, t);
@@ -1536,6 +1563,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     }
     sm->abort = 0;
     sm->peer_gone = 0;
+    // SwiGLU values past this CTA's (or its partner's) row count stay zero: the
+    // down projection reads kMaxJ of them
+    for (int j = 0; j < 32; ++j) sm->m[j] = sm->mrx[j] = 0.f;
     sm->is_last = 0;
     fence_mbar_init();
   }
@@ -1547,7 +1577,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
   const int splits = p.splits > 0 ? p.splits : choose_splits(last_cl, p.group_size);
   // Argument guard (uniform over the grid, before any wait).
   if (token < 0 || token >= kVocab || pos < 0 || pos + p.n_tokens > p.max_seq || cl < 1 ||
-      last_cl > p.max_seq || p.grid != static_cast<int>(gridDim.x) || p.grid > kMaxGrid ||
+      last_cl > p.max_seq || p.grid != static_cast<int>(gridDim.x) || p.grid > kMaxGrid || p.grid < kMinGrid ||
       p.group_size * kNKV > p.grid || p.grid % kCluster != 0 || splits < 1 || splits > kMaxSplits ||
       (splits > 1 && splits > p.group_size) || misaligned) {
     if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(c, kErrBadArgs, -1, -1, -1);

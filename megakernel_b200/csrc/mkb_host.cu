@@ -115,7 +115,7 @@ cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p) {
   p->mlp_out = a->mlp_out ? a->mlp_out : w->mlp;
   p->ws = w;
   p->grid = a->grid > 0 ? a->grid : grid_for(d->sms);
-  if (p->grid > d->sms || p->grid > kMaxGrid || p->grid < 128 || p->grid % kCluster != 0)
+  if (p->grid > d->sms || p->grid > kMaxGrid || p->grid < kMinGrid || p->grid % kCluster != 0)
     return cudaErrorInvalidConfiguration;
   p->group_size = p->grid / kNKV;
   p->splits = a->splits > 0 ? a->splits : 0;  // 0: chosen on the device per launch
