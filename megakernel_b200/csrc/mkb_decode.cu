@@ -512,11 +512,15 @@ __device__ __forceinline__ void load_bfrag(const Smem& sm, uint32_t bfr[kKSteps]
     bfr[st][1] = lane < 8 ? lds32(base + st * 32 + 16) : 0u;
   }
 }
-// One 16-row tile of padded 1024-wide rows at `base` (rows >= nrows read row 0).
+// One 16-row tile of padded 1024-wide rows at `base`. A row past nrows reads row
+// (tr & 7) instead, which sits in the same shared-memory banks as the row it
+// stands for: padded rows r and r + 8 share banks, so aliasing row 15 to row 0
+// (the earlier choice) put a 2-way bank conflict into every ldmatrix of the
+// tile (≈240 cycles of a 2-tile pass, measured).
 __device__ __forceinline__ void mma_tile_1024(uint32_t base, int nrows, const uint32_t bfr[kKSteps][2], float* d) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int tr = lane & 15;
-  const uint32_t row = base + (tr < nrows ? tr : 0) * kRowStride + (lane >> 4) * 16 + warp * (kKPerWarp * 2);
+  const uint32_t row = base + (tr < nrows ? tr : (tr & 7)) * kRowStride + (lane >> 4) * 16 + warp * (kKPerWarp * 2);
   float e[4] = {0.f, 0.f, 0.f, 0.f};  // second accumulator: two independent MMA chains
 #pragma unroll
   for (int st = 0; st < kKSteps; ++st) {
@@ -1214,7 +1218,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 #pragma unroll
             for (int tt = 0; tt < 4; ++tt) {
               const int rr = tt * 16 + tr16;
-              const uint32_t row = sa + (rr < nrows ? rr : 0) * kORowStride + (lane >> 4) * 16 +
+              // rows past nrows alias a row of the same bank group (see mma_tile_1024)
+              const uint32_t row = sa + (rr < nrows ? rr : (rr & 7)) * kORowStride + (lane >> 4) * 16 +
                                    warp * (kOSteps * 32);
 #pragma unroll
               for (int st = 0; st < kOSteps; ++st) {
