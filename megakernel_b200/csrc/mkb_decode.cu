@@ -1,21 +1,22 @@
 // Persistent single-launch batch-one Qwen3-0.6B decode kernel for sm_100a.
 //
-// Structure (one CTA per SM, 17 warps):
-//   * warp 16 (producer) walks this CTA's fixed chunk schedule for the whole
+// Structure (one CTA per SM, clusters of 2 CTAs, 9 warps):
+//   * warp 8 (producer) walks this CTA's fixed chunk schedule for the whole
 //     launch and streams every weight byte (and the KV rows that do not depend
 //     on the current token) into a 6 x 32 KB shared-memory ring with 1-D bulk
 //     async copies (cp.async.bulk, completion on mbarriers). It never waits on
 //     a grid transition (except a one-off acquire before re-reading KV rows in a
 //     multi-token launch), so HBM keeps streaming while the consumers wait.
-//   * warps 0-15 (consumers) run the stages of each layer and hand off between
+//   * warps 0-7 (consumers) run the stages of each layer and hand off between
 //     CTAs through the workspace without grid barriers or fences:
 //        A  : input RMSNorm + QKV GEMV rows -> tagged words (value | tag)
 //        BC : q/k RMSNorm + RoPE + KV append, GQA decode attention,
 //             o_proj partial of this KV head -> counted fixed-point
 //             red.add into acc_mid (complete when 8 heads have added)
-//        DE : post RMSNorm + gate/up SwiGLU rows + down-proj partial
-//             over the same rows of the transposed down weight
-//             -> counted red.add into acc_down (complete at G adds)
+//        DE : post RMSNorm + gate/up SwiGLU rows, SwiGLU values swapped with
+//             the cluster partner (st.async), down partial of this CTA's 512
+//             output columns over both CTAs' rows of the transposed down
+//             weight -> counted red.add into acc_down (complete at G/2 adds)
 //        (reference-layout down weight: D writes the SwiGLU vector and
 //         publishes a counter, E computes whole down rows and writes the
 //         residual, then publishes the next counter)
@@ -1046,96 +1047,101 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             const int k1 = min(kb, k0 + kKeysPerChunk);
             const int kw = k0 + warp * kKeysPerWarp;  // this warp's first key
             const uint32_t sa = ring_wait(c, n, l, 1, t, &tr);
-            // The producer skips row `pos` (the key appended this step): the warp
-            // that owns it writes the rotated K and the V row into the slot, so
-            // that every key is read the same way.
-            if (pos >= kw && pos < kw + kKeysPerWarp && pos < k1) {
-              const float4 kn = *reinterpret_cast<const float4*>(&sm.knew[lane * 4]);
-              const float4 vn = *reinterpret_cast<const float4*>(&sm.vnew[lane * 4]);
-              const uint32_t row = sa + (pos - k0) * (kHeadDim * 2) + lane * 8;
-              asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(row), "r"(pack_bf2(kn.x, kn.y)),
-                           "r"(pack_bf2(kn.z, kn.w)) : "memory");
-              asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(row + kSlotBytes / 2), "r"(pack_bf2(vn.x, vn.y)),
-                           "r"(pack_bf2(vn.z, vn.w)) : "memory");
-              fence_proxy_async_shared();  // before the slot is handed back to the bulk-copy engine
-              __syncwarp();
-            }
-            // all eight key rows of this warp (rows past k1 are in the slot but masked)
-            uint2 kr[kKeysPerWarp];
-#pragma unroll
-            for (int i = 0; i < kKeysPerWarp; ++i) kr[i] = lds64(sa + (kw + i - k0) * (kHeadDim * 2) + lane * 8);
-            float v[16];
-#pragma unroll
-            for (int i = 0; i < kKeysPerWarp; ++i) {
-              const float kx0 = bf_lo(kr[i].x), kx1 = bf_hi(kr[i].x), kx2 = bf_lo(kr[i].y), kx3 = bf_hi(kr[i].y);
-              v[i] = fmaf(q0[3], kx3, fmaf(q0[2], kx2, fmaf(q0[1], kx1, q0[0] * kx0)));
-              v[8 + i] = fmaf(q1[3], kx3, fmaf(q1[2], kx2, fmaf(q1[1], kx1, q1[0] * kx0)));
-            }
-            // value rows, loaded while the scores are reduced
-            uint2 vr[kKeysPerWarp];
-#pragma unroll
-            for (int i = 0; i < kKeysPerWarp; ++i)
-              vr[i] = lds64(sa + kSlotBytes / 2 + (kw + i - k0) * (kHeadDim * 2) + lane * 8);
-            // reduce-scatter butterfly: 16 -> 8 -> 4 -> 2 -> 1 values, then the last lane bit
-#pragma unroll
-            for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
-              const bool up = (lane & bit) != 0;
-#pragma unroll
-              for (int j = 0; j < half; ++j) {
-                const float send = up ? v[j] : v[j + half];
-                const float keep = up ? v[j + half] : v[j];
-                v[j] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+            // A warp whose 8 keys all lie past the end of the cache leaves its
+            // softmax state unchanged: skip the arithmetic (its SM sub-partition
+            // then issues for the other warp alone).
+            if (kw < k1) {
+              // The producer skips row `pos` (the key appended this step): the warp
+              // that owns it writes the rotated K and the V row into the slot, so
+              // that every key is read the same way.
+              if (pos >= kw && pos < kw + kKeysPerWarp && pos < k1) {
+                const float4 kn = *reinterpret_cast<const float4*>(&sm.knew[lane * 4]);
+                const float4 vn = *reinterpret_cast<const float4*>(&sm.vnew[lane * 4]);
+                const uint32_t row = sa + (pos - k0) * (kHeadDim * 2) + lane * 8;
+                asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(row), "r"(pack_bf2(kn.x, kn.y)),
+                             "r"(pack_bf2(kn.z, kn.w)) : "memory");
+                asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(row + kSlotBytes / 2), "r"(pack_bf2(vn.x, vn.y)),
+                             "r"(pack_bf2(vn.z, vn.w)) : "memory");
+                fence_proxy_async_shared();  // before the slot is handed back to the bulk-copy engine
+                __syncwarp();
               }
-            }
-            float s = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
-            if (kw + my_key >= k1) s = -INFINITY;
-            // online softmax for this lane's head over the warp's 8 keys
-            float mx = s;
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-            const float mnew = fmaxf(m, mx);
-            float sc = 1.f, pk = 0.f;
-            if (mnew > -INFINITY) {
-              sc = ex2_approx(m - mnew);
-              pk = s > -INFINITY ? ex2_approx(s - mnew) : 0.f;
-            }
-            float ps = pk;
-            ps += __shfl_xor_sync(0xffffffffu, ps, 2);
-            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-            lsum = lsum * sc + ps;
-            m = mnew;
-            // both heads' rescale factors and the 16 weights for the value rows
-            const float sco = __shfl_xor_sync(0xffffffffu, sc, 16);
-            const float sc0 = my_head1 ? sco : sc, sc1 = my_head1 ? sc : sco;
-            if ((lane & 1) == 0) sm.pbuf[warp][jm] = pk;
-            __syncwarp();
-            float p0[8], p1[8];
-            {
-              const float4 x = *reinterpret_cast<const float4*>(&sm.pbuf[warp][0]);
-              const float4 y = *reinterpret_cast<const float4*>(&sm.pbuf[warp][4]);
-              const float4 z = *reinterpret_cast<const float4*>(&sm.pbuf[warp][8]);
-              const float4 w = *reinterpret_cast<const float4*>(&sm.pbuf[warp][12]);
-              p0[0] = x.x; p0[1] = x.y; p0[2] = x.z; p0[3] = x.w; p0[4] = y.x; p0[5] = y.y; p0[6] = y.z; p0[7] = y.w;
-              p1[0] = z.x; p1[1] = z.y; p1[2] = z.z; p1[3] = z.w; p1[4] = w.x; p1[5] = w.y; p1[6] = w.z; p1[7] = w.w;
-            }
-            __syncwarp();
-#pragma unroll
-            for (int d = 0; d < 4; ++d) {
-              a0[d] *= sc0;
-              a1[d] *= sc1;
-            }
-#pragma unroll
-            for (int i = 0; i < kKeysPerWarp; ++i) {
-              // rows past k1 carry weight 0; select so that stale slot contents never reach the sums
-              const bool ok = kw + i < k1;
-              const float vx0 = ok ? bf_lo(vr[i].x) : 0.f, vx1 = ok ? bf_hi(vr[i].x) : 0.f;
-              const float vx2 = ok ? bf_lo(vr[i].y) : 0.f, vx3 = ok ? bf_hi(vr[i].y) : 0.f;
-              a0[0] = fmaf(p0[i], vx0, a0[0]); a0[1] = fmaf(p0[i], vx1, a0[1]);
-              a0[2] = fmaf(p0[i], vx2, a0[2]); a0[3] = fmaf(p0[i], vx3, a0[3]);
-              a1[0] = fmaf(p1[i], vx0, a1[0]); a1[1] = fmaf(p1[i], vx1, a1[1]);
-              a1[2] = fmaf(p1[i], vx2, a1[2]); a1[3] = fmaf(p1[i], vx3, a1[3]);
+              // all eight key rows of this warp (rows past k1 are in the slot but masked)
+              uint2 kr[kKeysPerWarp];
+  #pragma unroll
+              for (int i = 0; i < kKeysPerWarp; ++i) kr[i] = lds64(sa + (kw + i - k0) * (kHeadDim * 2) + lane * 8);
+              float v[16];
+  #pragma unroll
+              for (int i = 0; i < kKeysPerWarp; ++i) {
+                const float kx0 = bf_lo(kr[i].x), kx1 = bf_hi(kr[i].x), kx2 = bf_lo(kr[i].y), kx3 = bf_hi(kr[i].y);
+                v[i] = fmaf(q0[3], kx3, fmaf(q0[2], kx2, fmaf(q0[1], kx1, q0[0] * kx0)));
+                v[8 + i] = fmaf(q1[3], kx3, fmaf(q1[2], kx2, fmaf(q1[1], kx1, q1[0] * kx0)));
+              }
+              // value rows, loaded while the scores are reduced
+              uint2 vr[kKeysPerWarp];
+  #pragma unroll
+              for (int i = 0; i < kKeysPerWarp; ++i)
+                vr[i] = lds64(sa + kSlotBytes / 2 + (kw + i - k0) * (kHeadDim * 2) + lane * 8);
+              // reduce-scatter butterfly: 16 -> 8 -> 4 -> 2 -> 1 values, then the last lane bit
+  #pragma unroll
+              for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
+                const bool up = (lane & bit) != 0;
+  #pragma unroll
+                for (int j = 0; j < half; ++j) {
+                  const float send = up ? v[j] : v[j + half];
+                  const float keep = up ? v[j + half] : v[j];
+                  v[j] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+                }
+              }
+              float s = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+              if (kw + my_key >= k1) s = -INFINITY;
+              // online softmax for this lane's head over the warp's 8 keys
+              float mx = s;
+              mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+              mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+              mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+              const float mnew = fmaxf(m, mx);
+              float sc = 1.f, pk = 0.f;
+              if (mnew > -INFINITY) {
+                sc = ex2_approx(m - mnew);
+                pk = s > -INFINITY ? ex2_approx(s - mnew) : 0.f;
+              }
+              float ps = pk;
+              ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+              ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+              ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+              lsum = lsum * sc + ps;
+              m = mnew;
+              // both heads' rescale factors and the 16 weights for the value rows
+              const float sco = __shfl_xor_sync(0xffffffffu, sc, 16);
+              const float sc0 = my_head1 ? sco : sc, sc1 = my_head1 ? sc : sco;
+              if ((lane & 1) == 0) sm.pbuf[warp][jm] = pk;
+              __syncwarp();
+              float p0[8], p1[8];
+              {
+                const float4 x = *reinterpret_cast<const float4*>(&sm.pbuf[warp][0]);
+                const float4 y = *reinterpret_cast<const float4*>(&sm.pbuf[warp][4]);
+                const float4 z = *reinterpret_cast<const float4*>(&sm.pbuf[warp][8]);
+                const float4 w = *reinterpret_cast<const float4*>(&sm.pbuf[warp][12]);
+                p0[0] = x.x; p0[1] = x.y; p0[2] = x.z; p0[3] = x.w; p0[4] = y.x; p0[5] = y.y; p0[6] = y.z; p0[7] = y.w;
+                p1[0] = z.x; p1[1] = z.y; p1[2] = z.z; p1[3] = z.w; p1[4] = w.x; p1[5] = w.y; p1[6] = w.z; p1[7] = w.w;
+              }
+              __syncwarp();
+  #pragma unroll
+              for (int d = 0; d < 4; ++d) {
+                a0[d] *= sc0;
+                a1[d] *= sc1;
+              }
+  #pragma unroll
+              for (int i = 0; i < kKeysPerWarp; ++i) {
+                // rows past k1 carry weight 0; select so that stale slot contents never reach the sums
+                const bool ok = kw + i < k1;
+                const float vx0 = ok ? bf_lo(vr[i].x) : 0.f, vx1 = ok ? bf_hi(vr[i].x) : 0.f;
+                const float vx2 = ok ? bf_lo(vr[i].y) : 0.f, vx3 = ok ? bf_hi(vr[i].y) : 0.f;
+                a0[0] = fmaf(p0[i], vx0, a0[0]); a0[1] = fmaf(p0[i], vx1, a0[1]);
+                a0[2] = fmaf(p0[i], vx2, a0[2]); a0[3] = fmaf(p0[i], vx3, a0[3]);
+                a1[0] = fmaf(p1[i], vx0, a1[0]); a1[1] = fmaf(p1[i], vx1, a1[1]);
+                a1[2] = fmaf(p1[i], vx2, a1[2]); a1[3] = fmaf(p1[i], vx3, a1[3]);
+              }
             }
             ring_done(c, n);
           }
