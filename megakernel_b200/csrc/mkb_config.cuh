@@ -35,6 +35,9 @@ constexpr int kMinGrid = 128;
 // SwiGLU rows per CTA are at most kMaxJ (kInter split over at least kMinGrid CTAs).
 constexpr int kMaxJ = (kInter + kMinGrid - 1) / kMinGrid;
 constexpr int kMaxSplits = 32;
+// Caches of at least this many keys are split between the two CTAs of a cluster
+// pair that attend over the same KV head (partials swapped in shared memory).
+constexpr int kPairSplitKeys = 65;
 
 // Chunk geometry (rows per ring slot) for each streamed matrix. Rows read by
 // the tensor-core GEMVs (ldmatrix) are stored at a padded stride so that the 8
@@ -256,6 +259,28 @@ __host__ __device__ inline void key_range(int cache_len, int splits, int c, int*
   if (c >= splits) { *ka = 0; *kb = 0; return; }
   *ka = part(cache_len, splits, c);
   *kb = part(cache_len, splits, c + 1);
+}
+
+// Both CTAs of cluster pair `cta / 2` attend over the same KV head (true for
+// every pair when the head group size is even, as on 148 SMs).
+__host__ __device__ inline bool pair_shares_head(int cta, int grid, int group_size, int vocab) {
+  const Plan a = make_plan(cta & ~1, grid, group_size, vocab), b = make_plan(cta | 1, grid, group_size, vocab);
+  return a.in_bc && b.in_bc && a.h == b.h;
+}
+
+// Keys [ka, kb) this CTA attends over: its part of a split across the head
+// group's CTAs (long caches), else its half when the cluster pair shares the
+// head and the cache has at least kPairSplitKeys keys, else all keys.
+__host__ __device__ inline void attn_keys(int cache_len, int splits, int c, bool pair, int rank, int* ka, int* kb) {
+  if (splits > 1) {
+    key_range(cache_len, splits, c, ka, kb);
+  } else if (pair && cache_len >= kPairSplitKeys) {
+    *ka = part(cache_len, 2, rank);
+    *kb = part(cache_len, 2, rank + 1);
+  } else {
+    *ka = 0;
+    *kb = cache_len;
+  }
 }
 
 // Attention sequence splits for a launch whose longest cache is max_cache_len.

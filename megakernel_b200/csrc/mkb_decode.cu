@@ -47,6 +47,8 @@ struct __align__(128) Smem {
   // One phase per layer: this CTA's own arrival (with the expected byte count)
   // plus the cluster partner's SwiGLU values, each landing with complete_tx.
   uint64_t rxbar;
+  // The same for the attention partials of the partner's half of the keys.
+  uint64_t atbar;
   alignas(16) float r[kHidden];      // residual entering the current layer
   alignas(16) float rmid[kHidden];   // residual after attention + o_proj
   alignas(16) union {
@@ -65,6 +67,7 @@ struct __align__(128) Smem {
   alignas(16) float gu[2][32];
   alignas(16) float m[32];
   alignas(16) float mrx[32];  // the cluster partner's SwiGLU values (down projection)
+  alignas(16) float apeer[2][kHeadDim + 4];  // the partner's attention partial: o[128], m, l per head
   alignas(16) float pbuf[kConsumerWarps][16];  // attention weights exchanged within a warp
   float red[2 * kConsumerWarps];
   float best_v[kConsumerWarps];
@@ -345,6 +348,7 @@ template <bool kFused, bool kTraced>
 __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int pos0, int cl0,
                              int splits) {
   Producer pr(c);
+  const bool pair_attn = pair_shares_head(static_cast<int>(blockIdx.x), p.grid, p.group_size, kVocab);
   for (int t = 0; t < p.n_tokens && !pr.stop; ++t) {
     const int pos = pos0 + t;
     const int cl = cl0 + t;
@@ -367,7 +371,7 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       // BC: KV rows of this KV head (old positions only), then the o_proj slice
       if (pl.in_bc) {
         int ka, kb;
-        key_range(cl, splits, pl.c, &ka, &kb);
+        attn_keys(cl, splits, pl.c, pair_attn, static_cast<int>(cluster_ctarank()), &ka, &kb);
         if (t > 0 && kb > ka && pr.lane == 0) {
           // The previous token of this launch appended K/V at pos-1; make it
           // visible to the bulk-copy engine before re-reading those rows.
@@ -792,6 +796,9 @@ __device__ __forceinline__ void acc_clear4(uint64_t* row) {
 }
 
 static_assert(kCluster == 2 && kSlice == 2 * kConsumerThreads, "down projection: two columns per thread");
+// bytes of one pair attention exchange: o[128], m and l for each of the two heads
+constexpr uint32_t kPairAttnBytes = 2u * (kHeadDim + 2) * 4u;
+static_assert(2 * kHeadDim == kConsumerThreads, "one consumer thread per (head, dim) in the combine");
 
 
 // Bounded wait for the cluster partner's SwiGLU values of this layer; true once
@@ -799,19 +806,22 @@ static_assert(kCluster == 2 && kSlice == 2 * kConsumerThreads, "down projection:
 // an aborted partner still sends every layer until it leaves the token loop
 // (and then says so through peer_gone), and each value must have landed before
 // this CTA re-arms rxbar or exits.
-__device__ __noinline__ bool cluster_rx_wait_slow(const Ctl c, uint32_t ph, int layer, int tok) {
+// The same wait serves the attention partials (atbar).
+__device__ __noinline__ bool cluster_rx_wait_slow(const Ctl c, uint64_t* bar, uint32_t ph, int layer, int stage,
+                                                  int tok) {
   const uint64_t t0 = global_ns();
-  while (!mbar_wait_cluster(&c.sm->rxbar, ph, kSuspendNs)) {
+  while (!mbar_wait_cluster(bar, ph, kSuspendNs)) {
     if (*reinterpret_cast<volatile int*>(&c.sm->peer_gone) != 0) return false;
     if (global_ns() - t0 > c.timeout) {
-      raise_error(c, kErrTimeoutTransition, layer, kStDE, tok);
+      raise_error(c, kErrTimeoutTransition, layer, stage, tok);
       return false;
     }
   }
   return true;
 }
-__device__ __forceinline__ bool cluster_rx_wait(const Ctl& c, uint32_t ph, int layer, int tok) {
-  return mbar_wait_cluster(&c.sm->rxbar, ph, 0u) || cluster_rx_wait_slow(c, ph, layer, tok);
+__device__ __forceinline__ bool cluster_rx_wait(const Ctl& c, uint64_t* bar, uint32_t ph, int layer, int stage,
+                                                int tok) {
+  return mbar_wait_cluster(bar, ph, 0u) || cluster_rx_wait_slow(c, bar, ph, layer, stage, tok);
 }
 
 template <bool kFused, bool kTraced>
@@ -841,6 +851,13 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   const uint32_t rx_bar_peer = mapa_shared(smem_addr(&sm.rxbar), crank ^ 1u);
   const uint32_t rx_m_peer = mapa_shared(smem_addr(&sm.mrx[tid & 31]), crank ^ 1u);
   const int down_copy = (c.cta / kCluster) % kDownCopies;
+  // Attention split between the two CTAs of the pair (same KV head): partner's
+  // apeer buffer and atbar, this CTA's phase of atbar, and liveness as for rxbar.
+  const bool pair_attn = pair_shares_head(c.cta, G, p.group_size, kVocab);
+  const uint32_t apeer_remote = mapa_shared(smem_addr(&sm.apeer[0][0]), crank ^ 1u);
+  const uint32_t atbar_remote = mapa_shared(smem_addr(&sm.atbar), crank ^ 1u);
+  uint32_t aph = 0;
+  bool at_live = true;
   int flip = 0;
   float xr[32];
   Tracer<kTraced> tr{c.trace, sm.tbuf, c.trace_cap, 0, 0};
@@ -1029,7 +1046,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         // holds score j = (L >> 1) & 15 (head j >> 3, key j & 7). Online softmax
         // per warp in the exp2 domain, then a combine over the warps.
         int ka, kb;
-        key_range(cl, splits, pl.c, &ka, &kb);
+        attn_keys(cl, splits, pl.c, pair_attn, static_cast<int>(crank), &ka, &kb);
+        const bool pair_now = splits <= 1 && pair_attn && cl >= kPairSplitKeys;
         if (kb > ka) {
           float q0[4], q1[4];
           {
@@ -1166,7 +1184,27 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
               L = fmaf(sm.u.att[w][hh][kHeadDim + 1], f, L);
               O = fmaf(sm.u.att[w][hh][d], f, O);
             }
-            if (splits <= 1) {
+            if (pair_now) {
+              // this CTA's half of the keys: partial to the partner, then the
+              // partner's partial back, combined in rank order (both CTAs of the
+              // pair get identical outputs)
+              if (*reinterpret_cast<volatile int*>(&sm.peer_gone) == 0) {
+                const uint32_t dst = apeer_remote + static_cast<uint32_t>(hh * (kHeadDim + 4)) * 4u;
+                st_async_f32(dst + d * 4u, O, atbar_remote);
+                if (d == 0) {
+                  st_async_f32(dst + kHeadDim * 4u, M, atbar_remote);
+                  st_async_f32(dst + (kHeadDim + 1) * 4u, L, atbar_remote);
+                }
+              }
+              if (at_live) at_live = cluster_rx_wait(c, &sm.atbar, aph, l, kStBC, t);
+              const float Mp = sm.apeer[hh][kHeadDim], Lp = sm.apeer[hh][kHeadDim + 1], Op = sm.apeer[hh][d];
+              const float Ma = crank == 0 ? M : Mp, La = crank == 0 ? L : Lp, Oa = crank == 0 ? O : Op;
+              const float Mb = crank == 0 ? Mp : M, Lb = crank == 0 ? Lp : L, Ob = crank == 0 ? Op : O;
+              const float Mx = fmaxf(Ma, Mb);
+              const float fa = Ma > -INFINITY ? ex2_approx(Ma - Mx) : 0.f;
+              const float fb = Mb > -INFINITY ? ex2_approx(Mb - Mx) : 0.f;
+              sm.attn[tid] = fmaf(Oa, fa, Ob * fb) / fmaf(La, fa, Lb * fb);
+            } else if (splits <= 1) {
               sm.attn[tid] = O / L;
             } else {
               float* dst = ws->att_part[h][pl.c][hh];
@@ -1178,6 +1216,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             }
           }
           consumer_sync(kConsumerThreads);
+          if (pair_now) {
+            aph ^= 1u;
+            // every thread has read apeer: arm the next phase (one arrival with the
+            // expected bytes; the partner's next partial may land before or after)
+            if (at_live && tid == 0) mbar_arrive_expect_tx(&sm.atbar, kPairAttnBytes);
+          }
           if (splits > 1 && tid == 0) release_add(&ws->att_sync[l][h][0], 1u);
         }
         if (splits > 1) {
@@ -1325,7 +1369,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           down_rows(sa[0], sm.m, nj, pa0, pa1);
           ring_done_all(c, n, 1);
         }
-        if (rx_live) rx_live = cluster_rx_wait(c, xph, l, t);
+        if (rx_live) rx_live = cluster_rx_wait(c, &sm.rxbar, xph, l, kStDE, t);
         xph ^= 1u;
         {
           uint32_t sa[1];
@@ -1568,6 +1612,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
       mbar_init(&sm->empty[s], kConsumerWarps);
     }
     mbar_init(&sm->rxbar, 1);
+    mbar_init(&sm->atbar, 1);
+    mbar_arrive_expect_tx(&sm->atbar, kPairAttnBytes);  // the first pair exchange
     if (kFused) {  // the first layer's phase: one arrival plus the partner's SwiGLU bytes
       const int pc = static_cast<int>(blockIdx.x) ^ 1;
       mbar_arrive_expect_tx(&sm->rxbar, static_cast<uint32_t>(part(kInter, p.grid, pc + 1) - part(kInter, p.grid, pc)) * 4u);
