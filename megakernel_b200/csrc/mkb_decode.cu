@@ -631,6 +631,24 @@ __device__ __forceinline__ float block_sum(float v, float* s_red, int& flip) {
   return tot;
 }
 
+// RMSNorm feeding a GEMV stage with one barrier: x = v * w (without 1/rms)
+// goes to sm.xh / sm.xl alongside this warp's sum of squares; after the barrier
+// every thread adds the 8 warp sums and gets 1/rms, which scales the GEMV row
+// sums instead of x (the GEMV is linear in x; the BF16 high/remainder split of x
+// is scale-free). Same formula as megakernel.cu:704-739.
+__device__ __forceinline__ float norm_to_x(Smem& sm, const float v[4], uint2 w, int& flip) {
+  const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+  float* buf = sm.red + (flip ? kConsumerWarps : 0);
+  flip ^= 1;
+  if ((threadIdx.x & 31) == 0) buf[threadIdx.x >> 5] = ss;
+  store_x(sm, v, 1.0f, w);
+  consumer_sync(kConsumerThreads);
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kConsumerWarps; ++i) tot += buf[i];
+  return rsqrtf(tot * (1.0f / kHidden) + kEps);
+}
+
 // The 32 normalised activations this lane multiplies into every 2 KB row:
 // elements lane*8 + g*256 + e of v * rstd * w (RMSNorm, megakernel.cu:704-739).
 __device__ __forceinline__ void xr_from(const float* v, float rstd, const uint4 wv[4], float xr[32]) {
@@ -917,13 +935,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       }
       *reinterpret_cast<float4*>(&sm.r[e0]) = make_float4(r[0], r[1], r[2], r[3]);
       uint32_t bfr[kKSteps][2];
-      {
-        const float tot = block_sum(r[0] * r[0] + r[1] * r[1] + r[2] * r[2] + r[3] * r[3], sm.red, flip);
-        tr.mark(kTrMark, kSubAInput, l, t);
-        store_x(sm, r, rsqrtf(tot * (1.0f / kHidden) + kEps), wA);
-        consumer_sync(kConsumerThreads);
-        load_bfrag(sm, bfr);
-      }
+      tr.mark(kTrMark, kSubAInput, l, t);
+      const float rstd_a = norm_to_x(sm, r, wA, flip);
+      load_bfrag(sm, bfr);
       tr.mark(kTrMark, kSubANorm, l, t);
       // QKV rows: up to three padded chunks (one 16-row MMA tile each) per pass
       for (int rr = pl.qa; rr < pl.qb;) {
@@ -948,7 +962,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           const int row = (i == 0 ? ra0 : (i == 1 ? ra1 : ra2)) + (tid & 15);
           const int end = i == 0 ? ea0 : (i == 1 ? ea1 : ea2);
           if ((tid & 15) < 15 && row < end) {
-            const float val = sum_warps(xred, tid);
+            const float val = sum_warps(xred, tid) * rstd_a;
             st_tagged(&ws->qkv_tagged[l][row], val, tag);
             if (l == le - 1) {  // raw QKV outputs are reported for the last layer only
               float* dst = row < kQSize ? p.q_out + row
@@ -1306,6 +1320,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       // the next layer's input-norm weights, one stage ahead of their use
       if (l + 1 < le) wA = load_w4(lwt(c, l + 1, kWNorm));
       tr.mark(kTrWaitBegin, kStDE, l, t);
+      float rstd_d;
       {
         float a[4];
         acc_wait4(c, &ws->acc_mid[l][0], 1, static_cast<uint32_t>(kNKV), static_cast<uint32_t>(kNKV), 0, a, l, kStDE,
@@ -1314,10 +1329,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         const float4 rv = *reinterpret_cast<const float4*>(&sm.r[e0]);
         float mres[4] = {rv.x + a[0], rv.y + a[1], rv.z + a[2], rv.w + a[3]};
         *reinterpret_cast<float4*>(&sm.rmid[e0]) = make_float4(mres[0], mres[1], mres[2], mres[3]);
-        const float tot = block_sum(mres[0] * mres[0] + mres[1] * mres[1] + mres[2] * mres[2] + mres[3] * mres[3],
-                                    sm.red, flip);
-        store_x(sm, mres, rsqrtf(tot * (1.0f / kHidden) + kEps), wD);
-        consumer_sync(kConsumerThreads);
+        rstd_d = norm_to_x(sm, mres, wD, flip);
         load_bfrag(sm, bfr);
       }
       tr.mark(kTrMark, kSubDENorm, l, t);
@@ -1340,7 +1352,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         if (tid < 16 * ng) {
           const int i = (tid & 15) & 7;
           const int j = jb0 + (tid >> 4) * kGUPerChunk + i;
-          if (i < kGUPerChunk && j < nj) sm.gu[(tid & 15) >> 3][j] = sum_warps(xred, tid);
+          if (i < kGUPerChunk && j < nj) sm.gu[(tid & 15) >> 3][j] = sum_warps(xred, tid) * rstd_d;
         }
         consumer_sync(kConsumerThreads);
       }
