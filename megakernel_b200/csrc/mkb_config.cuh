@@ -141,8 +141,9 @@ struct alignas(128) Workspace {
   uint64_t qkv_tagged[kMaxLayers][kQKVRows];
   float mlp[kInter];
   float resid[kHidden];
-  float cand_val[kMaxGrid];
-  int cand_idx[kMaxGrid];
+  // Greedy-token candidate of the current token: the largest argmax key over
+  // the CTAs (red.max), read and reset by the last CTA to arrive.
+  unsigned long long tok_best[16];
 };
 
 // Fields read or cleared with 16-byte vector accesses.

@@ -260,6 +260,18 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
+// One 64-bit key per argmax candidate whose unsigned order is better()'s order:
+// order-preserving bits of the value (every NaN as one value above +inf, -0 as
+// +0) over the complement of the index (first index on ties).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+  uint32_t u = v != v ? 0x7fc00000u : (v == 0.f ? 0u : __float_as_uint(v));
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
+}
+__device__ __forceinline__ int argmax_key_index(unsigned long long k) {
+  return static_cast<int>(0xffffffffu - static_cast<uint32_t>(k & 0xffffffffull));
+}
+
 __device__ __forceinline__ float rope_at(const void* table, int fp32, size_t idx) {
   return fp32 ? __ldg(static_cast<const float*>(table) + idx)
               : __bfloat162float(static_cast<const __nv_bfloat16*>(table)[idx]);
@@ -1486,8 +1498,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             bv = sm.best_v[w];
             bi = sm.best_i[w];
           }
-        ws->cand_val[c.cta] = bv;
-        ws->cand_idx[c.cta] = bi;
+        // ordered before the arrival below by its release
+        asm volatile("red.relaxed.gpu.global.max.u64 [%0], %1;" ::"l"(&ws->tok_best[0]), "l"(argmax_key(bv, bi))
+                     : "memory");
       }
     }
     // ---- end of token: the last CTA to arrive reduces the argmax and resets ---
@@ -1516,41 +1529,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     }
     if (last_state) {
       int best = -1;
-      if (p.flags & kFlagLmHead) {
-        float v = -INFINITY;
-        int i = INT_MAX;
-        for (int k = tid; k < G; k += kConsumerThreads) {
-          const float cv = __ldcg(&ws->cand_val[k]);
-          const int ci = __ldcg(&ws->cand_idx[k]);
-          if (better(cv, ci, v, i)) {
-            v = cv;
-            i = ci;
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-          const int oi = __shfl_xor_sync(0xffffffffu, i, o);
-          if (better(ov, oi, v, i)) {
-            v = ov;
-            i = oi;
-          }
-        }
-        if (lane == 0) {
-          sm.best_v[warp] = v;
-          sm.best_i[warp] = i;
-        }
-        consumer_sync(kConsumerThreads);
-        if (tid == 0) {
-          v = sm.best_v[0];
-          i = sm.best_i[0];
-          for (int w = 1; w < kConsumerWarps; ++w)
-            if (better(sm.best_v[w], sm.best_i[w], v, i)) {
-              v = sm.best_v[w];
-              i = sm.best_i[w];
-            }
-          best = i;
-        }
+      if ((p.flags & kFlagLmHead) && tid == 0) {
+        best = argmax_key_index(__ldcg(&ws->tok_best[0]));
+        ws->tok_best[0] = 0ull;  // for the next token (ordered by the release below)
       }
       // the last two layers' accumulators (earlier ones were cleared on the way)
       for (int l = max(lb, le - 2); l < le; ++l) {
@@ -1579,8 +1560,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           ws->tag_base[0] = tag0 + static_cast<uint32_t>(p.n_tokens);
         } else {
           ws->tok_flag[1] = static_cast<uint32_t>(best);
-          __threadfence();
-          st_release(&ws->tok_flag[0], static_cast<uint32_t>(t + 1));
+          st_release(&ws->tok_flag[0], static_cast<uint32_t>(t + 1));  // covers the CTA's writes above
         }
       }
     }
