@@ -111,6 +111,10 @@ typedef struct mkb_decode_args {
                                   16 ring slot fill wait, 17 producer slot wait,
                                   18 chunk issue) */
   int trace_cap;
+  const int* prompt_tokens;    /* device int[n_tokens] or NULL: prefill mode. Token t of the
+                                  launch is prompt_tokens[t] (not the previous argmax), and
+                                  the LM head runs for the last token only. No counterpart
+                                  in the reference (model.py:72-87 prefills with HF). */
 } mkb_decode_args;
 
 void mkb_decode_args_init(mkb_decode_args* a);
@@ -166,6 +170,14 @@ cudaError_t mkb_engine_step(mkb_engine* e, int token, int position, int* next_to
  * ids land in out_tokens (device, n entries). Asynchronous. */
 cudaError_t mkb_engine_generate(mkb_engine* e, int token, int position, int n, int* out_tokens,
                                 cudaStream_t stream);
+/* In-engine prefill: the n prompt ids (device int[n]) enter at positions
+ * position .. position+n-1 in one persistent launch that appends their K/V rows;
+ * the LM head runs for the last one only, whose argmax (the first generated
+ * token) is written to *next_token (device int, may be NULL) and whose logits
+ * stay in mkb_engine_logits(). Asynchronous. Replaces the HF prefill of
+ * model.py:72-87 (no counterpart in the reference's kernel). */
+cudaError_t mkb_engine_prefill(mkb_engine* e, const int* prompt_tokens, int n, int position, int* next_token,
+                               cudaStream_t stream);
 float* mkb_engine_logits(mkb_engine* e);   /* device [vocab], last token's logits */
 void* mkb_engine_workspace(mkb_engine* e);
 int mkb_engine_grid(mkb_engine* e);

@@ -65,6 +65,7 @@ class DecodeArgs(Structure):
         ("withhold_cta", c_int),
         ("trace", c_void_p),
         ("trace_cap", c_int),
+        ("prompt_tokens", c_void_p),
     ]
 
 
@@ -110,6 +111,7 @@ SIGNATURES = [
     ("mkb_engine_create", c_int, [POINTER(Model), POINTER(c_void_p)]),
     ("mkb_engine_step", c_int, [c_void_p, c_int, c_int, POINTER(c_int), c_void_p]),
     ("mkb_engine_generate", c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    ("mkb_engine_prefill", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     ("mkb_engine_logits", c_void_p, [c_void_p]),
     ("mkb_engine_workspace", c_void_p, [c_void_p]),
     ("mkb_engine_grid", c_int, [c_void_p]),

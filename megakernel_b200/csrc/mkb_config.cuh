@@ -187,6 +187,7 @@ struct DecodeParams {
                                      // QKV arrival (-1 = off); the others time out
   unsigned long long* trace;         // optional [2*grid][trace_cap] stage time stamps
   int trace_cap;
+  const int* prompt;                 // prefill: forced input tokens [n_tokens], LM head on the last only
 };
 
 // Trace record: (code << 48) | (globaltimer ns & 0xffffffffffff). Row cta is

@@ -467,7 +467,8 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         }
       }
     }
-    if (p.flags & kFlagLmHead) {
+    // LM-head rows (prefill: for the last prompt token only)
+    if ((p.flags & kFlagLmHead) && (p.prompt == nullptr || t == p.n_tokens - 1)) {
       for (int v0 = pl.va; v0 < pl.vb; v0 += kRowsPerChunk1024) {
         const int v1 = min(pl.vb, v0 + kRowsPerChunk1024);
         const uint32_t bytes = static_cast<uint32_t>(v1 - v0) * kHidden * 2u;
@@ -900,15 +901,23 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     const uint32_t tgtG = static_cast<uint32_t>(G * (t + 1));
     const uint32_t tag = tag0 + static_cast<uint32_t>(t) + 1u;
     tr.mark(kTrMark, kStToken, 0, t);
+    // Prefill (p.prompt): the inputs are given, and the LM head (and the wait
+    // for the last layer's sums that feeds it) runs for the last token only.
+    const bool last_tok = t == p.n_tokens - 1;
+    const bool lm_now = (p.flags & kFlagLmHead) && (p.prompt == nullptr || last_tok);
 
     // ---- token input: embedding gather (megakernel.cu:783-795) ----
     if (t > 0) {
+      // the previous token is complete (and its last CTA has reset the shared state)
       if (tid == 0) spin_geq(c, &ws->tok_flag[0], static_cast<uint32_t>(t), kErrTimeoutToken, -1, 9, t);
       consumer_sync(kConsumerThreads);
-      if (tid == 0) sm.token = static_cast<int>(__ldcg(reinterpret_cast<const int*>(&ws->tok_flag[1])));
-      consumer_sync(kConsumerThreads);
-      token = sm.token;
+      if (p.prompt == nullptr) {
+        if (tid == 0) sm.token = static_cast<int>(__ldcg(reinterpret_cast<const int*>(&ws->tok_flag[1])));
+        consumer_sync(kConsumerThreads);
+        token = sm.token;
+      }
     }
+    if (p.prompt != nullptr) token = __ldg(p.prompt + t);
     token = min(max(token, 0), kVocab - 1);
     float r[4];
     if (p.input_residual) {
@@ -1446,7 +1455,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     // ================= final residual, LM head + argmax (megakernel.cu:870-886) ==
     uint4 fwv[4];
     load_norm_w((p.flags & kFlagSkipFinalNorm) ? nullptr : p.final_norm, fwv);
-    if (le > lb) {
+    if (le > lb && (p.prompt == nullptr || last_tok)) {
       if constexpr (fused) {
         tr.mark(kTrWaitBegin, kStLM, le - 1, t);
         float d[4];
@@ -1466,7 +1475,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       *reinterpret_cast<float4*>(p.residual_out + e0) = make_float4(r[0], r[1], r[2], r[3]);
     float bv = -INFINITY;
     int bi = INT_MAX;
-    if (p.flags & kFlagLmHead) {
+    if (lm_now) {
       const float tot = block_sum(r[0] * r[0] + r[1] * r[1] + r[2] * r[2] + r[3] * r[3], sm.red, flip);
       const float rstd = (p.flags & kFlagSkipFinalNorm) ? 1.0f : rsqrtf(tot * (1.0f / kHidden) + kEps);
       xr_from(sm.r, rstd, fwv, xr);
@@ -1529,7 +1538,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     }
     if (last_state) {
       int best = -1;
-      if ((p.flags & kFlagLmHead) && tid == 0) {
+      if (lm_now && tid == 0) {
         best = argmax_key_index(__ldcg(&ws->tok_best[0]));
         ws->tok_best[0] = 0ull;  // for the next token (ordered by the release below)
       }
@@ -1538,7 +1547,6 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         acc_clear4(&ws->acc_mid[l][0]);
         for (int q = 0; q < kDownCopies; ++q) acc_clear4(&ws->acc_down[l][q][0]);
       }
-      const bool last_tok = t == p.n_tokens - 1;
       if (last_tok) {
         for (int i = tid; i < kMaxLayers * 4; i += kConsumerThreads) ws->sync[i >> 2][i & 3][0] = 0u;
         for (int i = tid; i < kMaxLayers * kNKV; i += kConsumerThreads) ws->kv_ready[i / kNKV][i % kNKV][0] = 0u;
@@ -1546,7 +1554,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       }
       consumer_sync(kConsumerThreads);
       if (tid == 0) {
-        if (p.flags & kFlagLmHead) {
+        if (lm_now) {
           if (p.out_tokens != nullptr) p.out_tokens[t] = best;
           if (p.step != nullptr && (p.flags & kFlagAdvanceStep)) {
             p.step[0] = best;

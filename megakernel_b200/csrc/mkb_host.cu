@@ -124,6 +124,7 @@ cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p) {
   p->withhold_cta = a->withhold_cta;
   p->trace = a->trace;
   p->trace_cap = a->trace ? a->trace_cap : 0;
+  p->prompt = a->prompt_tokens;
   // Host-side validation of what the host can see (the kernel re-checks the rest).
   if (!p->embed || !p->layers || !p->k_cache || !p->v_cache || !p->cos_table || !p->sin_table)
     return cudaErrorInvalidValue;
@@ -279,6 +280,7 @@ struct mkb_engine {
   void* ws = nullptr;
   int* d_step = nullptr;                      // {token, position, -, count}
   int* d_out = nullptr;                       // argmax of the last step
+  int* d_pf = nullptr;                        // [max_seq] prefill launch ids (last one used)
   float* d_logits = nullptr;
   bool own_logits = false;
   int* h_io = nullptr;                        // pinned: [0..3] in, [4..7] out
@@ -298,6 +300,7 @@ void engine_free(mkb_engine* e) {
   cudaFree(e->ws);
   cudaFree(e->d_step);
   cudaFree(e->d_out);
+  cudaFree(e->d_pf);
   if (e->own_logits) cudaFree(e->d_logits);
   if (e->h_io) cudaFreeHost(e->h_io);
   delete e;
@@ -369,6 +372,7 @@ cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
   MKB_TRY(cudaMalloc(&e->d_step, 4 * sizeof(int)));
   MKB_TRY(cudaMemset(e->d_step, 0, 4 * sizeof(int)));
   MKB_TRY(cudaMalloc(&e->d_out, 4 * sizeof(int)));
+  MKB_TRY(cudaMalloc(&e->d_pf, sizeof(int) * m->max_seq));
   if (m->logits) {
     e->d_logits = m->logits;
   } else {
@@ -455,6 +459,23 @@ cudaError_t mkb_engine_generate(mkb_engine* e, int token, int position, int n, i
   a.n_tokens = n;
   a.out_tokens = out_tokens;
   return mkb_decode(&a, stream);
+}
+
+cudaError_t mkb_engine_prefill(mkb_engine* e, const int* prompt_tokens, int n, int position, int* next_token,
+                               cudaStream_t stream) {
+  if (!e || !prompt_tokens || n < 1) return cudaErrorInvalidValue;
+  if (position < 0 || position + n > e->max_seq) return cudaErrorInvalidValue;
+  mkb_decode_args a = e->step_args;
+  a.step = nullptr;
+  a.token = 0;  // the inputs come from prompt_tokens (ids are clamped on the device)
+  a.position = position;
+  a.cache_len = position + 1;
+  a.n_tokens = n;
+  a.prompt_tokens = prompt_tokens;
+  a.out_tokens = e->d_pf;  // only entry n-1 (the last prompt token) is written
+  cudaError_t err = mkb_decode(&a, stream);
+  if (err != cudaSuccess || !next_token) return err;
+  return cudaMemcpyAsync(next_token, e->d_pf + (n - 1), sizeof(int), cudaMemcpyDeviceToDevice, stream);
 }
 
 float* mkb_engine_logits(mkb_engine* e) { return e ? e->d_logits : nullptr; }

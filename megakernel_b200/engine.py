@@ -142,6 +142,27 @@ class DecodeEngine:
         _lib.check(code, "mkb_engine_generate")
         return out
 
+    def prefill(self, ids, position: int = 0, stream=None) -> int:
+        """In-engine prefill of prompt ``ids`` at ``position``.. (one persistent launch
+        appends their K/V rows; model.py:72-87 did this with HF). Returns the argmax
+        of the last prompt token, the first generated token; ``logits`` holds its
+        logits."""
+        ids = torch.as_tensor(ids, dtype=torch.int32).flatten()
+        n = int(ids.numel())
+        _require(n >= 1 and 0 <= position and position + n <= self.max_seq, "prefill range out of bounds")
+        _require(bool(((ids >= 0) & (ids < VOCAB)).all()), "token_id out of range")
+        dev_ids = ids.to(self.device)
+        nxt = torch.empty(1, dtype=torch.int32, device=self.device)
+        with torch.cuda.device(self.device):
+            code = self.lib.mkb_engine_prefill(self._h, c_void_p(dev_ids.data_ptr()), n, int(position),
+                                               c_void_p(nxt.data_ptr()), c_void_p(_stream_ptr(stream)))
+        _lib.check(code, "mkb_engine_prefill")
+        out = int(nxt.item())
+        st = self.status()
+        if st[0] != 0:
+            raise RuntimeError(f"in-kernel error {st}")
+        return out
+
     def status(self) -> list:
         return _lib.workspace_status(self.workspace_ptr)
 

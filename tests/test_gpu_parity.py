@@ -320,6 +320,64 @@ def test_generate_matches_stepwise_split_attention(w_gpu):
     eng.close()
 
 
+@pytest.mark.parametrize("n_prompt", [32, 200])
+def test_engine_prefill_matches_hf(n_prompt, w_gpu, hf_model):
+    """In-engine prefill (one persistent launch, forced inputs, LM head on the last
+    token only) against HF's prefill of the same prompt: the K/V rows it appends,
+    the last prompt token's logits and greedy id, and the decode steps that follow
+    from that cache. 200 tokens cross the cluster-pair attention split (65+ keys)."""
+    ids = C.config0_prompt(0) if n_prompt == 32 else torch.randint(0, 151936, (n_prompt,),
+                                                                      generator=torch.Generator().manual_seed(5))
+    ids = ids.view(-1)[:n_prompt]
+    logits_hf, cache, kh, vh = prefill_to_gpu(hf_model, ids, 512)
+    kg, vg = torch.zeros_like(kh), torch.zeros_like(vh)
+    eng = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), kg, vg)
+    nxt = eng.prefill(ids)
+    lg = eng.logits.cpu()
+    assert (lg - logits_hf).abs().max().item() <= 2e-2
+    assert cosine(lg, logits_hf) > 0.999
+    t2 = torch.topk(logits_hf.double(), 2).values
+    if float(t2[0] - t2[1]) > 0.05:
+        assert nxt == int(torch.argmax(logits_hf))
+    # the appended rows: BF16 roundings of slightly different FP32 paths
+    for got, ref in ((kg[:, :, :n_prompt], kh[:, :, :n_prompt]), (vg[:, :, :n_prompt], vh[:, :, :n_prompt])):
+        torch.testing.assert_close(got.float(), ref.float(), rtol=2e-2, atol=2e-2)
+    assert not kg[:, :, n_prompt:].any()  # nothing past the prompt
+    tok = int(torch.argmax(logits_hf))
+    for i in range(4):
+        nxt = eng.step(tok, n_prompt + i)
+        ref, cache = H.step(hf_model, cache, tok)
+        lg = eng.logits.cpu()
+        assert (lg - ref).abs().max().item() <= 2e-2, f"step {i}"
+        assert cosine(lg, ref) > 0.999
+        tok = int(torch.argmax(ref))
+    assert eng.status()[0] == 0
+    eng.close()
+
+
+def test_engine_prefill_matches_stepwise_prefill(w_gpu):
+    """The prefill launch appends the same K/V rows (within 2 BF16 ulp) as feeding
+    the prompt one decode step at a time, and ends on the same greedy id."""
+    ids = torch.randint(0, 151936, (80,), generator=torch.Generator().manual_seed(9))
+    k1 = torch.zeros((28, 8, 512, 128), dtype=torch.bfloat16, device=DEV)
+    v1, k2, v2 = torch.zeros_like(k1), torch.zeros_like(k1), torch.zeros_like(k1)
+    e1 = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), k1, v1)
+    nxt1 = e1.prefill(ids)
+    l1 = e1.logits.cpu()
+    e2 = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), k2, v2)
+    for i, t in enumerate(ids.tolist()):
+        nxt2 = e2.step(t, i)
+    l2 = e2.logits.cpu()
+    assert (l1 - l2).abs().max().item() <= 2e-3
+    t2 = torch.topk(l2.double(), 2).values
+    if float(t2[0] - t2[1]) > 1e-3:
+        assert nxt1 == nxt2
+    for got, ref in ((k1, k2), (v1, v2)):
+        torch.testing.assert_close(got.float(), ref.float(), rtol=1.6e-2, atol=1e-3)
+    e1.close()
+    e2.close()
+
+
 def test_repeat_is_deterministic_within_fp32_noise(w_gpu, hf_model, config0_hf):
     g, fed, _ = config0_hf
     _, _, kg, vg = prefill_to_gpu(hf_model, torch.from_numpy(g["prompt"]), 512)
