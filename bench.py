@@ -282,11 +282,8 @@ def main():
     eng = mk.DecodeEngine(embed, final_norm, layers, k, v, fused_down=True, use_graph=True)
     g = torch.Generator().manual_seed(rank)
     prompt = torch.randint(0, VOCAB, (PROMPT,), generator=g).tolist()
-    # prefill the cache by decoding the prompt through the engine (positions 0..31)
-    tok = prompt[0]
-    for p in range(PROMPT):
-        nxt = eng.step(prompt[p], p)
-    first = nxt
+    # in-engine prefill of the prompt (positions 0..31, one launch)
+    first = eng.prefill(prompt)
     span = MAX_SEQ - PROMPT
     steps, warm = max(1, a.steps), max(3, a.warmup)
 
