@@ -1132,8 +1132,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
               // value rows, loaded while the scores are reduced
               uint2 vr[kKeysPerWarp];
   #pragma unroll
-              for (int i = 0; i < kKeysPerWarp; ++i)
-                vr[i] = lds64(sa + kSlotBytes / 2 + (kw + i - k0) * (kHeadDim * 2) + lane * 8);
+              for (int i = 0; i < kKeysPerWarp; ++i) {
+                // rows past k1 are zeroed here (2 selects a row), so stale slot
+                // contents never reach the sums below
+                const uint2 x = lds64(sa + kSlotBytes / 2 + (kw + i - k0) * (kHeadDim * 2) + lane * 8);
+                vr[i] = kw + i < k1 ? x : make_uint2(0u, 0u);
+              }
               // reduce-scatter butterfly: 16 -> 8 -> 4 -> 2 -> 1 values, then the last lane bit
   #pragma unroll
               for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
@@ -1186,10 +1190,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
               }
   #pragma unroll
               for (int i = 0; i < kKeysPerWarp; ++i) {
-                // rows past k1 carry weight 0; select so that stale slot contents never reach the sums
-                const bool ok = kw + i < k1;
-                const float vx0 = ok ? bf_lo(vr[i].x) : 0.f, vx1 = ok ? bf_hi(vr[i].x) : 0.f;
-                const float vx2 = ok ? bf_lo(vr[i].y) : 0.f, vx3 = ok ? bf_hi(vr[i].y) : 0.f;
+                const float vx0 = bf_lo(vr[i].x), vx1 = bf_hi(vr[i].x);
+                const float vx2 = bf_lo(vr[i].y), vx3 = bf_hi(vr[i].y);
                 a0[0] = fmaf(p0[i], vx0, a0[0]); a0[1] = fmaf(p0[i], vx1, a0[1]);
                 a0[2] = fmaf(p0[i], vx2, a0[2]); a0[3] = fmaf(p0[i], vx3, a0[3]);
                 a1[0] = fmaf(p1[i], vx0, a1[0]); a1[1] = fmaf(p1[i], vx1, a1[1]);
