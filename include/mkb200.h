@@ -188,6 +188,11 @@ void mkb_engine_destroy(mkb_engine* e);
 int mkb_plan_query(int grid, int cta, int32_t out[16]);
 int mkb_choose_splits(int max_cache_len, int group_size);
 void mkb_key_range(int cache_len, int splits, int c, int32_t out[2]);
+/* Keys [out[0], out[1]) that CTA `cta` of a `grid`-CTA launch attends over at
+ * this cache length (split across the head group, or halved between the two
+ * CTAs of a cluster pair that share the KV head); returns whether the pair
+ * shares its head. */
+int mkb_attn_keys(int cache_len, int splits, int grid, int cta, int32_t out[2]);
 int mkb_qkv_chunk_end(int r, int qb);
 size_t mkb_smem_bytes(void);
 int mkb_version(void);

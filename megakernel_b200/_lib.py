@@ -119,6 +119,7 @@ SIGNATURES = [
     ("mkb_plan_query", c_int, [c_int, c_int, POINTER(c_int32)]),
     ("mkb_choose_splits", c_int, [c_int, c_int]),
     ("mkb_key_range", None, [c_int, c_int, c_int, POINTER(c_int32)]),
+    ("mkb_attn_keys", c_int, [c_int, c_int, c_int, c_int, POINTER(c_int32)]),
     ("mkb_qkv_chunk_end", c_int, [c_int, c_int]),
     ("mkb_smem_bytes", c_size_t, []),
     ("mkb_version", c_int, []),

@@ -263,6 +263,16 @@ void mkb_key_range(int cache_len, int splits, int c, int32_t out[2]) {
   out[1] = b;
 }
 int mkb_qkv_chunk_end(int r, int qb) { return qkv_chunk_end(r, qb); }
+int mkb_attn_keys(int cache_len, int splits, int grid, int cta, int32_t out[2]) {
+  const int gs = grid / kNKV;
+  const Plan p = make_plan(cta, grid, gs, kVocab);
+  const bool pair = pair_shares_head(cta, grid, gs, kVocab);
+  int a, b;
+  attn_keys(cache_len, splits, p.c, pair, cta & 1, &a, &b);
+  out[0] = a;
+  out[1] = b;
+  return pair ? 1 : 0;
+}
 
 }  // extern "C"
 

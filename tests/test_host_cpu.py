@@ -1,6 +1,7 @@
 """Host-side checks that need no GPU: the C ABI library loads and exports every
 declared symbol, the static work split covers every row exactly once, and the
 Python entry points reject bad arguments before any CUDA call."""
+import ctypes
 import os
 import re
 
@@ -110,3 +111,33 @@ def test_extension_decode_rejects_bad_arguments():
     e = torch.zeros((4, 4), dtype=torch.bfloat16)
     with pytest.raises(ValueError):
         ext.decode(0, e, e, e, [e] * 308, e, e, e, e, 0, 512)
+
+
+@pytest.mark.parametrize("grid", [128, 140, 148, 160, 256])
+@pytest.mark.parametrize("cache_len", [1, 33, 64, 65, 100, 160, 384])
+def test_cluster_pair_attention_halves_cover_the_cache(grid, cache_len):
+    """Below the group split (caches up to 384 keys), a CTA attends over all keys,
+    or, from kPairSplitKeys (65) on, when its cluster pair shares the KV head,
+    over one half: the two halves of a pair tile [0, cache_len) exactly."""
+    lib = _lib.load()
+    for cta in range(0, grid, 2):
+        outs, pairs = [], []
+        for r in (0, 1):
+            o = (ctypes.c_int32 * 2)()
+            pairs.append(lib.mkb_attn_keys(cache_len, 1, grid, cta + r, o))
+            outs.append((o[0], o[1]))
+        assert pairs[0] == pairs[1]
+        plan = _lib.plan(grid, cta)
+        if plan["in_bc"] and grid // 8 % 2 == 0:
+            assert pairs[0] == 1  # even group sizes put both CTAs of a pair on one head
+        if pairs[0] and cache_len >= 65:
+            assert outs[0][0] == 0 and outs[0][1] == outs[1][0] and outs[1][1] == cache_len
+            assert outs[0][1] - outs[0][0] >= 1 and outs[1][1] - outs[1][0] >= 1
+        else:
+            assert outs == [(0, cache_len), (0, cache_len)]
+
+
+def test_engine_prefill_rejects_bad_arguments():
+    lib = _lib.load()
+    ids = (ctypes.c_int * 4)(1, 2, 3, 4)
+    assert lib.mkb_engine_prefill(None, ctypes.cast(ids, ctypes.c_void_p), 4, 0, None, None) != 0
