@@ -13,7 +13,8 @@ architecture with random-init BF16 weights (synthetic data), max cache 512, a
   runs its own replica (prompt seed = rank) and value = all tokens / max time.
 * e2e: the same metric through the public per-token call (mkb_engine_step):
   every step copies (token, position) host->device from pinned memory, replays
-  the CUDA graph and reads the argmax id (and status word) back to the host.
+  the CUDA graph, and the kernel's last CTA stores the argmax id into the
+  engine's pinned (mapped) host memory, which the host reads after the sync.
 * roofline: decode_kernel's algorithmic bytes (every weight byte once per token
   + KV bytes read) / its measured launch duration, against the measured HBM peak.
 * cpu_baseline: HF Qwen3 FP32 decode on this host's cores (oracle), rank 0, N=1.
@@ -361,8 +362,9 @@ def main():
                        "l2": "inputs larger than L2: 1.19 GB of weights streamed per token vs 126 MB L2",
                        "us_per_token": dev_ms * 1000.0 / steps, "tokens_per_launch": toks_per_launch},
             "e2e": {"value": replica_throughput(world, steps, e2e_ms), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 8, "us_per_token": e2e_ms * 1000.0 / steps,
-                    "api": "mkb_engine_step (graph replay, host token in/out)"},
+                    "d2h_bytes_per_step": 4, "us_per_token": e2e_ms * 1000.0 / steps,
+                    "api": "mkb_engine_step (8 B copied in from pinned memory, graph replay, the kernel "
+                           "stores the 4 B argmax into pinned host memory)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
                          "traffic": traffic,

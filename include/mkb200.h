@@ -163,8 +163,10 @@ typedef struct mkb_model {
 
 typedef struct mkb_engine mkb_engine;
 cudaError_t mkb_engine_create(const mkb_model* model, mkb_engine** out);
-/* One token: host->device copy of (token, position), graph replay, device->host
- * copy of the argmax id; synchronises `stream`. */
+/* One token: host->device copy of (token, position), graph replay; the kernel
+ * stores the argmax id straight into the engine's pinned (mapped) host memory.
+ * Synchronises `stream`; the workspace status is read only when the token did
+ * not complete. */
 cudaError_t mkb_engine_step(mkb_engine* e, int token, int position, int* next_token, cudaStream_t stream);
 /* n greedy tokens in one persistent launch, starting from `token` at `position`;
  * ids land in out_tokens (device, n entries). Asynchronous. */

@@ -289,11 +289,13 @@ struct mkb_engine {
   __nv_bfloat16** d_down_t = nullptr;         // n_layers pointers
   void* ws = nullptr;
   int* d_step = nullptr;                      // {token, position, -, count}
-  int* d_out = nullptr;                       // argmax of the last step
   int* d_pf = nullptr;                        // [max_seq] prefill launch ids (last one used)
   float* d_logits = nullptr;
   bool own_logits = false;
-  int* h_io = nullptr;                        // pinned: [0..3] in, [4..7] out
+  // Pinned, mapped host words: [0..1] (token, position) copied in each step,
+  // [4] the argmax, stored there by the kernel's last CTA (no copy back).
+  int* h_io = nullptr;
+  int* d_io = nullptr;                        // device address of h_io
   cudaGraphExec_t graph = nullptr;
   cudaStream_t cap_stream = nullptr;
   mkb_decode_args step_args;
@@ -309,7 +311,6 @@ void engine_free(mkb_engine* e) {
   cudaFree(e->d_down_t);
   cudaFree(e->ws);
   cudaFree(e->d_step);
-  cudaFree(e->d_out);
   cudaFree(e->d_pf);
   if (e->own_logits) cudaFree(e->d_logits);
   if (e->h_io) cudaFreeHost(e->h_io);
@@ -381,7 +382,6 @@ cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
   MKB_TRY(cudaMemset(e->ws, 0, sizeof(Workspace)));
   MKB_TRY(cudaMalloc(&e->d_step, 4 * sizeof(int)));
   MKB_TRY(cudaMemset(e->d_step, 0, 4 * sizeof(int)));
-  MKB_TRY(cudaMalloc(&e->d_out, 4 * sizeof(int)));
   MKB_TRY(cudaMalloc(&e->d_pf, sizeof(int) * m->max_seq));
   if (m->logits) {
     e->d_logits = m->logits;
@@ -389,7 +389,9 @@ cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
     MKB_TRY(cudaMalloc(&e->d_logits, sizeof(float) * kVocab));
     e->own_logits = true;
   }
-  MKB_TRY(cudaMallocHost(&e->h_io, 8 * sizeof(int)));
+  MKB_TRY(cudaHostAlloc(&e->h_io, 8 * sizeof(int), cudaHostAllocMapped));
+  for (int i = 0; i < 8; ++i) e->h_io[i] = 0;
+  MKB_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->d_io), e->h_io, 0));
   MKB_TRY(cudaDeviceSynchronize());
 
   mkb_decode_args& a = e->step_args;
@@ -411,7 +413,7 @@ cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
   a.n_tokens = 1;
   a.flags = MKB_FLAG_LM_HEAD;
   a.logits = e->d_logits;
-  a.out_tokens = e->d_out;
+  a.out_tokens = e->d_io + 4;  // the last CTA writes the argmax straight into host memory
   a.workspace = e->ws;
   a.grid = e->grid;
 
@@ -439,21 +441,21 @@ cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
 cudaError_t mkb_engine_step(mkb_engine* e, int token, int position, int* next_token, cudaStream_t stream) {
   if (!e) return cudaErrorInvalidValue;
   if (token < 0 || token >= kVocab || position < 0 || position >= e->max_seq) return cudaErrorInvalidValue;
-  e->h_io[0] = token;
-  e->h_io[1] = position;
+  volatile int* io = e->h_io;
+  io[0] = token;
+  io[1] = position;
+  io[4] = -1;  // stays -1 unless the token completes (no CTA stopped on an error)
   cudaError_t err = cudaMemcpyAsync(e->d_step, e->h_io, 2 * sizeof(int), cudaMemcpyHostToDevice, stream);
   if (err != cudaSuccess) return err;
   err = e->graph ? cudaGraphLaunch(e->graph, stream) : mkb_decode(&e->step_args, stream);
   if (err != cudaSuccess) return err;
-  err = cudaMemcpyAsync(e->h_io + 4, e->d_out, sizeof(int), cudaMemcpyDeviceToHost, stream);
-  if (err != cudaSuccess) return err;
-  err = cudaMemcpyAsync(e->h_io + 5, static_cast<Workspace*>(e->ws)->error, sizeof(uint32_t),
-                        cudaMemcpyDeviceToHost, stream);
-  if (err != cudaSuccess) return err;
   err = cudaStreamSynchronize(stream);
   if (err != cudaSuccess) return err;
-  if (e->h_io[5] != 0) return engine_check_status(e);
-  if (next_token) *next_token = e->h_io[4];
+  if (io[4] < 0) {
+    const cudaError_t st = engine_check_status(e);
+    return st != cudaSuccess ? st : cudaErrorLaunchFailure;
+  }
+  if (next_token) *next_token = io[4];
   return cudaSuccess;
 }
 
