@@ -793,15 +793,16 @@ __device__ __noinline__ void acc_wait_pair(const Ctl c, const uint64_t* row, int
 }
 // This thread's 4 elements of a [copies][kHidden] accumulator row, each
 // complete with `expect` contributions in total. One thread of the CTA polls a
-// sentinel element of copy 0 only (complete at `expect0` contributions) and
-// the others wait at a barrier: every poll competes with the atomics landing on
-// the same L2 lines, so the fewer poll loads the faster the exchange
-// (measured). Elements still incomplete after the barrier are polled by their
-// owners.
+// sentinel element of copy 0 (complete at `expect0` contributions), a thread of
+// another warp the same element of copy 1 when there is one, and the others
+// wait at a barrier: every poll competes with the atomics landing on the same
+// L2 lines, so the fewer poll loads the faster the exchange (measured).
+// Elements still incomplete after the barrier are polled by their owners.
 __device__ __forceinline__ void acc_wait4(const Ctl& c, const uint64_t* row, int copies, uint32_t expect,
                                           uint32_t expect0, int s0, float v[4], int layer, int stage, int tok) {
   const uint64_t* w = row + threadIdx.x * kE;
   if (threadIdx.x == 0) acc_wait_pair(c, row, 1, expect0, s0, -1, layer, stage, tok);
+  if (threadIdx.x == 32 && copies > 1) acc_wait_pair(c, row + kHidden, 1, expect - expect0, s0, -1, layer, stage, tok);
   consumer_sync(kConsumerThreads);
   uint64_t low[4] = {0, 0, 0, 0}, cn[4] = {0, 0, 0, 0};
   for (int q = 0; q < copies; ++q) {
