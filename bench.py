@@ -1,11 +1,16 @@
 #!/usr/bin/env python
 """Batch-one Qwen3-0.6B decode benchmark on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mkb|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mkb|reference] [--config 0|2|3]
 
 One step = one greedy decode token (batch 1) of the 28-layer Qwen3-0.6B
 architecture with random-init BF16 weights (synthetic data), max cache 512, a
 32-token prompt, positions 32.. (config 0). Prints ONE JSON line on rank 0.
+
+``--config 2``: one step = one launch of the isolated LM head + argmax
+(151936 x 1024 BF16 weight, hidden N(0,1) taken as normalised).
+``--config 3``: config 0 with a 4096-slot cache, the 3584-token prompt prefilled
+in-engine, 256 greedy steps at positions 3584.. (cache lengths 3585..3840).
 
 * value: tokens/s of the on-device greedy loop (DecodeEngine.generate: one
   persistent launch decodes the K tokens, argmax feeding the next embedding),
@@ -45,6 +50,7 @@ HIDDEN, INTER, VOCAB, LAYERS = 1024, 3072, 151936, 28
 PROMPT, MAX_SEQ = 32, 512
 WEIGHT_BYTES = LAYERS * (31_457_280 + 4_608) + 311_164_928 + 2_048 + 2_048   # 1,192,101,888
 KV_BYTES_PER_POS = LAYERS * 8 * 128 * 2 * 2                                   # 114,688
+LM_BYTES = 311_164_928 + HIDDEN * 4                                           # LM head weight + FP32 hidden
 METRIC = "batch-1 decode tok/s (Qwen3-0.6B, 512-token cache)"
 
 
@@ -55,6 +61,7 @@ def args_parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["mkb", "reference"], default="mkb")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, choices=[0, 2, 3], default=0)
     return ap.parse_args()
 
 
@@ -236,6 +243,10 @@ def cpu_baseline(steps_cap: int = 128, budget_s: float = 12.0):
 def run_reference(a, rank, world):
     if rank != 0:
         return
+    if a.config != 0:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference arm is measured on config 0 only "
+                          "(its CPU model path takes minutes per step at these sizes)"}), flush=True)
+        return
     base = cpu_baseline(steps_cap=max(a.steps, 1), budget_s=60.0)
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": a.gpus,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 / base["value"],
@@ -249,6 +260,167 @@ def run_reference(a, rank, world):
     if ref_gpu is not None:
         line["reference_cuda_kernel_b200"] = ref_gpu
     print(json.dumps(line), flush=True)
+
+
+def timed_region(local, fn):
+    """Run fn() between CUDA events on the current stream with clocks sampled;
+    returns (device ms, clock summary)."""
+    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        out = fn()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    return ev0.elapsed_time(ev1), clk.summary(), out
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch of a committed ncu capture (profiles/<name>.json)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+def run_config2(a, rank, world, local):
+    """Isolated LM head + argmax, one launch per step."""
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import megakernel_b200 as mk
+    from megakernel_b200 import _lib
+    from megakernel_b200.engine import build_layer_table, decode_call
+    g = torch.Generator(device=dev).manual_seed(2001 + rank)
+    embed = (torch.randn((VOCAB, HIDDEN), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    x = torch.randn(HIDDEN, generator=g, device=dev).to(torch.bfloat16).float()
+    norm = torch.ones(HIDDEN, dtype=torch.bfloat16, device=dev)
+    layer = [norm, embed[:2048], embed[:1024], embed[:1024], norm[:128], norm[:128], embed[:1024, :1024].contiguous(),
+             norm, embed[:3072], embed[:3072], embed[:1024, :1024].contiguous()]
+    table = build_layer_table(layer, dev)
+    kv = torch.zeros((1, 8, 16, 128), dtype=torch.bfloat16, device=dev)
+    cos, sin = mk.rope_tables(16, dev)
+    logits = torch.empty(VOCAB, dtype=torch.float32, device=dev)
+    tok = torch.empty(max(a.steps, 1), dtype=torch.int32, device=dev)
+    common = dict(embed=embed, lm_head=embed, final_norm=norm, layers=table, cos_table=cos, sin_table=sin,
+                  rope_fp32=1, k_cache=kv, v_cache=kv, max_seq=16, layer_begin=0, layer_end=0, token=0,
+                  position=0, cache_len=1, flags=_lib.MKB_FLAG_LM_HEAD | _lib.MKB_FLAG_SKIP_FINAL_NORM,
+                  logits=logits)
+    steps, warm = max(1, a.steps), max(3, a.warmup)
+
+    def launches(n):
+        for i in range(n):
+            _lib.check(decode_call(input_residual=x, out_tokens=tok[i:i + 1], **common), "mkb_decode")
+
+    launches(warm)
+    dev_ms, clocks, _ = timed_region(local, lambda: launches(steps))
+    # steady-state stream: one launch that runs the LM head `steps` times over the same input
+    n_pass = min(steps, 16 - 1)
+    pass_ms, _, _ = timed_region(local, lambda: _lib.check(decode_call(
+        input_residual=x, out_tokens=tok, n_tokens=n_pass, **{**common, "max_seq": 16}), "mkb_decode"))
+    # e2e: hidden copied in from pinned memory, argmax copied back, per step
+    xh = x.cpu().pin_memory()
+    th = torch.empty(1, dtype=torch.int32).pin_memory()
+    xd = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(steps):
+        xd.copy_(xh, non_blocking=True)
+        _lib.check(decode_call(input_residual=xd, out_tokens=tok[:1], **common), "mkb_decode")
+        th.copy_(tok[:1], non_blocking=True)
+        stream.synchronize()
+    e2e_s = time.perf_counter() - t0
+    assert int(th.item()) == int(torch.argmax(embed.float() @ x).item())
+    dev_ms, e2e_ms, pass_ms = max_over_ranks([dev_ms, e2e_s * 1000.0, pass_ms], world, dev)
+    per_launch = LM_BYTES
+    achieved = per_launch / (dev_ms / 1000.0 / steps) / 1e9
+    peak, peak_kind = measured_peak()
+    tr = profile_traffic("lm_head_traffic.json")
+    if rank == 0:
+        line = {"metric": "isolated LM-head GEMV + argmax launches/s (151936 x 1024 BF16)",
+                "value": world * steps / (dev_ms / 1000.0), "unit": "launch/s", "n_gpus": world, "steps": steps,
+                "warmup": warm, "ms_per_step": dev_ms / steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (E ~ N(0,0.02) BF16, hidden ~ N(0,1) BF16 taken as normalised)",
+                "config": {"workload": "config2: isolated LM head + argmax, 311 MB weight per launch",
+                           "us_per_launch": dev_ms * 1000.0 / steps,
+                           "us_per_pass_in_one_launch": pass_ms * 1000.0 / n_pass,
+                           "l2": "inputs larger than L2: 311 MB weight per launch vs 126 MB L2"},
+                "e2e": {"value": world * steps / (e2e_ms / 1000.0), "unit": "launch/s",
+                        "h2d_bytes_per_step": HIDDEN * 4, "d2h_bytes_per_step": 4,
+                        "us_per_launch": e2e_ms * 1000.0 / steps,
+                        "api": "mkb_decode (hidden copied in, argmax copied out, stream synchronised per step)"},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "peak_source": peak_kind,
+                             "traffic": tr["dram_bytes_per_launch"] if tr else None, "kernel": "decode_kernel",
+                             "algorithmic_bytes_per_launch": per_launch,
+                             "stream_frac_in_one_launch": per_launch / (pass_ms / 1000.0 / n_pass) / 1e9 / peak},
+                "gpu_launches": steps, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+
+
+def run_config3(a, rank, world, local):
+    """Long cache: 4096-slot cache, 3584-token prompt
+    prefilled in-engine, 256 greedy steps in one persistent launch."""
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import megakernel_b200 as mk
+    prompt_len, max_seq = 3584, 4096
+    steps = max(1, min(a.steps, max_seq - prompt_len))
+    warm = max(3, a.warmup)
+    embed, final_norm, layers = synthetic_weights(1000 + rank, dev)
+    k = torch.zeros((LAYERS, 8, max_seq, 128), dtype=torch.bfloat16, device=dev)
+    v = torch.zeros_like(k)
+    eng = mk.DecodeEngine(embed, final_norm, layers, k, v, fused_down=True, use_graph=True)
+    prompt = torch.randint(0, VOCAB, (prompt_len,), generator=torch.Generator().manual_seed(rank)).tolist()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    first = eng.prefill(prompt)
+    prefill_s = time.perf_counter() - t0
+    out = torch.empty(steps, dtype=torch.int32, device=dev)
+    eng.generate(first, prompt_len, warm, out=out[:warm])
+    dev_ms, clocks, _ = timed_region(local, lambda: eng.generate(first, prompt_len, steps, out=out))
+    assert eng.status()[0] == 0
+    for i in range(warm):
+        eng.step(first, prompt_len + i)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    t = first
+    for i in range(steps):
+        t = eng.step(t, prompt_len + i)
+    e2e_s = time.perf_counter() - t0
+    dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_s * 1000.0], world, dev)
+    alg = sum(WEIGHT_BYTES + KV_BYTES_PER_POS * (prompt_len + i + 1) for i in range(steps))
+    achieved = alg / (dev_ms / 1000.0) / 1e9
+    peak, peak_kind = measured_peak()
+    tr = ncu_traffic()
+    traffic = None
+    if tr is not None:
+        tok_bytes, cl0, per_pos = tr
+        traffic = sum(tok_bytes + per_pos * (prompt_len + i + 1 - cl0) for i in range(steps))
+    line = {"metric": METRIC.replace("512", "4096"), "value": replica_throughput(world, steps, dev_ms),
+            "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": dev_ms / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init BF16 weights N(0,0.02), random prompt ids)",
+            "config": {"workload": "config3: Qwen3-0.6B batch-1 greedy decode, 3584-token prompt, cache 4096, "
+                                   "cache lengths 3585..3840", "model": "Qwen3-0.6B", "global_batch": world,
+                       "seq_len": max_seq, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2: 1.6 GB streamed per token vs 126 MB L2",
+                       "us_per_token": dev_ms * 1000.0 / steps, "prefill_s_3584_tokens": prefill_s,
+                       "kv_share_of_bytes": sum(KV_BYTES_PER_POS * (prompt_len + i + 1) for i in range(steps)) / alg},
+            "e2e": {"value": replica_throughput(world, steps, e2e_ms), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4, "us_per_token": e2e_ms * 1000.0 / steps,
+                    "api": "mkb_engine_step (8 B copied in from pinned memory, graph replay, the kernel "
+                           "stores the 4 B argmax into pinned host memory)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": peak_kind, "traffic": traffic, "kernel": "decode_kernel",
+                         "algorithmic_bytes_per_launch": alg},
+            "gpu_launches": 1, "clocks": clocks}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
 
 
 def reference_kernel_on_gpu(a):
@@ -269,6 +441,12 @@ def main():
     rank, world, local = dist_env()
     if a.impl == "reference":
         run_reference(a, rank, world)
+        return
+    if a.config == 2:
+        run_config2(a, rank, world, local)
+        return
+    if a.config == 3:
+        run_config3(a, rank, world, local)
         return
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)

@@ -7,9 +7,19 @@
  * instead of being copied.
  *
  * Error model: functions return cudaError_t. Launch-time errors come back
- * directly; in-kernel failures (a bounded wait that expired, bad arguments seen
- * on the device) are recorded in the workspace and read with
- * mkb_workspace_status(); the engine calls check it after every step.
+ * directly. In-kernel failures (a bounded wait that expired, bad arguments seen
+ * on the device, a sum outside the fixed-point range) are
+ *   - recorded in the workspace (read with mkb_workspace_status),
+ *   - copied to an optional error word (mkb_decode_args.err_flag; the launchers
+ *     point it at pinned host memory, so the host reads it without a copy),
+ *   - made visible in the outputs: the failed launch writes NaN over its logits
+ *     rows and -1 over every output token it did not complete.
+ * A workspace that holds an error refuses further launches (outputs poisoned)
+ * until it is reset. Launches on a library-owned workspace (launch_decode_kernel,
+ * mkb_decode without a workspace, the engine calls) report an earlier
+ * asynchronous launch's in-kernel failure the way CUDA reports asynchronous
+ * errors: the next call returns cudaErrorLaunchFailure without launching, after
+ * resetting the workspace; the call after it runs normally.
  */
 #ifndef MKB200_H
 #define MKB200_H
@@ -31,7 +41,10 @@ extern "C" {
  * layer's raw QKV projections and g_mlp_intermediate its SwiGLU vector;
  * hidden_buffer, g_activations, g_attn_output and g_normalized are not used.
  * The extra synchronisation workspace is allocated once per device on first use
- * (mkb_default_workspace); calls on one device must not overlap in time. */
+ * (mkb_default_workspace); calls on one device must not overlap in time.
+ * In-kernel failure: the logits are NaN, and the next launch on the device's
+ * workspace returns cudaErrorLaunchFailure without launching (workspace reset).
+ * The reference reported its errors through this return code alone. */
 cudaError_t launch_decode_kernel(int token_id, const void* embed_weight, const void* lm_head_weight,
                                  const void* final_norm_weight, const void* layer_weights,
                                  const void* cos_table, const void* sin_table, void* k_cache, void* v_cache,
@@ -48,7 +61,9 @@ cudaError_t launch_decode_kernel(int token_id, const void* embed_weight, const v
  * address (cudaGetSymbolAddress) and caches it; make that first call before
  * any stream capture. Every call clears the workspace bytes with
  * cudaMemsetAsync on `stream`, then launches. The array is shared by all calls
- * on the device: calls that overlap in time race on it. */
+ * on the device: calls that overlap in time race on it. An in-kernel failure
+ * leaves NaN logits; its status stays readable with mkb_noalloc_status() after
+ * the stream is synchronised and until the next call clears the array. */
 cudaError_t launch_decode_kernel_noalloc(int token_id, const void* embed_weight, const void* lm_head_weight,
                                          const void* final_norm_weight, const void* layer_weights,
                                          const void* cos_table, const void* sin_table, void* k_cache,
@@ -57,6 +72,11 @@ cudaError_t launch_decode_kernel_noalloc(int token_id, const void* embed_weight,
                                          void* g_mlp_intermediate, void* g_logits, void* g_q, void* g_k,
                                          void* g_v, int position, int cache_len, int max_seq_len,
                                          cudaStream_t stream);
+/* In-kernel status of launch_decode_kernel_noalloc's static workspace on
+ * `device` (same words as mkb_workspace_status; synchronous copy, allocates
+ * nothing). Read it after synchronising the launch's stream and before the next
+ * launch_decode_kernel_noalloc call on that device, which clears it. */
+cudaError_t mkb_noalloc_status(int device, uint32_t out[8]);
 
 /* ---- explicit-argument launch ----------------------------------------------
  * Generalises the reference launcher (megakernel.cu:898-994): layer range,
@@ -115,6 +135,15 @@ typedef struct mkb_decode_args {
                                   launch is prompt_tokens[t] (not the previous argmax), and
                                   the LM head runs for the last token only. No counterpart
                                   in the reference (model.py:72-87 prefills with HF). */
+  uint32_t* err_flag;          /* optional: receives the first in-kernel error code (device
+                                  or mapped pinned host memory); NULL with workspace NULL
+                                  = the device's own pinned word (checked by the next
+                                  launch, see the error model above) */
+  int stop_token;              /* -1 (default): none. Otherwise the launch ends after the
+                                  first generated token equal to it (the reference loop's
+                                  eos_token_id check, model.py:102-105): its id is the last
+                                  one written, later out_tokens read -1, and no K/V row is
+                                  appended for it. */
 } mkb_decode_args;
 
 void mkb_decode_args_init(mkb_decode_args* a);
@@ -169,9 +198,16 @@ cudaError_t mkb_engine_create(const mkb_model* model, mkb_engine** out);
  * not complete. */
 cudaError_t mkb_engine_step(mkb_engine* e, int token, int position, int* next_token, cudaStream_t stream);
 /* n greedy tokens in one persistent launch, starting from `token` at `position`;
- * ids land in out_tokens (device, n entries). Asynchronous. */
+ * ids land in out_tokens (device, n entries). Asynchronous; a token that did not
+ * complete reads -1, and the next engine call reports the failure
+ * (cudaErrorLaunchFailure, workspace reset). */
 cudaError_t mkb_engine_generate(mkb_engine* e, int token, int position, int n, int* out_tokens,
                                 cudaStream_t stream);
+/* As mkb_engine_generate, but the launch ends after the first generated token
+ * equal to stop_token (>= 0; the reference loop stops on eos_token_id,
+ * model.py:102-105): that id is the last one written, later entries read -1. */
+cudaError_t mkb_engine_generate_until(mkb_engine* e, int token, int position, int n, int stop_token,
+                                      int* out_tokens, cudaStream_t stream);
 /* In-engine prefill: the n prompt ids (device int[n]) enter at positions
  * position .. position+n-1 in one persistent launch that appends their K/V rows;
  * the LM head runs for the last one only, whose argmax (the first generated

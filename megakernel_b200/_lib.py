@@ -24,6 +24,7 @@ ERROR_NAMES = {
     2: "timeout waiting for a shared-memory ring slot",
     3: "timeout waiting for the greedy token broadcast",
     4: "bad arguments (range or alignment) seen on the device",
+    5: "a partial sum outside the counted fixed-point range (|x| >= 2^19 or NaN)",
 }
 
 
@@ -66,6 +67,8 @@ class DecodeArgs(Structure):
         ("trace", c_void_p),
         ("trace_cap", c_int),
         ("prompt_tokens", c_void_p),
+        ("err_flag", c_void_p),
+        ("stop_token", c_int),
     ]
 
 
@@ -100,6 +103,7 @@ SIGNATURES = [
      [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
       c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
       c_void_p, c_int, c_int, c_int, c_void_p]),
+    ("mkb_noalloc_status", c_int, [c_int, POINTER(c_uint32)]),
     ("mkb_decode_args_init", None, [POINTER(DecodeArgs)]),
     ("mkb_decode", c_int, [POINTER(DecodeArgs), c_void_p]),
     ("mkb_workspace_bytes", c_size_t, []),
@@ -111,6 +115,7 @@ SIGNATURES = [
     ("mkb_engine_create", c_int, [POINTER(Model), POINTER(c_void_p)]),
     ("mkb_engine_step", c_int, [c_void_p, c_int, c_int, POINTER(c_int), c_void_p]),
     ("mkb_engine_generate", c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    ("mkb_engine_generate_until", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     ("mkb_engine_prefill", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     ("mkb_engine_logits", c_void_p, [c_void_p]),
     ("mkb_engine_workspace", c_void_p, [c_void_p]),

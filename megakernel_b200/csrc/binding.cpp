@@ -11,7 +11,11 @@
 // raise ValueError/RuntimeError; the device LayerWeights table and the scratch
 // vectors are kept resident per device instead of being allocated and freed on
 // every call (pytorch_binding.cu:49-60,84-126), so a call performs no
-// cudaMalloc/cudaFree and no device synchronisation.
+// cudaMalloc/cudaFree. Like the reference's call (whose per-call cudaFree
+// synchronises), it returns after the kernel has finished: it synchronises the
+// stream and raises RuntimeError, after resetting the workspace, when the kernel
+// reported a failure (a bounded wait that expired, bad arguments seen on the
+// device), instead of returning the poisoned logits.
 
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -119,6 +123,18 @@ torch::Tensor decode(int64_t token_id, torch::Tensor embed_weight, torch::Tensor
       st.residual.data_ptr(), nullptr, nullptr, nullptr, st.mlp.data_ptr(), logits.data_ptr(), st.q.data_ptr(),
       st.k.data_ptr(), st.v.data_ptr(), static_cast<int>(position), cache_len, static_cast<int>(max_seq_len),
       stream));
+  C10_CUDA_CHECK(cudaStreamSynchronize(stream));
+  void* ws = nullptr;
+  C10_CUDA_CHECK(mkb_default_workspace(d, &ws));
+  uint32_t out[8];
+  C10_CUDA_CHECK(mkb_workspace_status(ws, out));
+  if (out[0] != 0) {
+    C10_CUDA_CHECK(mkb_workspace_reset(ws, stream));
+    C10_CUDA_CHECK(cudaStreamSynchronize(stream));
+    TORCH_CHECK(false, "decode: in-kernel error ", out[0], " (", mkb_error_name(out[0]), ") at cta ", out[1],
+                ", layer ", static_cast<int>(out[2]), ", stage ", static_cast<int>(out[3]),
+                "; the workspace was reset and the logits are invalid");
+  }
   return logits;
 }
 

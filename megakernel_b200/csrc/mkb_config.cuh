@@ -127,6 +127,7 @@ struct alignas(128) Workspace {
   uint32_t tok_flag[32];                     // greedy token broadcast (multi-token launches)
   uint32_t error[32];                        // [0] code, [1] cta, [2] layer, [3] stage, [4] token
   uint32_t tag_base[32];                     // [0]: tag of the last token decoded (tagged words)
+  uint32_t stop_seen[32];                    // CTAs that saw a stop token (the last one resets tok_flag)
   // Per-layer sums as counted fixed-point words (see kAccShift): o_proj
   // partials (one per KV head) and down-proj partials (one per CTA).
   uint64_t acc_mid[kMaxLayers][kHidden];
@@ -188,6 +189,8 @@ struct DecodeParams {
   unsigned long long* trace;         // optional [2*grid][trace_cap] stage time stamps
   int trace_cap;
   const int* prompt;                 // prefill: forced input tokens [n_tokens], LM head on the last only
+  uint32_t* err_flag;                // optional (host-mapped) word that receives the error code
+  int stop_token;                    // end the launch after generating this id (-1: none)
 };
 
 // Trace record: (code << 48) | (globaltimer ns & 0xffffffffffff). Row cta is

@@ -100,6 +100,7 @@ struct Ctl {
   int cta;
   unsigned long long* trace;  // this CTA's row of the trace buffer (or null)
   int trace_cap;
+  uint32_t* err_flag;         // copy of the error code for the host (or null)
 };
 
 // Stage time stamps of consumer thread 0, compiled in only for the traced
@@ -142,6 +143,9 @@ __device__ __noinline__ void raise_error(const Ctl c, uint32_t code, int layer, 
     c.ws->error[2] = static_cast<uint32_t>(layer);
     c.ws->error[3] = static_cast<uint32_t>(stage);
     c.ws->error[4] = static_cast<uint32_t>(tok);
+    // the first error also goes to the caller's flag (pinned host memory for the
+    // launchers), which the host reads without a copy
+    if (c.err_flag != nullptr) *reinterpret_cast<volatile uint32_t*>(c.err_flag) = code;
   }
   *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
 }
@@ -156,6 +160,7 @@ __device__ __noinline__ void spin_geq(const Ctl c, const uint32_t* ctr, uint32_t
   while (true) {
     if (static_cast<int>(ld_acquire(ctr) - target) >= 0) return;
     if ((++it & 15u) == 0u) {
+      if (aborted(c)) return;  // also set when the launch stops on a stop token
       if (ld_relaxed(&c.ws->error[0]) != 0u) {
         *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
         return;
@@ -856,6 +861,16 @@ __device__ __forceinline__ bool cluster_rx_wait(const Ctl& c, uint64_t* bar, uin
   return mbar_wait_cluster(bar, ph, 0u) || cluster_rx_wait_slow(c, bar, ph, layer, stage, tok);
 }
 
+// Outputs of a launch that stopped on an error: NaN over the logits rows
+// [va, vb) and -1 for output tokens [t0, n_tokens) (none of those completed, so
+// no CTA writes a valid id there). Called by every consumer thread of a CTA.
+__device__ __forceinline__ void poison_outputs(const DecodeParams& p, int va, int vb, int t0) {
+  if (p.logits != nullptr)
+    for (int i = va + static_cast<int>(threadIdx.x); i < vb; i += kConsumerThreads) p.logits[i] = __int_as_float(0x7fc00000);
+  if (p.out_tokens != nullptr && threadIdx.x == 0)
+    for (int i = max(t0, 0); i < p.n_tokens; ++i) p.out_tokens[i] = -1;
+}
+
 template <bool kFused, bool kTraced>
 __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int token0, int pos0, int cl0,
                              int splits, uint32_t tag0) {
@@ -916,6 +931,24 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         if (tid == 0) sm.token = static_cast<int>(__ldcg(reinterpret_cast<const int*>(&ws->tok_flag[1])));
         consumer_sync(kConsumerThreads);
         token = sm.token;
+        if (p.stop_token >= 0 && token == p.stop_token && !aborted(c)) {
+          // The previous token was the stop id (model.py:102-105 ends its loop
+          // there): every CTA leaves here, uniformly; the producer stops too. The
+          // token's last CTA already reset the shared state except tok_flag,
+          // which the last CTA to see the stop clears.
+          if (tid == 0) {
+            *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+            uint32_t old;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&ws->stop_seen[0]) : "memory");
+            if (old == static_cast<uint32_t>(G - 1)) {
+              ws->stop_seen[0] = 0u;
+              ws->tok_flag[0] = 0u;
+            }
+            if (c.cta == 0 && p.out_tokens != nullptr)
+              for (int i = t; i < p.n_tokens; ++i) p.out_tokens[i] = -1;
+          }
+          return;
+        }
       }
     }
     if (p.prompt != nullptr) token = __ldg(p.prompt + t);
@@ -1261,6 +1294,22 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             if (at_live && tid == 0) mbar_arrive_expect_tx(&sm.atbar, kPairAttnBytes);
           }
           if (splits > 1 && tid == 0) release_add(&ws->att_sync[l][h][0], 1u);
+        } else if (splits > 1 && pl.c < splits) {
+          // The launch's split count comes from its longest cache: an earlier
+          // token of the launch (a prefill, a generate that starts short) can
+          // leave this split without keys. Publish an empty partial (m = -inf,
+          // l = 0, o = 0), which the combine weighs by zero.
+          if (tid < 2 * kHeadDim) {
+            const int hh = tid >> 7, d = tid & (kHeadDim - 1);
+            float* dst = ws->att_part[h][pl.c][hh];
+            dst[d] = 0.f;
+            if (d == 0) {
+              dst[kHeadDim] = -INFINITY;
+              dst[kHeadDim + 1] = 0.f;
+            }
+          }
+          consumer_sync(kConsumerThreads);
+          if (tid == 0) release_add(&ws->att_sync[l][h][0], 1u);
         }
         if (splits > 1) {
           transition_wait(c, tr, &ws->att_sync[l][h][0], static_cast<uint32_t>(splits * (t + 1)), l, kStSplit, t);
@@ -1536,7 +1585,10 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     if (last_state < 0) {
       // leaving early: the cluster partner must not wait for (or send) more
       // SwiGLU values; this store is ordered before the final cluster barrier
-      if (kFused && tid == 0) st_cluster_u32(mapa_shared(smem_addr(&sm.peer_gone), cluster_ctarank() ^ 1u), 1u);
+      if (tid == 0) st_cluster_u32(mapa_shared(smem_addr(&sm.peer_gone), cluster_ctarank() ^ 1u), 1u);
+      // make the failure visible in the outputs: NaN over this CTA's logits rows,
+      // -1 for every token of the launch that has not completed
+      poison_outputs(p, pl.va, pl.vb, t);
       return;
     }
     if (last_state) {
@@ -1544,13 +1596,19 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       if (lm_now && tid == 0) {
         best = argmax_key_index(__ldcg(&ws->tok_best[0]));
         ws->tok_best[0] = 0ull;  // for the next token (ordered by the release below)
+        sm.token = best;
       }
+      consumer_sync(kConsumerThreads);
+      // the launch ends after this token: the last one, or a generated stop id
+      const bool stop_now = !last_tok && lm_now && p.prompt == nullptr && p.stop_token >= 0 &&
+                            sm.token == p.stop_token;
+      const bool final_tok = last_tok || stop_now;
       // the last two layers' accumulators (earlier ones were cleared on the way)
       for (int l = max(lb, le - 2); l < le; ++l) {
         acc_clear4(&ws->acc_mid[l][0]);
         for (int q = 0; q < kDownCopies; ++q) acc_clear4(&ws->acc_down[l][q][0]);
       }
-      if (last_tok) {
+      if (final_tok) {
         for (int i = tid; i < kMaxLayers * 4; i += kConsumerThreads) ws->sync[i >> 2][i & 3][0] = 0u;
         for (int i = tid; i < kMaxLayers * kNKV; i += kConsumerThreads) ws->kv_ready[i / kNKV][i % kNKV][0] = 0u;
         for (int i = tid; i < kMaxLayers * kNKV; i += kConsumerThreads) ws->att_sync[i / kNKV][i % kNKV][0] = 0u;
@@ -1569,6 +1627,13 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           ws->arrive[0] = 0u;
           ws->tok_flag[0] = 0u;
           ws->tag_base[0] = tag0 + static_cast<uint32_t>(p.n_tokens);
+        } else if (stop_now) {
+          // every CTA has arrived for this token and none adds again; tok_flag
+          // still carries the stop id to the others (cleared by the last to see it)
+          ws->arrive[0] = 0u;
+          ws->tag_base[0] = tag0 + static_cast<uint32_t>(t) + 1u;
+          ws->tok_flag[1] = static_cast<uint32_t>(best);
+          st_release(&ws->tok_flag[0], static_cast<uint32_t>(t + 1));
         } else {
           ws->tok_flag[1] = static_cast<uint32_t>(best);
           st_release(&ws->tok_flag[0], static_cast<uint32_t>(t + 1));  // covers the CTA's writes above
@@ -1584,10 +1649,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem* sm = reinterpret_cast<Smem*>(smem_raw);
   Ctl c{sm, p.ws, p.timeout_ns, static_cast<int>(blockIdx.x),
-        p.trace ? p.trace + (size_t)blockIdx.x * p.trace_cap : nullptr, p.trace_cap};
+        p.trace ? p.trace + (size_t)blockIdx.x * p.trace_cap : nullptr, p.trace_cap, p.err_flag};
 
   int token = p.token, pos = p.position, cl = p.cache_len;
   const uint32_t tag0 = __ldcg(&p.ws->tag_base[0]);
+  // A workspace that still holds an earlier launch's error has stale counters
+  // and sums: refuse to run on it (outputs poisoned) until it is reset.
+  const uint32_t stale_err = __ldcg(&p.ws->error[0]);
   if (p.step != nullptr) {
     token = __ldcg(p.step + 0);
     pos = __ldcg(p.step + 1);
@@ -1641,6 +1709,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
       p.group_size * kNKV > p.grid || p.grid % kCluster != 0 || splits < 1 || splits > kMaxSplits ||
       (splits > 1 && splits > p.group_size) || misaligned) {
     if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(c, kErrBadArgs, -1, -1, -1);
+    // nothing was read or appended; the outputs say so
+    if (threadIdx.x < kConsumerThreads)
+      poison_outputs(p, part(kVocab, gridDim.x, blockIdx.x), part(kVocab, gridDim.x, blockIdx.x + 1), 0);
     return;
   }
 
@@ -1648,7 +1719,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
   // arrival, and none exits while a peer may still write into its shared memory.
   cluster_sync_all();
   const Plan pl = make_plan(blockIdx.x, p.grid, p.group_size, kVocab);
-  if (threadIdx.x >= kConsumerThreads) {
+  if (stale_err != 0u) {
+    // Not uniform over the grid when this launch raised an error of its own
+    // before a late CTA started: such a CTA skips its work, so its partner is
+    // told (peer_gone) and every wait on it stays bounded.
+    if (threadIdx.x == 0 && blockIdx.x == 0 && p.err_flag != nullptr)
+      *reinterpret_cast<volatile uint32_t*>(p.err_flag) = stale_err;
+    if (threadIdx.x == 0) st_cluster_u32(mapa_shared(smem_addr(&sm->peer_gone), cluster_ctarank() ^ 1u), 1u);
+    if (threadIdx.x < kConsumerThreads) poison_outputs(p, pl.va, pl.vb, 0);
+  } else if (threadIdx.x >= kConsumerThreads) {
     producer_run<kFused, kTraced>(p, pl, c, pos, cl, splits);
   } else {
     consumer_run<kFused, kTraced>(p, pl, c, token, pos, cl, splits, tag0);

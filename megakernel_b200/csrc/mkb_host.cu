@@ -33,6 +33,10 @@ constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s per wait
 struct DeviceInfo {
   int sms = 0;
   void* ws = nullptr;
+  // Pinned, mapped word that receives the first in-kernel error of a launch on
+  // `ws` (host view / device view); checked before the next launch on `ws`.
+  uint32_t* h_err = nullptr;
+  uint32_t* d_err = nullptr;
 };
 std::mutex g_mu;
 DeviceInfo g_dev[64];
@@ -56,13 +60,21 @@ cudaError_t default_ws(int dev, void** out) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (d->ws == nullptr) {
     void* p = nullptr;
+    uint32_t* h = nullptr;
+    uint32_t* dv = nullptr;
+    e = cudaHostAlloc(reinterpret_cast<void**>(&h), 32, cudaHostAllocMapped);
+    if (e != cudaSuccess) return e;
+    *reinterpret_cast<volatile uint32_t*>(h) = 0u;
+    e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&dv), h, 0);
+    if (e != cudaSuccess) { cudaFreeHost(h); return e; }
     e = cudaMalloc(&p, sizeof(Workspace));
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) { cudaFreeHost(h); return e; }
     e = cudaMemset(p, 0, sizeof(Workspace));
-    if (e != cudaSuccess) return e;
-    e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) return e;
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { cudaFree(p); cudaFreeHost(h); return e; }
     d->ws = p;
+    d->h_err = h;
+    d->d_err = dv;
   }
   *out = d->ws;
   return cudaSuccess;
@@ -71,7 +83,7 @@ cudaError_t default_ws(int dev, void** out) {
 int grid_for(int sms) { return sms > kMaxGrid ? kMaxGrid : sms; }
 
 // Fill DecodeParams from the C argument block; resolves every default.
-cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p) {
+cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p, DeviceInfo** dflt = nullptr) {
   if (a == nullptr) return cudaErrorInvalidValue;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -80,9 +92,11 @@ cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p) {
   e = device_info(dev, &d);
   if (e != cudaSuccess) return e;
   void* ws = a->workspace;
+  if (dflt) *dflt = nullptr;
   if (ws == nullptr) {
     e = default_ws(dev, &ws);
     if (e != cudaSuccess) return e;
+    if (dflt) *dflt = d;
   }
   std::memset(p, 0, sizeof(*p));
   p->embed = static_cast<const __nv_bfloat16*>(a->embed);
@@ -125,6 +139,9 @@ cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p) {
   p->trace = a->trace;
   p->trace_cap = a->trace ? a->trace_cap : 0;
   p->prompt = a->prompt_tokens;
+  p->err_flag = a->err_flag ? a->err_flag : (a->workspace == nullptr ? d->d_err : nullptr);
+  p->stop_token = a->stop_token;
+  if (p->stop_token >= kVocab) return cudaErrorInvalidValue;
   // Host-side validation of what the host can see (the kernel re-checks the rest).
   if (!p->embed || !p->layers || !p->k_cache || !p->v_cache || !p->cos_table || !p->sin_table)
     return cudaErrorInvalidValue;
@@ -169,14 +186,30 @@ void mkb_decode_args_init(mkb_decode_args* a) {
   std::memset(a, 0, sizeof(*a));
   a->n_tokens = 1;
   a->withhold_cta = -1;
+  a->stop_token = -1;
   a->layer_end = kMaxLayers;
   a->flags = MKB_FLAG_LM_HEAD;
 }
 
 cudaError_t mkb_decode(const mkb_decode_args* a, cudaStream_t stream) {
   DecodeParams p;
-  cudaError_t e = to_params(a, &p);
+  DeviceInfo* dflt = nullptr;
+  cudaError_t e = to_params(a, &p, &dflt);
   if (e != cudaSuccess) return e;
+  if (dflt != nullptr && a->err_flag == nullptr) {
+    volatile uint32_t* flag = dflt->h_err;
+    if (*flag != 0u) {
+      // An earlier asynchronous launch on the device's workspace failed in the
+      // kernel: report it here (as CUDA reports asynchronous errors), reset the
+      // workspace, and do not launch on its stale state.
+      fprintf(stderr, "mkb200: an earlier launch on device workspace failed in the kernel: %s\n",
+              mkb_error_name(*flag));
+      e = cudaMemsetAsync(dflt->ws, 0, sizeof(Workspace), stream);
+      if (e != cudaSuccess) return e;
+      *flag = 0u;
+      return cudaErrorLaunchFailure;
+    }
+  }
   return launch_decode(p, stream);
 }
 
@@ -221,6 +254,12 @@ cudaError_t launch_decode_kernel(int token_id, const void* embed_weight, const v
 cudaError_t mkb_default_workspace(int device, void** out) { return default_ws(device, out); }
 
 cudaError_t mkb_workspace_reset(void* workspace, cudaStream_t stream) {
+  {
+    // resetting a device's own workspace also clears its pending error word
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (DeviceInfo& d : g_dev)
+      if (d.ws != nullptr && d.ws == workspace) *reinterpret_cast<volatile uint32_t*>(d.h_err) = 0u;
+  }
   return cudaMemsetAsync(workspace, 0, sizeof(Workspace), stream);
 }
 
@@ -236,6 +275,7 @@ const char* mkb_error_name(uint32_t code) {
     case kErrTimeoutRing: return "timeout waiting for a shared-memory ring slot";
     case kErrTimeoutToken: return "timeout waiting for the greedy token broadcast";
     case kErrBadArgs: return "bad arguments (range or alignment) seen on the device";
+    case kErrRange: return "a partial sum outside the counted fixed-point range (|x| >= 2^19 or NaN)";
     default: return "unknown";
   }
 }
@@ -293,7 +333,8 @@ struct mkb_engine {
   float* d_logits = nullptr;
   bool own_logits = false;
   // Pinned, mapped host words: [0..1] (token, position) copied in each step,
-  // [4] the argmax, stored there by the kernel's last CTA (no copy back).
+  // [4] the argmax, stored there by the kernel's last CTA (no copy back),
+  // [5] the first in-kernel error code of a launch (checked by the next call).
   int* h_io = nullptr;
   int* d_io = nullptr;                        // device address of h_io
   cudaGraphExec_t graph = nullptr;
@@ -321,6 +362,7 @@ cudaError_t engine_check_status(mkb_engine* e) {
   uint32_t st[8];
   cudaError_t err = mkb_workspace_status(e->ws, st);
   if (err != cudaSuccess) return err;
+  reinterpret_cast<volatile int*>(e->h_io)[5] = 0;
   if (st[0] != 0) {
     fprintf(stderr, "mkb200: in-kernel error %u (%s) cta=%u layer=%d stage=%d token=%d\n", st[0],
             mkb_error_name(st[0]), st[1], static_cast<int>(st[2]), static_cast<int>(st[3]),
@@ -330,6 +372,16 @@ cudaError_t engine_check_status(mkb_engine* e) {
     return cudaErrorLaunchFailure;
   }
   return cudaSuccess;
+}
+// An earlier asynchronous engine launch (generate, prefill) that failed in the
+// kernel is reported by the next engine call: workspace status printed and
+// reset, cudaErrorLaunchFailure returned, nothing launched.
+cudaError_t engine_report_earlier(mkb_engine* e, cudaStream_t stream) {
+  if (reinterpret_cast<volatile int*>(e->h_io)[5] == 0) return cudaSuccess;
+  cudaError_t err = cudaStreamSynchronize(stream);
+  if (err != cudaSuccess) return err;
+  err = engine_check_status(e);
+  return err != cudaSuccess ? err : cudaErrorLaunchFailure;
 }
 }  // namespace
 
@@ -414,6 +466,7 @@ cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
   a.flags = MKB_FLAG_LM_HEAD;
   a.logits = e->d_logits;
   a.out_tokens = e->d_io + 4;  // the last CTA writes the argmax straight into host memory
+  a.err_flag = reinterpret_cast<uint32_t*>(e->d_io + 5);
   a.workspace = e->ws;
   a.grid = e->grid;
 
@@ -441,11 +494,13 @@ cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
 cudaError_t mkb_engine_step(mkb_engine* e, int token, int position, int* next_token, cudaStream_t stream) {
   if (!e) return cudaErrorInvalidValue;
   if (token < 0 || token >= kVocab || position < 0 || position >= e->max_seq) return cudaErrorInvalidValue;
+  cudaError_t err = engine_report_earlier(e, stream);
+  if (err != cudaSuccess) return err;
   volatile int* io = e->h_io;
   io[0] = token;
   io[1] = position;
   io[4] = -1;  // stays -1 unless the token completes (no CTA stopped on an error)
-  cudaError_t err = cudaMemcpyAsync(e->d_step, e->h_io, 2 * sizeof(int), cudaMemcpyHostToDevice, stream);
+  err = cudaMemcpyAsync(e->d_step, e->h_io, 2 * sizeof(int), cudaMemcpyHostToDevice, stream);
   if (err != cudaSuccess) return err;
   err = e->graph ? cudaGraphLaunch(e->graph, stream) : mkb_decode(&e->step_args, stream);
   if (err != cudaSuccess) return err;
@@ -461,7 +516,14 @@ cudaError_t mkb_engine_step(mkb_engine* e, int token, int position, int* next_to
 
 cudaError_t mkb_engine_generate(mkb_engine* e, int token, int position, int n, int* out_tokens,
                                 cudaStream_t stream) {
-  if (!e || n < 1 || !out_tokens) return cudaErrorInvalidValue;
+  return mkb_engine_generate_until(e, token, position, n, -1, out_tokens, stream);
+}
+
+cudaError_t mkb_engine_generate_until(mkb_engine* e, int token, int position, int n, int stop_token,
+                                      int* out_tokens, cudaStream_t stream) {
+  if (!e || n < 1 || !out_tokens || stop_token >= kVocab) return cudaErrorInvalidValue;
+  cudaError_t err = engine_report_earlier(e, stream);
+  if (err != cudaSuccess) return err;
   if (token < 0 || token >= kVocab || position < 0 || position + n > e->max_seq) return cudaErrorInvalidValue;
   mkb_decode_args a = e->step_args;
   a.step = nullptr;
@@ -470,6 +532,7 @@ cudaError_t mkb_engine_generate(mkb_engine* e, int token, int position, int n, i
   a.cache_len = position + 1;
   a.n_tokens = n;
   a.out_tokens = out_tokens;
+  a.stop_token = stop_token < 0 ? -1 : stop_token;
   return mkb_decode(&a, stream);
 }
 
@@ -477,6 +540,8 @@ cudaError_t mkb_engine_prefill(mkb_engine* e, const int* prompt_tokens, int n, i
                                cudaStream_t stream) {
   if (!e || !prompt_tokens || n < 1) return cudaErrorInvalidValue;
   if (position < 0 || position + n > e->max_seq) return cudaErrorInvalidValue;
+  cudaError_t err = engine_report_earlier(e, stream);
+  if (err != cudaSuccess) return err;
   mkb_decode_args a = e->step_args;
   a.step = nullptr;
   a.token = 0;  // the inputs come from prompt_tokens (ids are clamped on the device)
@@ -485,7 +550,7 @@ cudaError_t mkb_engine_prefill(mkb_engine* e, const int* prompt_tokens, int n, i
   a.n_tokens = n;
   a.prompt_tokens = prompt_tokens;
   a.out_tokens = e->d_pf;  // only entry n-1 (the last prompt token) is written
-  cudaError_t err = mkb_decode(&a, stream);
+  err = mkb_decode(&a, stream);
   if (err != cudaSuccess || !next_token) return err;
   return cudaMemcpyAsync(next_token, e->d_pf + (n - 1), sizeof(int), cudaMemcpyDeviceToDevice, stream);
 }

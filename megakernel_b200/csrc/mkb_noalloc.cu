@@ -12,7 +12,10 @@
 //    the status word must start at zero; the tag base restarts with them), so
 //    a call that timed out in the kernel leaves nothing stale for the next;
 //  * the device's one array is shared by every call on that device: calls
-//    that overlap in time (other streams, other host threads) race on it.
+//    that overlap in time (other streams, other host threads) race on it;
+//  * an in-kernel failure leaves NaN logits and its status in the array, read
+//    with mkb_noalloc_status (a synchronous copy, no allocation) after the
+//    stream is synchronised and before the next call clears it.
 
 #include <cstdio>
 #include <mutex>
@@ -97,4 +100,21 @@ extern "C" cudaError_t launch_decode_kernel_noalloc(
   a.mlp_out = static_cast<float*>(g_mlp_intermediate);
   a.workspace = ws;
   return mkb_decode(&a, stream);
+}
+
+extern "C" cudaError_t mkb_noalloc_status(int device, uint32_t out[8]) {
+  if (out == nullptr) return cudaErrorInvalidValue;
+  int cur = 0;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return e;
+  if (device != cur && (e = cudaSetDevice(device)) != cudaSuccess) return e;
+  void* ws = nullptr;
+  e = noalloc_scratch(device, &ws);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(out, static_cast<const mkb::Workspace*>(ws)->error, 8 * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (device != cur) {
+    const cudaError_t r = cudaSetDevice(cur);
+    if (e == cudaSuccess) e = r;
+  }
+  return e;
 }

@@ -131,14 +131,22 @@ class DecodeEngine:
         _lib.check(code, "mkb_engine_step")
         return out.value
 
-    def generate(self, token: int, position: int, n: int, out: torch.Tensor | None = None, stream=None):
-        """Greedy-decode ``n`` tokens on the device in one launch; returns int32 ids [n]."""
+    def generate(self, token: int, position: int, n: int, out: torch.Tensor | None = None, stream=None,
+                 stop_token: int | None = None):
+        """Greedy-decode ``n`` tokens on the device in one launch; returns int32 ids [n].
+
+        ``stop_token`` (e.g. the tokenizer's ``eos_token_id``) ends the launch after
+        the first generated token equal to it, as the reference loop does
+        (model.py:102-105); the ids after it read -1. A token that did not complete
+        because of an in-kernel error also reads -1, and the next engine call raises."""
         _require(n >= 1 and 0 <= position and position + n <= self.max_seq, "generate range out of bounds")
+        _require(stop_token is None or 0 <= stop_token < VOCAB, "stop_token out of range")
         if out is None:
             out = torch.empty(n, dtype=torch.int32, device=self.device)
         with torch.cuda.device(self.device):
-            code = self.lib.mkb_engine_generate(self._h, int(token), int(position), int(n),
-                                                c_void_p(out.data_ptr()), c_void_p(_stream_ptr(stream)))
+            code = self.lib.mkb_engine_generate_until(self._h, int(token), int(position), int(n),
+                                                      -1 if stop_token is None else int(stop_token),
+                                                      c_void_p(out.data_ptr()), c_void_p(_stream_ptr(stream)))
         _lib.check(code, "mkb_engine_generate")
         return out
 

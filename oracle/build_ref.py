@@ -8,6 +8,9 @@ torch.utils.cpp_extension with pytorch_binding.cu) is not used: the shim stands
 in for the binding without PyTorch headers.
 
     python oracle/build_ref.py [/path/to/reference]
+
+The reference checkout is taken from ``MKB_REFERENCE_DIR`` when set, else from
+``DEFAULT_REF`` (where this build container mounts it).
 """
 from __future__ import annotations
 
@@ -18,7 +21,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 OUT = os.path.join(OUT_DIR, "libref_megakernel.so")
-DEFAULT_REF = "/root/reference"
+DEFAULT_REF = os.environ.get("MKB_REFERENCE_DIR", "/root/reference")
 
 
 def build(ref_dir: str = DEFAULT_REF, force: bool = False) -> str | None:

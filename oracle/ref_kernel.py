@@ -62,6 +62,63 @@ class RefDecoder:
         return scratch[6]
 
 
+def load_launcher():
+    """The reference's own ``launch_decode_kernel`` (megakernel.cu:898-927) from
+    the library built from its sources."""
+    lib = load()
+    fn = lib.launch_decode_kernel
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_int] + [ctypes.c_void_p] * 18 + [ctypes.c_int] * 3 + [ctypes.c_void_p]
+    return fn
+
+
+def time_reference_resident(steps: int = 64, warmup: int = 5, seed: int = 0) -> dict:
+    """Per-token time of the reference kernel alone: the device LayerWeights table
+    and the scratch vectors are allocated once and kept, and the CUDA events
+    bracket the launch only (no per-call cudaMalloc/cudaFree, no table copy).
+    Host argmax between calls, outside the timed region."""
+    from .weights import make_weights, rope_tables
+    dev = torch.device("cuda", torch.cuda.current_device())
+    w = make_weights(seed).to(dev)
+    cos, sin = rope_tables(512, torch.bfloat16)
+    cos, sin = cos.to(dev), sin.to(dev)
+    k = torch.zeros((28, 8, 512, 128), dtype=torch.bfloat16, device=dev)
+    v = torch.zeros_like(k)
+    table = torch.tensor([t.data_ptr() for t in w.flat_layer_list()], dtype=torch.int64, device=dev)
+    f32 = dict(dtype=torch.float32, device=dev)
+    scratch = [torch.empty(1024, dtype=torch.bfloat16, device=dev), torch.empty(1024, **f32),
+               torch.empty(1024, **f32), torch.empty(2048, **f32), torch.empty(1024, **f32),
+               torch.empty(3072, **f32), torch.empty(151936, **f32), torch.empty(2048, **f32),
+               torch.empty(1024, **f32), torch.empty(1024, **f32)]
+    fn = load_launcher()
+    stream = torch.cuda.current_stream()
+
+    def call(tok, pos):
+        code = fn(int(tok), w.embed.data_ptr(), w.embed.data_ptr(), w.final_norm.data_ptr(), table.data_ptr(),
+                  cos.data_ptr(), sin.data_ptr(), k.data_ptr(), v.data_ptr(), *[t.data_ptr() for t in scratch],
+                  int(pos), int(pos) + 1, 512, ctypes.c_void_p(stream.cuda_stream))
+        if code != 0:
+            raise RuntimeError(f"reference launch failed with CUDA error {code}")
+
+    tok = 1
+    for p in range(32 + warmup):
+        call(tok, p)
+        tok = int(torch.argmax(scratch[6]).item())
+    times = []
+    for i in range(steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        call(tok, 32 + warmup + i)
+        e.record(stream)
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+        tok = int(torch.argmax(scratch[6]).item())
+    ms = sum(times) / len(times)
+    return {"us_per_token": ms * 1000.0, "tok_s": 1000.0 / ms, "steps": steps,
+            "source": "reference megakernel.cu built from its sources for sm_100a (oracle/_ref): "
+                      "launch_decode_kernel alone, table and scratch resident, CUDA events around the launch"}
+
+
 def time_reference(steps: int = 64, warmup: int = 5, seed: int = 0) -> dict:
     """Per-token time of the reference kernel on this GPU, config 0 shapes.
 

@@ -141,3 +141,37 @@ def test_engine_prefill_rejects_bad_arguments():
     lib = _lib.load()
     ids = (ctypes.c_int * 4)(1, 2, 3, 4)
     assert lib.mkb_engine_prefill(None, ctypes.cast(ids, ctypes.c_void_p), 4, 0, None, None) != 0
+
+
+def test_every_error_code_has_a_name():
+    """Each ErrorCode of the kernel (mkb_config.cuh) has a name in the C ABI
+    (mkb_error_name) and in the Python table; unknown codes say so."""
+    src = open(os.path.join(ROOT, "megakernel_b200", "csrc", "mkb_config.cuh")).read()
+    body = src[src.index("enum ErrorCode"):]
+    body = body[:body.index("};")]
+    codes = {name: int(val) for name, val in re.findall(r"\b(kErr\w+)\s*=\s*(\d+)", body)}
+    assert codes["kErrNone"] == 0 and "kErrRange" in codes
+    lib = _lib.load()
+    for name, val in codes.items():
+        c_name = lib.mkb_error_name(val).decode()
+        assert c_name != "unknown", name
+        assert _lib.ERROR_NAMES[val] == c_name, name
+    assert lib.mkb_error_name(max(codes.values()) + 1).decode() == "unknown"
+
+
+def test_decode_args_mirror_matches_the_header():
+    """The ctypes mirror of mkb_decode_args lists the header's fields in order."""
+    src = open(os.path.join(ROOT, "include", "mkb200.h")).read()
+    body = src[src.index("typedef struct mkb_decode_args {"):src.index("} mkb_decode_args;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S).split("{", 1)[1]
+    names = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if not decl:
+            continue
+        head, _, rest = decl.rpartition(" ")
+        # "int layer_begin, layer_end" declares several fields
+        first = decl.split(",")
+        names.append(re.findall(r"\**(\w+)$", first[0].strip())[0])
+        names += [re.sub(r"^\*+", "", x.strip()) for x in first[1:]]
+    assert names == [f[0] for f in _lib.DecodeArgs._fields_]
