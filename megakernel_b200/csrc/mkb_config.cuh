@@ -199,7 +199,7 @@ struct DecodeParams {
 enum TraceKind : uint32_t { kTrWaitBegin = 0, kTrWaitEnd = 1, kTrPublish = 2, kTrMark = 3 };
 // Trace window: consumer stamps staged in shared memory for these layers.
 constexpr int kTraceLayerLo = 8;
-constexpr int kTraceLayers = 8;
+constexpr int kTraceLayers = 4;
 constexpr int kTraceSmem = 192;
 
 enum TraceStage : uint32_t {
@@ -209,7 +209,18 @@ enum TraceStage : uint32_t {
   kSubDENorm = 13, kSubDEGU = 14, kSubDEDown = 15,
   kStRing = 16,   // consumer waited for a ring slot to fill
   kStSlot = 17,   // producer waited for a ring slot to empty (layer field = chunk index & 31)
-  kStIssue = 18   // producer issued a chunk
+  kStIssue = 18,  // producer issued a chunk
+  // finer sub-stage marks of the consumer chain
+  kSubAMma = 19,       // QKV: MMA tiles of a pass done
+  kSubABar = 20,       // QKV: warp partials stashed, barrier passed
+  kSubBCAttW = 21,     // attention: per-warp partials written, barrier passed
+  kSubBCOMma = 22,     // o_proj: MMA tiles of a chunk done
+  kSubBCOBar = 23,     // o_proj: barrier passed (sums follow)
+  kSubDEMma = 24,      // gate/up: MMA tiles of a pass done
+  kSubDEBar = 25,      // gate/up: barrier passed (sums follow)
+  kSubDESilu = 26,     // SwiGLU values formed and sent, barrier passed
+  kSubDEOwn = 27,      // down: own rows reduced
+  kSubDERx = 28        // down: partner's SwiGLU values arrived
 };
 
 // ---------------------------------------------------------------------------

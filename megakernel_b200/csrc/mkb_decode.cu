@@ -1008,10 +1008,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         if (na > 1) mma_tile_1024(sa[1], ea1 - ra1, bfr, d1);
         if (na > 2) mma_tile_1024(sa[2], ea2 - ra2, bfr, d2);
         ring_done_all(c, n, na);
+        tr.mark(kTrMark, kSubAMma, l, t);
         stash_tile(xred, 0, d0);
         stash_tile(xred, 1, d1);
         stash_tile(xred, 2, d2);
         consumer_sync(kConsumerThreads);
+        tr.mark(kTrMark, kSubABar, l, t);
         if (tid < 48 && !(t == 0 && l == lb && c.cta == p.withhold_cta)) {
           const int i = tid >> 4;
           const int row = (i == 0 ? ra0 : (i == 1 ? ra1 : ra2)) + (tid & 15);
@@ -1242,6 +1244,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             sm.u.att[warp][lane >> 4][kHeadDim + 1] = lsum;
           }
           consumer_sync(kConsumerThreads);
+          tr.mark(kTrMark, kSubBCAttW, l, t);
           if (tid < 2 * kHeadDim) {
             const int hh = tid >> 7, d = tid & (kHeadDim - 1);
             float M = -INFINITY;
@@ -1366,9 +1369,11 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
               }
             }
             ring_done(c, n);
+            tr.mark(kTrMark, kSubBCOMma, l, t);
 #pragma unroll
             for (int tt = 0; tt < 4; ++tt) stash_tile(xred, tt, d[tt]);
             consumer_sync(kConsumerThreads);
+            tr.mark(kTrMark, kSubBCOBar, l, t);
             if (tid < nrows) {
               bool bad = false;
               red_add_u64(&ws->acc_mid[l][o0 + tid], acc_term(sum_warps(xred, tid), bad));
@@ -1418,10 +1423,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         if (ng > 1) mma_tile_gu(sa[1], min(kGUPerChunk, nj - jb0 - kGUPerChunk), bfr, d1);
         if (ng > 2) mma_tile_gu(sa[2], min(kGUPerChunk, nj - jb0 - 2 * kGUPerChunk), bfr, d2);
         ring_done_all(c, n, ng);
+        tr.mark(kTrMark, kSubDEMma, l, t);
         stash_tile(xred, 0, d0);
         stash_tile(xred, 1, d1);
         stash_tile(xred, 2, d2);
         consumer_sync(kConsumerThreads);
+        tr.mark(kTrMark, kSubDEBar, l, t);
         if (tid < 16 * ng) {
           const int i = (tid & 15) & 7;
           const int j = jb0 + (tid >> 4) * kGUPerChunk + i;
@@ -1442,6 +1449,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         }
       }
       consumer_sync(kConsumerThreads);
+      tr.mark(kTrMark, kSubDESilu, l, t);
       if constexpr (fused) {
         // Down projection split by output columns within the cluster pair: rank r
         // reduces columns [kSlice r, kSlice (r + 1)) over both CTAs' intermediate
@@ -1454,8 +1462,10 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           down_rows(sa[0], sm.m, nj, pa0, pa1);
           ring_done_all(c, n, 1);
         }
+        tr.mark(kTrMark, kSubDEOwn, l, t);
         if (rx_live) rx_live = cluster_rx_wait(c, &sm.rxbar, xph, l, kStDE, t);
         xph ^= 1u;
+        tr.mark(kTrMark, kSubDERx, l, t);
         {
           uint32_t sa[1];
           ring_wait_all(c, n, 1, sa, l, 5, t, &tr);

@@ -27,7 +27,9 @@ STAGE_NAMES = {0: "qkv", 1: "attn+o_proj", 2: "swiglu(+down)", 3: "down", 4: "lm
                5: "split-combine", 6: "token", 7: "end", 8: "qkv:input", 9: "qkv:norm",
                10: "attn:head-prep", 11: "attn:softmax-v", 12: "attn:combine", 13: "swiglu:input+norm",
                14: "swiglu:gate-up", 15: "swiglu:down", 16: "ring-fill", 17: "slot-free", 18: "issue",
-               19: "mark19", 20: "mark20", 21: "mark21", 22: "mark22", 23: "mark23"}
+               19: "qkv:mma", 20: "qkv:stash+bar", 21: "attn:partials+bar", 22: "o_proj:mma",
+               23: "o_proj:stash+bar", 24: "gate-up:mma", 25: "gate-up:stash+bar", 26: "swiglu:silu+send+bar",
+               27: "down:own-rows", 28: "down:partner-wait"}
 KIND_NAMES = {0: "pre-wait", 1: "wait", 2: "publish", 3: "mark"}
 
 
