@@ -23,6 +23,10 @@ in-engine, 256 greedy steps at positions 3584.. (cache lengths 3585..3840).
 * roofline: decode_kernel's algorithmic bytes (every weight byte once per token
   + KV bytes read) / its measured launch duration, against the measured HBM peak.
 * cpu_baseline: HF Qwen3 FP32 decode on this host's cores (oracle), rank 0, N=1.
+* tp (N > 1): the same greedy loop with the model split over the N GPUs
+  (tensor parallel: KV heads, SwiGLU rows and vocabulary rows per rank, the two
+  hidden-state all-reduces per layer and the argmax inside the kernel over NVLink),
+  one stream: per-token latency, device-timed, max over ranks.
 
 ``--impl reference`` times the reference's model path on the host CPU (HF
 Qwen3ForCausalLM FP32, the comparison decode of model.py:139-180) for the same
@@ -455,7 +459,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     import megakernel_b200 as mk
 
-    embed, final_norm, layers = synthetic_weights(1000 + rank, dev)
+    # the same weights on every rank (the tensor-parallel run below shares them);
+    # the replicas are independent streams through their own prompts
+    embed, final_norm, layers = synthetic_weights(1000, dev)
     k = torch.zeros((LAYERS, 8, MAX_SEQ, 128), dtype=torch.bfloat16, device=dev)
     v = torch.zeros_like(k)
     eng = mk.DecodeEngine(embed, final_norm, layers, k, v, fused_down=True, use_graph=True)
@@ -555,11 +561,64 @@ def main():
                 line["cpu_baseline"] = cpu_baseline()
             except Exception as e:
                 line["cpu_baseline"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
-        print(json.dumps(line), flush=True)
     eng.close()
+    if world > 1:
+        tp = tensor_parallel_run(rank, world, dev, embed, final_norm, layers, steps, warm, local)
+        if rank == 0:
+            line["tp"] = tp
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def tensor_parallel_run(rank, world, dev, embed, final_norm, layers, steps, warm, local):
+    """One decode stream with the model split over `world` GPUs (megakernel_b200.tp):
+    32-token prompt prefilled, then `steps` greedy tokens in one launch per rank,
+    CUDA events on each rank, max over ranks."""
+    import torch.distributed as dist
+    from megakernel_b200.tp import TPDecodeEngine
+    res, ok = {}, 1.0
+    tpe = None
+    try:
+        h = 8 // world
+        ks = torch.zeros((LAYERS, h, MAX_SEQ, 128), dtype=torch.bfloat16, device=dev)
+        vs = torch.zeros_like(ks)
+        tpe = TPDecodeEngine(embed, final_norm, layers, ks, vs)
+        prompt = torch.randint(0, VOCAB, (PROMPT,), generator=torch.Generator().manual_seed(0)).tolist()
+        first = tpe.prefill(prompt)
+        n = min(steps, MAX_SEQ - PROMPT)
+        out = torch.empty(n, dtype=torch.int32, device=dev)
+        tpe.generate(first, PROMPT, min(warm, n), out=out[:min(warm, n)])
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms, clocks, _ = timed_region(local, lambda: tpe.generate(first, PROMPT, n, out=out))
+        st = tpe.status()
+        if st[0] != 0:
+            raise RuntimeError(f"in-kernel error {st}")
+        res = {"us_per_token": None, "tp_size": world, "tokens": n, "device_ms_local": ms, "clocks": clocks,
+               "split": f"KV heads {h}/GPU, SwiGLU rows {3072 // world}/GPU, vocabulary rows {VOCAB // world}/GPU",
+               "exchange": "in-kernel over NVLink: o_proj partials added into every GPU's counted accumulators, "
+                           "down-projection sums reduced per GPU then forwarded (one CTA per GPU), argmax "
+                           "candidates red.max into every GPU; local polling only"}
+    except Exception as e:  # reported, never fatal for the replica measurement above
+        ok = 0.0
+        res = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    flags = max_over_ranks([1.0 - ok, res.get("device_ms_local", 0.0)], world, dev)
+    if flags[0] > 0:
+        res = res if "unavailable" in res else {"unavailable": "failed on another rank"}
+    else:
+        res["us_per_token"] = flags[1] * 1000.0 / res["tokens"]
+        res["tok_s"] = res["tokens"] / (flags[1] / 1000.0)
+        res["bytes_per_gpu_per_token"] = WEIGHT_BYTES / world
+        res.pop("device_ms_local", None)
+    if tpe is not None:
+        try:
+            tpe.close()
+        except Exception:
+            pass
+    return res
 
 
 if __name__ == "__main__":

@@ -144,6 +144,17 @@ typedef struct mkb_decode_args {
                                   eos_token_id check, model.py:102-105): its id is the last
                                   one written, later out_tokens read -1, and no K/V row is
                                   appended for it. */
+  int tp_rank, tp_size;        /* tensor parallel (no counterpart in the
+                                  reference): tp_size 1 (default), 2, 4 or 8 GPUs, one
+                                  launch per GPU at the same time. Rank r takes KV heads
+                                  [r*8/tp_size, (r+1)*8/tp_size), SwiGLU rows and
+                                  vocabulary rows in equal contiguous blocks; k_cache /
+                                  v_cache are its [n_layers, 8/tp_size, max_seq, 128]
+                                  shard; logits receives its vocabulary rows; the
+                                  argmax is over the whole vocabulary. Needs down_t. */
+  void* peer_workspaces[8];    /* tp_size > 1: every rank's workspace as this GPU
+                                  addresses it (peer_workspaces[tp_rank] == workspace;
+                                  the others mapped with mkb_ipc_open) */
 } mkb_decode_args;
 
 void mkb_decode_args_init(mkb_decode_args* a);
@@ -188,6 +199,9 @@ typedef struct mkb_model {
   int use_graph;                    /* 1: replay the per-token launch as a CUDA graph */
   float* logits;                    /* device [vocab] for the last token's logits, or NULL
                                        (the engine then owns the buffer) */
+  int tp_size;                      /* 0 or 1: one GPU. 2, 4, 8: one rank of a tensor-parallel
+                                       group (k_cache/v_cache are the rank's 8/tp_size-head
+                                       shard); every call is refused until mkb_engine_tp_attach */
 } mkb_model;
 
 typedef struct mkb_engine mkb_engine;
@@ -216,14 +230,46 @@ cudaError_t mkb_engine_generate_until(mkb_engine* e, int token, int position, in
  * model.py:72-87 (no counterpart in the reference's kernel). */
 cudaError_t mkb_engine_prefill(mkb_engine* e, const int* prompt_tokens, int n, int position, int* next_token,
                                cudaStream_t stream);
+/* Batched prefill (no counterpart in the reference, which prefills with HF,
+ * model.py:72-87): the n prompt ids (device int[n]) at positions position ..
+ * position+n-1 go through each layer together -- projections as tcgen05
+ * tensor-core GEMMs, causal attention on the tensor cores -- appending their
+ * K/V rows; the last token's logits and greedy id are produced as by
+ * mkb_engine_prefill. Asynchronous. Not for tensor-parallel engines. */
+cudaError_t mkb_engine_prefill_batched(mkb_engine* e, const int* prompt_tokens, int n, int position, int* next_token,
+                                      cudaStream_t stream);
+/* The prefill's GEMM on its own: c[m, n] (FP32, row-major) = (a_hi + a_lo)[m, k]
+ * b[n, k]^T with a_hi / a_lo / b BF16 row-major (16-byte aligned), n a multiple
+ * of 128, k a multiple of 64. Asynchronous. */
+cudaError_t mkb_gemm_bf16_split(const void* a_hi, const void* a_lo, const void* b, float* c, int m, int n, int k,
+                                cudaStream_t stream);
 float* mkb_engine_logits(mkb_engine* e);   /* device [vocab], last token's logits */
 void* mkb_engine_workspace(mkb_engine* e);
+/* Tensor parallel: make this rank's engine one of tp_size (2, 4 or 8) engines
+ * that decode together, one per GPU, every call made on every rank with the
+ * same arguments. peer_workspaces[g] is rank g's mkb_engine_workspace() as this
+ * GPU addresses it (its own for g == tp_rank; the others through
+ * mkb_ipc_export / mkb_ipc_open). The engine's KV cache must be the rank's
+ * [n_layers, 8/tp_size, max_seq, 128] shard and it must use the transposed down
+ * weight. Re-captures the step graph. No counterpart in the reference. */
+cudaError_t mkb_engine_tp_attach(mkb_engine* e, int tp_rank, int tp_size, void* const* peer_workspaces);
+/* Device memory shared across processes for the peer workspaces (CUDA IPC):
+ * export writes 64 opaque bytes for a cudaMalloc'd pointer; open maps another
+ * process's exported pointer into this one (NVLink peer access); close unmaps. */
+cudaError_t mkb_ipc_export(const void* device_ptr, unsigned char handle[64]);
+cudaError_t mkb_ipc_open(const unsigned char handle[64], void** device_ptr);
+cudaError_t mkb_ipc_close(void* device_ptr);
 int mkb_engine_grid(mkb_engine* e);
 void mkb_engine_destroy(mkb_engine* e);
 
 /* ---- schedule introspection (host only, no GPU needed) ------------------------ */
 /* out[0..13] = qa, qb, in_bc, h, c, oa, ob, ja, jb, da, db, va, vb, group_size. */
 int mkb_plan_query(int grid, int cta, int32_t out[16]);
+/* The same for rank tp_rank of a tp_size-GPU launch; out[14] = the CTA's local
+ * KV head (cache shard index); qa/qb are in the rank's local QKV row space,
+ * mapped to [Wq; Wk; Wv] rows by mkb_qkv_global_row. */
+int mkb_plan_query_tp(int grid, int cta, int tp_rank, int tp_size, int32_t out[16]);
+int mkb_qkv_global_row(int tp_rank, int tp_size, int local_row);
 int mkb_choose_splits(int max_cache_len, int group_size);
 void mkb_key_range(int cache_len, int splits, int c, int32_t out[2]);
 /* Keys [out[0], out[1]) that CTA `cta` of a `grid`-CTA launch attends over at

@@ -69,6 +69,9 @@ class DecodeArgs(Structure):
         ("prompt_tokens", c_void_p),
         ("err_flag", c_void_p),
         ("stop_token", c_int),
+        ("tp_rank", c_int),
+        ("tp_size", c_int),
+        ("peer_workspaces", c_void_p * 8),
     ]
 
 
@@ -90,6 +93,7 @@ class Model(Structure):
         ("fused_down", c_int),
         ("use_graph", c_int),
         ("logits", c_void_p),
+        ("tp_size", c_int),
     ]
 
 
@@ -117,11 +121,19 @@ SIGNATURES = [
     ("mkb_engine_generate", c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     ("mkb_engine_generate_until", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     ("mkb_engine_prefill", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    ("mkb_engine_prefill_batched", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    ("mkb_gemm_bf16_split", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     ("mkb_engine_logits", c_void_p, [c_void_p]),
     ("mkb_engine_workspace", c_void_p, [c_void_p]),
+    ("mkb_engine_tp_attach", c_int, [c_void_p, c_int, c_int, POINTER(c_void_p)]),
+    ("mkb_ipc_export", c_int, [c_void_p, ctypes.c_char_p]),
+    ("mkb_ipc_open", c_int, [ctypes.c_char_p, POINTER(c_void_p)]),
+    ("mkb_ipc_close", c_int, [c_void_p]),
     ("mkb_engine_grid", c_int, [c_void_p]),
     ("mkb_engine_destroy", None, [c_void_p]),
     ("mkb_plan_query", c_int, [c_int, c_int, POINTER(c_int32)]),
+    ("mkb_plan_query_tp", c_int, [c_int, c_int, c_int, c_int, POINTER(c_int32)]),
+    ("mkb_qkv_global_row", c_int, [c_int, c_int, c_int]),
     ("mkb_choose_splits", c_int, [c_int, c_int]),
     ("mkb_key_range", None, [c_int, c_int, c_int, POINTER(c_int32)]),
     ("mkb_attn_keys", c_int, [c_int, c_int, c_int, c_int, POINTER(c_int32)]),
@@ -187,6 +199,14 @@ def plan(grid: int, cta: int) -> dict:
         raise ValueError("bad grid/cta")
     keys = ["qa", "qb", "in_bc", "h", "c", "oa", "ob", "ja", "jb", "da", "db", "va", "vb", "group_size"]
     return dict(zip(keys, list(out)[:14]))
+
+
+def plan_tp(grid: int, cta: int, tp_rank: int, tp_size: int) -> dict:
+    out = (c_int32 * 16)()
+    if load().mkb_plan_query_tp(grid, cta, tp_rank, tp_size, out) != 0:
+        raise ValueError("bad grid/cta/tp shape")
+    keys = ["qa", "qb", "in_bc", "h", "c", "oa", "ob", "ja", "jb", "da", "db", "va", "vb", "group_size", "hl"]
+    return dict(zip(keys, list(out)[:15]))
 
 
 def key_range(cache_len: int, splits: int, c: int) -> tuple:

@@ -21,7 +21,7 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(HERE, "libmkb200.so")
 EXT_DIR = os.path.join(HERE, "_build")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-KERNEL_SOURCES = ["mkb_decode.cu", "mkb_host.cu", "mkb_noalloc.cu"]
+KERNEL_SOURCES = ["mkb_decode.cu", "mkb_host.cu", "mkb_noalloc.cu", "mkb_prefill.cu"]
 
 
 def nvcc() -> str:

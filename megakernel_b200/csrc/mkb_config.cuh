@@ -84,6 +84,9 @@ constexpr int kSlice = 1024 / kCluster;  // output columns of the down projectio
 #define MKB_DOWN_COPIES 2
 #endif
 constexpr int kDownCopies = MKB_DOWN_COPIES;
+// Tensor parallelism: at most kMaxTP GPUs, each taking kNKV / tp_size KV heads,
+// a contiguous block of SwiGLU rows and of vocabulary rows.
+constexpr int kMaxTP = 8;
 
 // Flags in DecodeParams::flags.
 enum : int {
@@ -128,10 +131,14 @@ struct alignas(128) Workspace {
   uint32_t error[32];                        // [0] code, [1] cta, [2] layer, [3] stage, [4] token
   uint32_t tag_base[32];                     // [0]: tag of the last token decoded (tagged words)
   uint32_t stop_seen[32];                    // CTAs that saw a stop token (the last one resets tok_flag)
+  uint32_t arrive_x[32];                     // end-of-token arrivals of the other GPUs' CTAs (tensor parallel)
   // Per-layer sums as counted fixed-point words (see kAccShift): o_proj
   // partials (one per KV head) and down-proj partials (one per CTA).
   uint64_t acc_mid[kMaxLayers][kHidden];
   uint64_t acc_down[kMaxLayers][kDownCopies][kHidden];
+  // Tensor parallel: each GPU's complete down-projection sum, forwarded by one
+  // CTA of every GPU into every GPU's copy (tp_size contributions per element).
+  uint64_t acc_x[kMaxLayers][kHidden];
   // K/V append of (layer, KV head) published for a later token of the same
   // launch (two adds per token: the K and the V writer).
   uint32_t kv_ready[kMaxLayers][kNKV][32];
@@ -149,8 +156,22 @@ struct alignas(128) Workspace {
 
 // Fields read or cleared with 16-byte vector accesses.
 static_assert(offsetof(Workspace, acc_mid) % 16 == 0 && offsetof(Workspace, acc_down) % 16 == 0 &&
+                  offsetof(Workspace, acc_x) % 16 == 0 &&
                   offsetof(Workspace, resid) % 16 == 0 && offsetof(Workspace, qkv_tagged) % 16 == 0,
               "workspace vector fields must be 16-byte aligned");
+
+// Scratch of the batched prefill (mkb_prefill.cu), owned by the engine; cap rows.
+struct PrefillScratch {
+  float* h;                  // [cap, 1024] residual
+  __nv_bfloat16* ah;         // [cap, 2048] GEMM A operand (normed activation, attention output), high part
+  __nv_bfloat16* al;         //              remainder
+  __nv_bfloat16* mh;         // [cap, 3072] SwiGLU output (the down GEMM's A operand), high part
+  __nv_bfloat16* ml;         //              remainder
+  float* qkv;                // [cap, 4096]
+  float* q;                  // [cap, 2048] rotated, scaled queries
+  uint32_t* err;             // device error word (a GEMM wait that expired)
+  int cap;
+};
 
 // Launch parameters (passed by value; all pointers are device pointers).
 struct DecodeParams {
@@ -191,6 +212,9 @@ struct DecodeParams {
   const int* prompt;                 // prefill: forced input tokens [n_tokens], LM head on the last only
   uint32_t* err_flag;                // optional (host-mapped) word that receives the error code
   int stop_token;                    // end the launch after generating this id (-1: none)
+  int tp_rank, tp_size;              // tensor parallel position (size 1: single GPU)
+  Workspace* peer_ws[kMaxTP];        // every rank's workspace as this GPU addresses it
+                                     // (peer_ws[tp_rank] == ws)
 };
 
 // Trace record: (code << 48) | (globaltimer ns & 0xffffffffffff). Row cta is
@@ -230,40 +254,76 @@ __host__ __device__ inline int part(int n, int parts, int i) {
   return (int)(((long long)n * i) / parts);
 }
 
+// This GPU's share of a tensor-parallel launch (size 1: everything).
+struct TpShape {
+  int rank, size;
+  int hl, h0;     // local KV heads and the first global one
+  int i0, i1;     // SwiGLU rows [i0, i1)
+  int v0, v1;     // vocabulary rows [v0, v1)
+};
+
+__host__ __device__ inline TpShape tp_shape(int rank, int size, int vocab) {
+  TpShape s;
+  s.rank = rank;
+  s.size = size;
+  s.hl = kNKV / size;
+  s.h0 = rank * s.hl;
+  s.i0 = part(kInter, size, rank);
+  s.i1 = part(kInter, size, rank + 1);
+  s.v0 = part(vocab, size, rank);
+  s.v1 = part(vocab, size, rank + 1);
+  return s;
+}
+
+// This GPU's QKV rows in a local row space: its heads' q rows, then k rows,
+// then v rows (2 * 128 * hl, 128 * hl, 128 * hl). A local row maps to the
+// concatenated [Wq; Wk; Wv] row space; rows stay contiguous inside a segment.
+__host__ __device__ inline int qkv_local_rows(const TpShape& s) { return 4 * kHeadDim * s.hl; }
+__host__ __device__ inline int qkv_global_row(const TpShape& s, int r) {
+  const int nq = 2 * kHeadDim * s.hl, nk = kHeadDim * s.hl;
+  if (r < nq) return s.h0 * 2 * kHeadDim + r;
+  if (r < nq + nk) return kQSize + s.h0 * kHeadDim + (r - nq);
+  return kQSize + kKVSize + s.h0 * kHeadDim + (r - nq - nk);
+}
+
 struct Plan {
-  int qa, qb;     // QKV rows [qa, qb) of the concatenated [Wq; Wk; Wv]
+  int qa, qb;     // QKV rows [qa, qb) of this GPU's local row space (qkv_global_row)
   int in_bc;      // takes part in attention + o_proj
-  int h, c;       // KV head and index inside its group
+  int h, c;       // KV head (global) and index inside its group
+  int hl;         // KV head index on this GPU (its KV-cache shard)
   int oa, ob;     // o_proj rows
   int ja, jb;     // gate/up rows (and rows of the transposed down weight)
   int da, db;     // down rows (reference layout)
   int va, vb;     // LM-head rows
 };
 
-__host__ __device__ inline Plan make_plan(int cta, int grid, int group_size, int vocab) {
+__host__ __device__ inline Plan make_plan(int cta, int grid, int group_size, const TpShape& s) {
   Plan p;
-  p.qa = part(kQKVRows, grid, cta);
-  p.qb = part(kQKVRows, grid, cta + 1);
-  const int nbc = kNKV * group_size;
+  const int nq = qkv_local_rows(s);
+  p.qa = part(nq, grid, cta);
+  p.qb = part(nq, grid, cta + 1);
+  const int nbc = s.hl * group_size;
   p.in_bc = cta < nbc;
-  p.h = p.in_bc ? cta / group_size : 0;
+  p.hl = p.in_bc ? cta / group_size : 0;
+  p.h = s.h0 + p.hl;
   p.c = p.in_bc ? cta % group_size : 0;
   p.oa = p.in_bc ? part(kHidden, group_size, p.c) : 0;
   p.ob = p.in_bc ? part(kHidden, group_size, p.c + 1) : 0;
-  p.ja = part(kInter, grid, cta);
-  p.jb = part(kInter, grid, cta + 1);
+  p.ja = s.i0 + part(s.i1 - s.i0, grid, cta);
+  p.jb = s.i0 + part(s.i1 - s.i0, grid, cta + 1);
   p.da = part(kHidden, grid, cta);
   p.db = part(kHidden, grid, cta + 1);
-  p.va = part(vocab, grid, cta);
-  p.vb = part(vocab, grid, cta + 1);
+  p.va = s.v0 + part(s.v1 - s.v0, grid, cta);
+  p.vb = s.v0 + part(s.v1 - s.v0, grid, cta + 1);
   return p;
 }
 
-// End of the QKV chunk that starts at row r: at most kQKVRowsPerChunk rows,
-// never crossing the q/k/v matrix boundaries.
-__host__ __device__ inline int qkv_chunk_end(int r, int qb) {
+// End of the QKV chunk that starts at local row r: at most kQKVRowsPerChunk
+// rows, never crossing the q/k/v segment boundaries of the local row space.
+__host__ __device__ inline int qkv_chunk_end(int r, int qb, const TpShape& s) {
   int e = r + kQKVRowsPerChunk;
-  const int bound = r < kQSize ? kQSize : (r < kQSize + kKVSize ? kQSize + kKVSize : kQKVRows);
+  const int nq = 2 * kHeadDim * s.hl, nk = kHeadDim * s.hl;
+  const int bound = r < nq ? nq : (r < nq + nk ? nq + nk : qkv_local_rows(s));
   if (e > bound) e = bound;
   if (e > qb) e = qb;
   return e;
@@ -279,8 +339,8 @@ __host__ __device__ inline void key_range(int cache_len, int splits, int c, int*
 
 // Both CTAs of cluster pair `cta / 2` attend over the same KV head (true for
 // every pair when the head group size is even, as on 148 SMs).
-__host__ __device__ inline bool pair_shares_head(int cta, int grid, int group_size, int vocab) {
-  const Plan a = make_plan(cta & ~1, grid, group_size, vocab), b = make_plan(cta | 1, grid, group_size, vocab);
+__host__ __device__ inline bool pair_shares_head(int cta, int grid, int group_size, const TpShape& s) {
+  const Plan a = make_plan(cta & ~1, grid, group_size, s), b = make_plan(cta | 1, grid, group_size, s);
   return a.in_bc && b.in_bc && a.h == b.h;
 }
 

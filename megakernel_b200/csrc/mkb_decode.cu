@@ -173,6 +173,27 @@ __device__ __noinline__ void spin_geq(const Ctl c, const uint32_t* ctr, uint32_t
   }
 }
 
+// spin_geq on a counter that other GPUs add into (tensor parallel).
+__device__ __noinline__ void spin_geq_sys(const Ctl c, const uint32_t* ctr, uint32_t target, uint32_t code,
+                                          int layer, int stage, int tok) {
+  if (aborted(c)) return;
+  const uint64_t t0 = global_ns();
+  uint32_t it = 0;
+  while (static_cast<int>(ld_acquire_sys(ctr) - target) < 0) {
+    if ((++it & 15u) == 0u) {
+      if (aborted(c)) return;
+      if (ld_relaxed(&c.ws->error[0]) != 0u) {
+        *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
+        return;
+      }
+      if (global_ns() - t0 > c.timeout) {
+        raise_error(c, code, layer, stage, tok);
+        return;
+      }
+    }
+  }
+}
+
 // Consumer-side transition: thread 0 waits, then all consumers proceed.
 template <class TR>
 __device__ __forceinline__ void transition_wait(const Ctl& c, TR& tr, const uint32_t* ctr, uint32_t target,
@@ -365,18 +386,20 @@ template <bool kFused, bool kTraced>
 __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int pos0, int cl0,
                              int splits) {
   Producer pr(c);
-  const bool pair_attn = pair_shares_head(static_cast<int>(blockIdx.x), p.grid, p.group_size, kVocab);
+  const TpShape tp = tp_shape(p.tp_rank, p.tp_size, kVocab);
+  const bool pair_attn = pair_shares_head(static_cast<int>(blockIdx.x), p.grid, p.group_size, tp);
   for (int t = 0; t < p.n_tokens && !pr.stop; ++t) {
     const int pos = pos0 + t;
     const int cl = cl0 + t;
     for (int l = p.layer_begin; l < p.layer_end && !pr.stop; ++l) {
       // A: QKV rows, one bulk copy per row into a padded row slot
       for (int r = pl.qa; r < pl.qb;) {
-        const int e = qkv_chunk_end(r, pl.qb);
-        const __nv_bfloat16* src = r < kQSize ? lwt(pr.c, l, kWQ) + (size_t)r * kHidden
-                                   : r < kQSize + kKVSize
-                                       ? lwt(pr.c, l, kWK) + (size_t)(r - kQSize) * kHidden
-                                       : lwt(pr.c, l, kWV) + (size_t)(r - kQSize - kKVSize) * kHidden;
+        const int e = qkv_chunk_end(r, pl.qb, tp);
+        const int g = qkv_global_row(tp, r);  // rows of a chunk are contiguous in [Wq; Wk; Wv]
+        const __nv_bfloat16* src = g < kQSize ? lwt(pr.c, l, kWQ) + (size_t)g * kHidden
+                                   : g < kQSize + kKVSize
+                                       ? lwt(pr.c, l, kWK) + (size_t)(g - kQSize) * kHidden
+                                       : lwt(pr.c, l, kWV) + (size_t)(g - kQSize - kKVSize) * kHidden;
         const int s = pr.begin(static_cast<uint32_t>(e - r) * kHidden * 2u);
         if (s < 0) break;
         if (pr.lane < e - r)
@@ -395,7 +418,8 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           spin_geq(c, &p.ws->kv_ready[l][pl.h][0], 2u * static_cast<uint32_t>(t), kErrTimeoutTransition, l, 10, t);
           fence_proxy_async_global();
         }
-        const size_t head_off = ((size_t)l * kNKV + pl.h) * (size_t)p.max_seq * kHeadDim;
+        // this GPU's cache shard holds its tp.hl heads
+        const size_t head_off = ((size_t)l * tp.hl + pl.hl) * (size_t)p.max_seq * kHeadDim;
         const __nv_bfloat16* kbase = p.k_cache + head_off;
         const __nv_bfloat16* vbase = p.v_cache + head_off;
         for (int k0 = ka; k0 < kb; k0 += kKeysPerChunk) {
@@ -451,8 +475,8 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         // then its cluster partner's rows (one slot each)
         const uint32_t rank = cluster_ctarank();
         const __nv_bfloat16* wdt = lwt(pr.c, l, kWDownT) + (size_t)rank * kInter * kSlice;
-        const int partner = static_cast<int>(blockIdx.x ^ 1u);
-        const int rows[2][2] = {{pl.ja, pl.jb}, {part(kInter, p.grid, partner), part(kInter, p.grid, partner + 1)}};
+        const Plan pp = make_plan(static_cast<int>(blockIdx.x ^ 1u), p.grid, p.group_size, tp);
+        const int rows[2][2] = {{pl.ja, pl.jb}, {pp.ja, pp.jb}};
         for (int q = 0; q < 2; ++q) {
           const uint32_t bytes = static_cast<uint32_t>(rows[q][1] - rows[q][0]) * kSlice * 2u;
           const int s = pr.begin(bytes);
@@ -740,10 +764,11 @@ __device__ __forceinline__ float acc_decode(uint64_t low, uint64_t cnt) {
 }
 // Sum carried by `copies` words at stride kHidden; `count` receives the number
 // of contributions.
-__device__ __forceinline__ float acc_value(const uint64_t* w, int copies, uint32_t& count) {
+// `sys`: the words also receive other GPUs' contributions (tensor parallel).
+__device__ __forceinline__ float acc_value(const uint64_t* w, int copies, uint32_t& count, bool sys = false) {
   uint64_t low = 0, cnt = 0;
   for (int q = 0; q < copies; ++q) {
-    const uint64_t v = ld_relaxed_u64(w + q * kHidden);
+    const uint64_t v = sys ? ld_relaxed_u64_sys(w + q * kHidden) : ld_relaxed_u64(w + q * kHidden);
     cnt += v >> 56;
     low += v & kAccLowMask;
   }
@@ -752,12 +777,12 @@ __device__ __forceinline__ float acc_value(const uint64_t* w, int copies, uint32
 }
 // Bounded poll of one element until it holds `expect` contributions.
 __device__ __noinline__ float acc_wait_slow(const Ctl c, const uint64_t* w, int copies, uint32_t expect, int layer,
-                                            int stage, int tok) {
+                                            int stage, int tok, bool sys) {
   const uint64_t t0 = global_ns();
   uint32_t it = 0, cnt = 0;
   float v = 0.f;
   while (true) {
-    v = acc_value(w, copies, cnt);
+    v = acc_value(w, copies, cnt, sys);
     if (cnt == expect) break;
     if ((++it & 15u) == 0u) {
       if (aborted(c) || ld_relaxed(&c.ws->error[0]) != 0u) {
@@ -776,13 +801,13 @@ __device__ __noinline__ float acc_wait_slow(const Ctl c, const uint64_t* w, int 
 // (e1 < 0: e0 only) both hold `expect` contributions; both are loaded in every
 // round, so the second costs no extra round trip.
 __device__ __noinline__ void acc_wait_pair(const Ctl c, const uint64_t* row, int copies, uint32_t expect, int e0,
-                                           int e1, int layer, int stage, int tok) {
+                                           int e1, int layer, int stage, int tok, bool sys) {
   const uint64_t t0 = global_ns();
   uint32_t it = 0;
   while (true) {
     uint32_t n0 = 0, n1 = expect;
-    acc_value(row + e0, copies, n0);
-    if (e1 >= 0) acc_value(row + e1, copies, n1);
+    acc_value(row + e0, copies, n0, sys);
+    if (e1 >= 0) acc_value(row + e1, copies, n1, sys);
     if (n0 == expect && n1 == expect) break;
     if ((++it & 15u) == 0u) {
       if (aborted(c) || ld_relaxed(&c.ws->error[0]) != 0u) {
@@ -804,16 +829,23 @@ __device__ __noinline__ void acc_wait_pair(const Ctl c, const uint64_t* row, int
 // L2 lines, so the fewer poll loads the faster the exchange (measured).
 // Elements still incomplete after the barrier are polled by their owners.
 __device__ __forceinline__ void acc_wait4(const Ctl& c, const uint64_t* row, int copies, uint32_t expect,
-                                          uint32_t expect0, int s0, float v[4], int layer, int stage, int tok) {
+                                          uint32_t expect0, int s0, float v[4], int layer, int stage, int tok,
+                                          bool sys = false) {
   const uint64_t* w = row + threadIdx.x * kE;
-  if (threadIdx.x == 0) acc_wait_pair(c, row, 1, expect0, s0, -1, layer, stage, tok);
-  if (threadIdx.x == 32 && copies > 1) acc_wait_pair(c, row + kHidden, 1, expect - expect0, s0, -1, layer, stage, tok);
+  if (threadIdx.x == 0) acc_wait_pair(c, row, 1, expect0, s0, -1, layer, stage, tok, sys);
+  if (threadIdx.x == 32 && copies > 1)
+    acc_wait_pair(c, row + kHidden, 1, expect - expect0, s0, -1, layer, stage, tok, sys);
   consumer_sync(kConsumerThreads);
   uint64_t low[4] = {0, 0, 0, 0}, cn[4] = {0, 0, 0, 0};
   for (int q = 0; q < copies; ++q) {
     uint64_t a, b, x, y;
-    ld_tagged2(w + q * kHidden, a, b);
-    ld_tagged2(w + q * kHidden + 2, x, y);
+    if (sys) {
+      ld_relaxed2_sys(w + q * kHidden, a, b);
+      ld_relaxed2_sys(w + q * kHidden + 2, x, y);
+    } else {
+      ld_tagged2(w + q * kHidden, a, b);
+      ld_tagged2(w + q * kHidden + 2, x, y);
+    }
     cn[0] += a >> 56; low[0] += a & kAccLowMask;
     cn[1] += b >> 56; low[1] += b & kAccLowMask;
     cn[2] += x >> 56; low[2] += x & kAccLowMask;
@@ -822,7 +854,7 @@ __device__ __forceinline__ void acc_wait4(const Ctl& c, const uint64_t* row, int
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     v[i] = acc_decode(low[i], cn[i]);
-    if (cn[i] != expect) v[i] = acc_wait_slow(c, w + i, copies, expect, layer, stage, tok);
+    if (cn[i] != expect) v[i] = acc_wait_slow(c, w + i, copies, expect, layer, stage, tok, sys);
   }
 }
 // Clear this thread's 4 elements of an accumulator row.
@@ -830,6 +862,26 @@ __device__ __forceinline__ void acc_clear4(uint64_t* row) {
   uint64_t* w = row + threadIdx.x * kE;
   *reinterpret_cast<ulonglong2*>(w) = make_ulonglong2(0ull, 0ull);
   *reinterpret_cast<ulonglong2*>(w + 2) = make_ulonglong2(0ull, 0ull);
+}
+
+// The same field of rank g's workspace (tensor parallel), as this GPU addresses it.
+template <typename T>
+__device__ __forceinline__ T* peer_field(const DecodeParams& p, int g, T* local) {
+  const size_t off = reinterpret_cast<const char*>(local) - reinterpret_cast<const char*>(p.ws);
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(p.peer_ws[g]) + off);
+}
+// One counted contribution to an accumulator word: the local word on a single
+// GPU; with tensor parallelism the same word on every GPU (each one sums all
+// GPUs' contributions). The loop over ranks is unrolled so that the peer table
+// is indexed statically.
+__device__ __forceinline__ void acc_add(const DecodeParams& p, uint64_t* local, uint64_t term) {
+  if (p.tp_size <= 1) {
+    red_add_u64(local, term);
+    return;
+  }
+#pragma unroll
+  for (int g = 0; g < kMaxTP; ++g)
+    if (g < p.tp_size) red_add_u64_sys(peer_field(p, g, local), term);
 }
 
 static_assert(kCluster == 2 && kSlice == 2 * kConsumerThreads, "down projection: two columns per thread");
@@ -871,6 +923,33 @@ __device__ __forceinline__ void poison_outputs(const DecodeParams& p, int va, in
     for (int i = max(t0, 0); i < p.n_tokens; ++i) p.out_tokens[i] = -1;
 }
 
+// The complete down-projection sums of layer l, this thread's 4 elements. One
+// GPU: the local counted accumulator (G / 2 cluster pairs). Tensor parallel:
+// the last CTA of every GPU waits for its GPU's sums and forwards them, one
+// contribution per GPU, into every GPU's acc_x; every CTA then reads acc_x
+// (tp_size contributions). Forwarding keeps the cross-GPU traffic at one word
+// per element and GPU instead of one per cluster pair.
+__device__ __forceinline__ void down_sums(const DecodeParams& p, const Ctl& c, int l, int down_copy0, float d[4],
+                                          int stage, int tok) {
+  const int G = p.grid;
+  if (p.tp_size <= 1) {
+    acc_wait4(c, &p.ws->acc_down[l][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster),
+              static_cast<uint32_t>(down_copy0), 0, d, l, stage, tok);
+    return;
+  }
+  if (c.cta == G - 1) {
+    float v[4];
+    acc_wait4(c, &p.ws->acc_down[l][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster),
+              static_cast<uint32_t>(down_copy0), 0, v, l, stage, tok);
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < kE; ++i) acc_add(p, &p.ws->acc_x[l][threadIdx.x * kE + i], acc_term(v[i], bad));
+    if (bad) raise_error(c, kErrRange, l, stage, tok);
+  }
+  acc_wait4(c, &p.ws->acc_x[l][0], 1, static_cast<uint32_t>(p.tp_size), static_cast<uint32_t>(p.tp_size), 0, d, l,
+            stage, tok, true);
+}
+
 template <bool kFused, bool kTraced>
 __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int token0, int pos0, int cl0,
                              int splits, uint32_t tag0) {
@@ -882,6 +961,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   const int e0 = tid * kE;  // first element owned by this thread
   constexpr bool fused = kFused;
   const int G = p.grid;
+  const TpShape tp = tp_shape(p.tp_rank, p.tp_size, kVocab);
+  const bool tpx = tp.size > 1;
   const int lb = p.layer_begin, le = p.layer_end;
   const int zero_cta = G - 1;
   // contributions that land in copy 0 of a down row: clusters k with k % kDownCopies == 0
@@ -894,13 +975,14 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   // this CTA's rank, the partner's SwiGLU row count, the partner's mrx slot and
   // rxbar for this thread's value, and this pair's copy of the down accumulators.
   const uint32_t crank = cluster_ctarank();
-  const int nj2 = part(kInter, G, (c.cta ^ 1) + 1) - part(kInter, G, c.cta ^ 1);
+  const Plan pplan = make_plan(c.cta ^ 1, G, p.group_size, tp);
+  const int nj2 = pplan.jb - pplan.ja;
   const uint32_t rx_bar_peer = mapa_shared(smem_addr(&sm.rxbar), crank ^ 1u);
   const uint32_t rx_m_peer = mapa_shared(smem_addr(&sm.mrx[tid & 31]), crank ^ 1u);
   const int down_copy = (c.cta / kCluster) % kDownCopies;
   // Attention split between the two CTAs of the pair (same KV head): partner's
   // apeer buffer and atbar, this CTA's phase of atbar, and liveness as for rxbar.
-  const bool pair_attn = pair_shares_head(c.cta, G, p.group_size, kVocab);
+  const bool pair_attn = pair_shares_head(c.cta, G, p.group_size, tp);
   const uint32_t apeer_remote = mapa_shared(smem_addr(&sm.apeer[0][0]), crank ^ 1u);
   const uint32_t atbar_remote = mapa_shared(smem_addr(&sm.atbar), crank ^ 1u);
   uint32_t aph = 0;
@@ -970,8 +1052,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         if constexpr (fused) {
           tr.mark(kTrWaitBegin, kStA, l, t);
           float d[4];
-          acc_wait4(c, &ws->acc_down[l - 1][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster),
-                    static_cast<uint32_t>(down_copy0), 0, d, l, kStA, t);
+          down_sums(p, c, l - 1, down_copy0, d, kStA, t);
           tr.mark(kTrWaitEnd, kStA, l, t);
           const float4 rm = *reinterpret_cast<const float4*>(&sm.rmid[e0]);
           r[0] = rm.x + d[0]; r[1] = rm.y + d[1]; r[2] = rm.z + d[2]; r[3] = rm.w + d[3];
@@ -986,6 +1067,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           acc_clear4(&ws->acc_mid[l - 2][0]);
 #pragma unroll
           for (int q = 0; q < kDownCopies; ++q) acc_clear4(&ws->acc_down[l - 2][q][0]);
+          if (tpx) acc_clear4(&ws->acc_x[l - 2][0]);
         }
       }
       *reinterpret_cast<float4*>(&sm.r[e0]) = make_float4(r[0], r[1], r[2], r[3]);
@@ -996,9 +1078,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       tr.mark(kTrMark, kSubANorm, l, t);
       // QKV rows: up to three padded chunks (one 16-row MMA tile each) per pass
       for (int rr = pl.qa; rr < pl.qb;) {
-        const int ra0 = rr, ea0 = qkv_chunk_end(ra0, pl.qb);
-        const int ra1 = ea0, ea1 = ra1 < pl.qb ? qkv_chunk_end(ra1, pl.qb) : ra1;
-        const int ra2 = ea1, ea2 = ra2 < pl.qb ? qkv_chunk_end(ra2, pl.qb) : ra2;
+        const int ra0 = rr, ea0 = qkv_chunk_end(ra0, pl.qb, tp);
+        const int ra1 = ea0, ea1 = ra1 < pl.qb ? qkv_chunk_end(ra1, pl.qb, tp) : ra1;
+        const int ra2 = ea1, ea2 = ra2 < pl.qb ? qkv_chunk_end(ra2, pl.qb, tp) : ra2;
         const int na = 1 + (ea1 > ra1) + (ea2 > ra2);
         rr = ea2;
         uint32_t sa[3];
@@ -1020,11 +1102,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           const int end = i == 0 ? ea0 : (i == 1 ? ea1 : ea2);
           if ((tid & 15) < 15 && row < end) {
             const float val = sum_warps(xred, tid) * rstd_a;
-            st_tagged(&ws->qkv_tagged[l][row], val, tag);
+            const int grow = qkv_global_row(tp, row);
+            st_tagged(&ws->qkv_tagged[l][grow], val, tag);
             if (l == le - 1) {  // raw QKV outputs are reported for the last layer only
-              float* dst = row < kQSize ? p.q_out + row
-                           : row < kQSize + kKVSize ? p.k_out + (row - kQSize)
-                                                    : p.v_out + (row - kQSize - kKVSize);
+              float* dst = grow < kQSize ? p.q_out + grow
+                           : grow < kQSize + kKVSize ? p.k_out + (grow - kQSize)
+                                                     : p.v_out + (grow - kQSize - kKVSize);
               *dst = val;
             }
           }
@@ -1088,7 +1171,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
               sm.knew[d0 + 64] = __low2float(b23);
               sm.knew[d0 + 65] = __high2float(b23);
               if (pl.c == 0) {
-                __nv_bfloat16* dst = p.k_cache + (((size_t)l * kNKV + h) * p.max_seq + pos) * kHeadDim;
+                __nv_bfloat16* dst = p.k_cache + (((size_t)l * tp.hl + pl.hl) * p.max_seq + pos) * kHeadDim;
                 *reinterpret_cast<__nv_bfloat162*>(dst + d0) = b01;
                 *reinterpret_cast<__nv_bfloat162*>(dst + d0 + 64) = b23;
               }
@@ -1101,7 +1184,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             sm.vnew[d0 + 64] = __low2float(b23);
             sm.vnew[d0 + 65] = __high2float(b23);
             if (pl.c == 0) {
-              __nv_bfloat16* dst = p.v_cache + (((size_t)l * kNKV + h) * p.max_seq + pos) * kHeadDim;
+              __nv_bfloat16* dst = p.v_cache + (((size_t)l * tp.hl + pl.hl) * p.max_seq + pos) * kHeadDim;
               *reinterpret_cast<__nv_bfloat162*>(dst + d0) = b01;
               *reinterpret_cast<__nv_bfloat162*>(dst + d0 + 64) = b23;
             }
@@ -1376,7 +1459,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             tr.mark(kTrMark, kSubBCOBar, l, t);
             if (tid < nrows) {
               bool bad = false;
-              red_add_u64(&ws->acc_mid[l][o0 + tid], acc_term(sum_warps(xred, tid), bad));
+              acc_add(p, &ws->acc_mid[l][o0 + tid], acc_term(sum_warps(xred, tid), bad));
               if (bad) raise_error(c, kErrRange, l, kStBC, t);
             }
             consumer_sync(kConsumerThreads);
@@ -1402,7 +1485,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       {
         float a[4];
         acc_wait4(c, &ws->acc_mid[l][0], 1, static_cast<uint32_t>(kNKV), static_cast<uint32_t>(kNKV), 0, a, l, kStDE,
-                  t);
+                  t, tpx);
         tr.mark(kTrWaitEnd, kStDE, l, t);
         const float4 rv = *reinterpret_cast<const float4*>(&sm.r[e0]);
         float mres[4] = {rv.x + a[0], rv.y + a[1], rv.z + a[2], rv.w + a[3]};
@@ -1521,8 +1604,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       if constexpr (fused) {
         tr.mark(kTrWaitBegin, kStLM, le - 1, t);
         float d[4];
-        acc_wait4(c, &ws->acc_down[le - 1][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster),
-                  static_cast<uint32_t>(down_copy0), 0, d, le - 1, kStLM, t);
+        down_sums(p, c, le - 1, down_copy0, d, kStLM, t);
         tr.mark(kTrWaitEnd, kStLM, le - 1, t);
         const float4 rm = *reinterpret_cast<const float4*>(&sm.rmid[e0]);
         r[0] = rm.x + d[0]; r[1] = rm.y + d[1]; r[2] = rm.z + d[2]; r[3] = rm.w + d[3];
@@ -1570,8 +1652,14 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             bi = sm.best_i[w];
           }
         // ordered before the arrival below by its release
-        asm volatile("red.relaxed.gpu.global.max.u64 [%0], %1;" ::"l"(&ws->tok_best[0]), "l"(argmax_key(bv, bi))
-                     : "memory");
+        if (!tpx) {
+          asm volatile("red.relaxed.gpu.global.max.u64 [%0], %1;" ::"l"(&ws->tok_best[0]), "l"(argmax_key(bv, bi))
+                       : "memory");
+        } else {
+#pragma unroll
+          for (int g = 0; g < kMaxTP; ++g)
+            if (g < tp.size) red_max_u64_sys(peer_field(p, g, &ws->tok_best[0]), argmax_key(bv, bi));
+        }
       }
     }
     // ---- end of token: the last CTA to arrive reduces the argmax and resets ---
@@ -1582,6 +1670,12 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       if (aborted(c)) {
         sm.is_last = -1;
       } else {
+        if (tpx) {
+          // this CTA's arrival on the other GPUs, ordered after its argmax candidate
+#pragma unroll
+          for (int g = 0; g < kMaxTP; ++g)
+            if (g < tp.size && g != tp.rank) red_release_add_sys(peer_field(p, g, &ws->arrive_x[0]), 1u);
+        }
         uint32_t old;
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&ws->arrive[0]) : "memory");
         sm.is_last = (old == tgtG - 1u) ? 1 : 0;
@@ -1603,6 +1697,11 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     }
     if (last_state) {
       int best = -1;
+      if (tpx && tid == 0) {
+        // every CTA of the other GPUs has arrived too (their candidates are in)
+        spin_geq_sys(c, &ws->arrive_x[0], static_cast<uint32_t>(G * (tp.size - 1) * (t + 1)), kErrTimeoutToken, -1,
+                     kStEnd, t);
+      }
       if (lm_now && tid == 0) {
         best = argmax_key_index(__ldcg(&ws->tok_best[0]));
         ws->tok_best[0] = 0ull;  // for the next token (ordered by the release below)
@@ -1617,6 +1716,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       for (int l = max(lb, le - 2); l < le; ++l) {
         acc_clear4(&ws->acc_mid[l][0]);
         for (int q = 0; q < kDownCopies; ++q) acc_clear4(&ws->acc_down[l][q][0]);
+        if (tpx) acc_clear4(&ws->acc_x[l][0]);
       }
       if (final_tok) {
         for (int i = tid; i < kMaxLayers * 4; i += kConsumerThreads) ws->sync[i >> 2][i & 3][0] = 0u;
@@ -1635,12 +1735,14 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         }
         if (last_tok) {
           ws->arrive[0] = 0u;
+          ws->arrive_x[0] = 0u;
           ws->tok_flag[0] = 0u;
           ws->tag_base[0] = tag0 + static_cast<uint32_t>(p.n_tokens);
         } else if (stop_now) {
           // every CTA has arrived for this token and none adds again; tok_flag
           // still carries the stop id to the others (cleared by the last to see it)
           ws->arrive[0] = 0u;
+          ws->arrive_x[0] = 0u;
           ws->tag_base[0] = tag0 + static_cast<uint32_t>(t) + 1u;
           ws->tok_flag[1] = static_cast<uint32_t>(best);
           st_release(&ws->tok_flag[0], static_cast<uint32_t>(t + 1));
@@ -1672,6 +1774,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     cl = pos + 1;
   }
 
+  // tensor parallel shape: 1, 2, 4 or 8 ranks, every peer workspace present,
+  // the fused (transposed-down) schedule
+  bool tp_ok = p.tp_size == 1 || ((p.tp_size == 2 || p.tp_size == 4 || p.tp_size == 8) && kFused);
+  tp_ok = tp_ok && p.tp_rank >= 0 && p.tp_rank < p.tp_size;
+  for (int g = 0; g < kMaxTP; ++g)
+    if (g < p.tp_size && p.tp_size > 1) tp_ok = tp_ok && p.peer_ws[g] != nullptr;
   int misaligned = 0;
   for (int i = threadIdx.x; i < kMaxLayers * 12; i += blockDim.x) {
     const int l = i / 12, f = i % 12;
@@ -1696,8 +1804,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     mbar_init(&sm->atbar, 1);
     mbar_arrive_expect_tx(&sm->atbar, kPairAttnBytes);  // the first pair exchange
     if (kFused) {  // the first layer's phase: one arrival plus the partner's SwiGLU bytes
-      const int pc = static_cast<int>(blockIdx.x) ^ 1;
-      mbar_arrive_expect_tx(&sm->rxbar, static_cast<uint32_t>(part(kInter, p.grid, pc + 1) - part(kInter, p.grid, pc)) * 4u);
+      const Plan pp = make_plan(static_cast<int>(blockIdx.x) ^ 1, p.grid, p.group_size,
+                                tp_shape(p.tp_rank, p.tp_size, kVocab));
+      mbar_arrive_expect_tx(&sm->rxbar, static_cast<uint32_t>(pp.jb - pp.ja) * 4u);
     }
     sm->abort = 0;
     sm->peer_gone = 0;
@@ -1716,8 +1825,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
   // Argument guard (uniform over the grid, before any wait).
   if (token < 0 || token >= kVocab || pos < 0 || pos + p.n_tokens > p.max_seq || cl < 1 ||
       last_cl > p.max_seq || p.grid != static_cast<int>(gridDim.x) || p.grid > kMaxGrid || p.grid < kMinGrid ||
-      p.group_size * kNKV > p.grid || p.grid % kCluster != 0 || splits < 1 || splits > kMaxSplits ||
-      (splits > 1 && splits > p.group_size) || misaligned) {
+      p.group_size * (kNKV / max(p.tp_size, 1)) > p.grid || p.grid % kCluster != 0 || splits < 1 ||
+      splits > kMaxSplits || (splits > 1 && splits > p.group_size) || misaligned || !tp_ok) {
     if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(c, kErrBadArgs, -1, -1, -1);
     // nothing was read or appended; the outputs say so
     if (threadIdx.x < kConsumerThreads)
@@ -1728,7 +1837,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
   // Every CTA of the cluster has initialised its barriers before any remote
   // arrival, and none exits while a peer may still write into its shared memory.
   cluster_sync_all();
-  const Plan pl = make_plan(blockIdx.x, p.grid, p.group_size, kVocab);
+  const Plan pl = make_plan(blockIdx.x, p.grid, p.group_size, tp_shape(p.tp_rank, p.tp_size, kVocab));
   if (stale_err != 0u) {
     // Not uniform over the grid when this launch raised an error of its own
     // before a late CTA started: such a CTA skips its work, so its partner is

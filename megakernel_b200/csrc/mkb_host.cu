@@ -22,6 +22,11 @@
 namespace mkb {
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream);
 size_t decode_smem_bytes();
+cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const __nv_bfloat16* embed,
+                           const void* cos_t, const void* sin_t, int rope_fp32, __nv_bfloat16* kc, __nv_bfloat16* vc,
+                           int max_seq, const int* ids, int n, int pos0, const PrefillScratch& s, cudaStream_t stream);
+cudaError_t gemm_split(const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, const __nv_bfloat16* b, float* c, int M,
+                       int N, int K, uint32_t* err, cudaStream_t stream);
 }  // namespace mkb
 
 using namespace mkb;
@@ -131,7 +136,22 @@ cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p, DeviceInfo** df
   p->grid = a->grid > 0 ? a->grid : grid_for(d->sms);
   if (p->grid > d->sms || p->grid > kMaxGrid || p->grid < kMinGrid || p->grid % kCluster != 0)
     return cudaErrorInvalidConfiguration;
-  p->group_size = p->grid / kNKV;
+  p->tp_rank = a->tp_size > 1 ? a->tp_rank : 0;
+  p->tp_size = a->tp_size > 1 ? a->tp_size : 1;
+  if (p->tp_size != 1 && p->tp_size != 2 && p->tp_size != 4 && p->tp_size != 8) return cudaErrorInvalidValue;
+  if (p->tp_rank < 0 || p->tp_rank >= p->tp_size) return cudaErrorInvalidValue;
+  for (int g = 0; g < kMaxTP; ++g) p->peer_ws[g] = nullptr;
+  if (p->tp_size > 1) {
+    if (!a->down_t) return cudaErrorInvalidValue;  // tensor parallel runs the transposed-down schedule
+    for (int g = 0; g < p->tp_size; ++g) {
+      if (!a->peer_workspaces[g]) return cudaErrorInvalidValue;
+      p->peer_ws[g] = static_cast<Workspace*>(a->peer_workspaces[g]);
+    }
+    if (p->peer_ws[p->tp_rank] != w) return cudaErrorInvalidValue;
+  } else {
+    p->peer_ws[0] = w;
+  }
+  p->group_size = p->grid / (kNKV / p->tp_size);
   p->splits = a->splits > 0 ? a->splits : 0;  // 0: chosen on the device per launch
   if (p->splits > kMaxSplits || p->splits > p->group_size) return cudaErrorInvalidValue;
   p->timeout_ns = a->timeout_ns ? a->timeout_ns : kDefaultTimeoutNs;
@@ -290,7 +310,7 @@ cudaError_t mkb_transpose_down(const void* down, void* down_t, cudaStream_t stre
 int mkb_plan_query(int grid, int cta, int32_t out[16]) {
   if (grid < kNKV || cta < 0 || cta >= grid) return -1;
   const int gs = grid / kNKV;
-  const Plan p = make_plan(cta, grid, gs, kVocab);
+  const Plan p = make_plan(cta, grid, gs, tp_shape(0, 1, kVocab));
   const int32_t v[14] = {p.qa, p.qb, p.in_bc, p.h, p.c, p.oa, p.ob, p.ja, p.jb, p.da, p.db, p.va, p.vb, gs};
   for (int i = 0; i < 14; ++i) out[i] = v[i];
   return 0;
@@ -302,11 +322,25 @@ void mkb_key_range(int cache_len, int splits, int c, int32_t out[2]) {
   out[0] = a;
   out[1] = b;
 }
-int mkb_qkv_chunk_end(int r, int qb) { return qkv_chunk_end(r, qb); }
+int mkb_qkv_chunk_end(int r, int qb) { return qkv_chunk_end(r, qb, tp_shape(0, 1, kVocab)); }
+int mkb_plan_query_tp(int grid, int cta, int tp_rank, int tp_size, int32_t out[16]) {
+  if (tp_size < 1 || tp_size > kMaxTP || kNKV % tp_size || tp_rank < 0 || tp_rank >= tp_size) return -1;
+  const TpShape s = tp_shape(tp_rank, tp_size, kVocab);
+  if (grid < s.hl || cta < 0 || cta >= grid) return -1;
+  const int gs = grid / s.hl;
+  const Plan p = make_plan(cta, grid, gs, s);
+  const int32_t v[15] = {p.qa, p.qb, p.in_bc, p.h, p.c, p.oa, p.ob, p.ja, p.jb, p.da, p.db, p.va, p.vb, gs, p.hl};
+  for (int i = 0; i < 15; ++i) out[i] = v[i];
+  return 0;
+}
+int mkb_qkv_global_row(int tp_rank, int tp_size, int local_row) {
+  return qkv_global_row(tp_shape(tp_rank, tp_size, kVocab), local_row);
+}
 int mkb_attn_keys(int cache_len, int splits, int grid, int cta, int32_t out[2]) {
   const int gs = grid / kNKV;
-  const Plan p = make_plan(cta, grid, gs, kVocab);
-  const bool pair = pair_shares_head(cta, grid, gs, kVocab);
+  const TpShape s = tp_shape(0, 1, kVocab);
+  const Plan p = make_plan(cta, grid, gs, s);
+  const bool pair = pair_shares_head(cta, grid, gs, s);
   int a, b;
   attn_keys(cache_len, splits, p.c, pair, cta & 1, &a, &b);
   out[0] = a;
@@ -324,6 +358,8 @@ struct mkb_engine {
   int n_layers = 0;
   int max_seq = 0;
   int grid = 0;
+  int tp_size = 1;                            // > 1: tensor-parallel rank
+  bool tp_ready = true;                       // false until mkb_engine_tp_attach
   LayerWeights* d_layers = nullptr;
   __nv_bfloat16* d_down_t_buf = nullptr;      // n_layers * [3072, 1024]
   __nv_bfloat16** d_down_t = nullptr;         // n_layers pointers
@@ -340,6 +376,9 @@ struct mkb_engine {
   cudaGraphExec_t graph = nullptr;
   cudaStream_t cap_stream = nullptr;
   mkb_decode_args step_args;
+  std::vector<LayerWeights> host_layers;      // the layer table as the host sees it (prefill tensor maps)
+  PrefillScratch pf = {};                     // batched prefill scratch, allocated on first use
+  void* pf_block = nullptr;
 };
 
 namespace {
@@ -355,6 +394,7 @@ void engine_free(mkb_engine* e) {
   cudaFree(e->d_pf);
   if (e->own_logits) cudaFree(e->d_logits);
   if (e->h_io) cudaFreeHost(e->h_io);
+  cudaFree(e->pf_block);
   delete e;
 }
 
@@ -377,6 +417,7 @@ cudaError_t engine_check_status(mkb_engine* e) {
 // kernel is reported by the next engine call: workspace status printed and
 // reset, cudaErrorLaunchFailure returned, nothing launched.
 cudaError_t engine_report_earlier(mkb_engine* e, cudaStream_t stream) {
+  if (!e->tp_ready) return cudaErrorInvalidValue;  // a tensor-parallel rank before mkb_engine_tp_attach
   if (reinterpret_cast<volatile int*>(e->h_io)[5] == 0) return cudaSuccess;
   cudaError_t err = cudaStreamSynchronize(stream);
   if (err != cudaSuccess) return err;
@@ -402,6 +443,10 @@ cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
   DeviceInfo* d = nullptr;
   MKB_TRY(device_info(e->device, &d));
   e->grid = grid_for(d->sms);
+  e->tp_size = m->tp_size > 1 ? m->tp_size : 1;
+  if (e->tp_size != 1 && e->tp_size != 2 && e->tp_size != 4 && e->tp_size != 8) { engine_free(e); return cudaErrorInvalidValue; }
+  if (e->tp_size > 1 && !m->fused_down) { engine_free(e); return cudaErrorInvalidValue; }
+  e->tp_ready = e->tp_size == 1;
   e->n_layers = m->n_layers;
   e->max_seq = m->max_seq;
 
@@ -417,6 +462,7 @@ cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
                            static_cast<const __nv_bfloat16*>(w[8]), static_cast<const __nv_bfloat16*>(w[9]),
                            static_cast<const __nv_bfloat16*>(w[10])};
   }
+  e->host_layers = host;
   MKB_TRY(cudaMalloc(&e->d_layers, sizeof(LayerWeights) * m->n_layers));
   MKB_TRY(cudaMemcpy(e->d_layers, host.data(), sizeof(LayerWeights) * m->n_layers, cudaMemcpyHostToDevice));
   if (m->fused_down) {
@@ -472,6 +518,8 @@ cudaError_t mkb_engine_create(const mkb_model* m, mkb_engine** out) {
 
   if (m->use_graph) {
     MKB_TRY(cudaStreamCreateWithFlags(&e->cap_stream, cudaStreamNonBlocking));
+  }
+  if (m->use_graph && e->tp_ready) {  // a tensor-parallel rank captures at attach time
     cudaGraph_t g = nullptr;
     MKB_TRY(cudaStreamBeginCapture(e->cap_stream, cudaStreamCaptureModeThreadLocal));
     cudaError_t le = mkb_decode(&a, e->cap_stream);
@@ -553,6 +601,121 @@ cudaError_t mkb_engine_prefill(mkb_engine* e, const int* prompt_tokens, int n, i
   err = mkb_decode(&a, stream);
   if (err != cudaSuccess || !next_token) return err;
   return cudaMemcpyAsync(next_token, e->d_pf + (n - 1), sizeof(int), cudaMemcpyDeviceToDevice, stream);
+}
+
+cudaError_t mkb_engine_tp_attach(mkb_engine* e, int tp_rank, int tp_size, void* const* peer_workspaces) {
+  if (!e || !peer_workspaces) return cudaErrorInvalidValue;
+  if ((tp_size != 2 && tp_size != 4 && tp_size != 8) || tp_rank < 0 || tp_rank >= tp_size) return cudaErrorInvalidValue;
+  if (tp_size != e->tp_size || !e->d_down_t || peer_workspaces[tp_rank] != e->ws) return cudaErrorInvalidValue;
+  mkb_decode_args a = e->step_args;
+  a.tp_rank = tp_rank;
+  a.tp_size = tp_size;
+  for (int g = 0; g < 8; ++g) a.peer_workspaces[g] = g < tp_size ? peer_workspaces[g] : nullptr;
+  DecodeParams check;
+  cudaError_t err = to_params(&a, &check);
+  if (err != cudaSuccess) return err;
+  e->step_args = a;
+  e->tp_ready = true;
+  if (e->cap_stream) {
+    // the step graph carries the launch parameters: capture it (again)
+    if (e->graph) cudaGraphExecDestroy(e->graph);
+    e->graph = nullptr;
+    cudaGraph_t g = nullptr;
+    err = cudaStreamBeginCapture(e->cap_stream, cudaStreamCaptureModeThreadLocal);
+    if (err != cudaSuccess) return err;
+    const cudaError_t le = mkb_decode(&e->step_args, e->cap_stream);
+    const cudaError_t ce = cudaStreamEndCapture(e->cap_stream, &g);
+    if (le != cudaSuccess || ce != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      return le != cudaSuccess ? le : ce;
+    }
+    err = cudaGraphInstantiate(&e->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (err != cudaSuccess) return err;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t mkb_ipc_export(const void* device_ptr, unsigned char handle[64]) {
+  if (!device_ptr || !handle) return cudaErrorInvalidValue;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(device_ptr));
+  if (e != cudaSuccess) return e;
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle, &h, sizeof(h));
+  return cudaSuccess;
+}
+
+cudaError_t mkb_ipc_open(const unsigned char handle[64], void** device_ptr) {
+  if (!handle || !device_ptr) return cudaErrorInvalidValue;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(device_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+cudaError_t mkb_ipc_close(void* device_ptr) { return cudaIpcCloseMemHandle(device_ptr); }
+
+cudaError_t mkb_engine_prefill_batched(mkb_engine* e, const int* prompt_tokens, int n, int position, int* next_token,
+                                      cudaStream_t stream) {
+  if (!e || !prompt_tokens || n < 1) return cudaErrorInvalidValue;
+  if (position < 0 || position + n > e->max_seq) return cudaErrorInvalidValue;
+  if (e->tp_size > 1) return cudaErrorNotSupported;
+  cudaError_t err = engine_report_earlier(e, stream);
+  if (err != cudaSuccess) return err;
+  const mkb_decode_args& sa = e->step_args;
+  if (e->pf_block == nullptr) {
+    // one block: residual, GEMM operands, SwiGLU output, QKV, rotated q, error word
+    const size_t cap = static_cast<size_t>(e->max_seq);
+    const size_t b_h = cap * kHidden * 4, b_a = cap * kQSize * 2, b_m = cap * kInter * 2, b_qkv = cap * kQKVRows * 4,
+                 b_q = cap * kQSize * 4;
+    const size_t total = b_h + 2 * b_a + 2 * b_m + b_qkv + b_q + 256;
+    err = cudaMalloc(&e->pf_block, total);
+    if (err != cudaSuccess) return err;
+    char* p = static_cast<char*>(e->pf_block);
+    e->pf.h = reinterpret_cast<float*>(p);
+    p += b_h;
+    e->pf.ah = reinterpret_cast<__nv_bfloat16*>(p);
+    p += b_a;
+    e->pf.al = reinterpret_cast<__nv_bfloat16*>(p);
+    p += b_a;
+    e->pf.mh = reinterpret_cast<__nv_bfloat16*>(p);
+    p += b_m;
+    e->pf.ml = reinterpret_cast<__nv_bfloat16*>(p);
+    p += b_m;
+    e->pf.qkv = reinterpret_cast<float*>(p);
+    p += b_qkv;
+    e->pf.q = reinterpret_cast<float*>(p);
+    p += b_q;
+    e->pf.cap = e->max_seq;
+  }
+  // a GEMM wait that expires is recorded in the workspace's status word (the
+  // final LM-head launch then refuses the stale workspace and poisons its outputs)
+  e->pf.err = static_cast<Workspace*>(e->ws)->error;
+  err = prefill_layers(e->host_layers.data(), e->n_layers, static_cast<const __nv_bfloat16*>(sa.embed), sa.cos_table,
+                       sa.sin_table, sa.rope_fp32, static_cast<__nv_bfloat16*>(sa.k_cache),
+                       static_cast<__nv_bfloat16*>(sa.v_cache), e->max_seq, prompt_tokens, n, position, e->pf, stream);
+  if (err != cudaSuccess) return err;
+  // final norm + LM head + argmax of the last prompt token (the decode kernel, no layers)
+  mkb_decode_args a = sa;
+  a.step = nullptr;
+  a.layer_begin = 0;
+  a.layer_end = 0;
+  a.token = 0;
+  a.position = position + n - 1;
+  a.cache_len = position + n;
+  a.n_tokens = 1;
+  a.input_residual = e->pf.h + static_cast<size_t>(n - 1) * kHidden;
+  a.out_tokens = e->d_pf + (n - 1);
+  err = mkb_decode(&a, stream);
+  if (err != cudaSuccess || !next_token) return err;
+  return cudaMemcpyAsync(next_token, e->d_pf + (n - 1), sizeof(int), cudaMemcpyDeviceToDevice, stream);
+}
+
+cudaError_t mkb_gemm_bf16_split(const void* a_hi, const void* a_lo, const void* b, float* c, int m, int n, int k,
+                                cudaStream_t stream) {
+  if (!a_hi || !a_lo || !b || !c || m < 1 || n < 128 || n % 128 || k < 64 || k % 64) return cudaErrorInvalidValue;
+  return gemm_split(static_cast<const __nv_bfloat16*>(a_hi), static_cast<const __nv_bfloat16*>(a_lo),
+                    static_cast<const __nv_bfloat16*>(b), c, m, n, k, nullptr, stream);
 }
 
 float* mkb_engine_logits(mkb_engine* e) { return e ? e->d_logits : nullptr; }

@@ -1,0 +1,604 @@
+// Batched prompt prefill: every prompt token of a layer at once, on the
+// Blackwell tensor cores (no counterpart in the reference, which prefills with
+// Hugging Face, model.py:72-87, and copies the cache, model.py:79-87).
+//
+// Per layer, for the n prompt tokens (M = n rows):
+//   RMSNorm (FP32 residual -> activation split into a BF16 high part and the BF16
+//   remainder) -> QKV GEMMs -> q/k RMSNorm + RoPE, K/V rows into the cache ->
+//   causal attention -> o_proj GEMM added into the residual -> RMSNorm ->
+//   gate/up GEMM with the SwiGLU in its epilogue -> down GEMM added into the
+//   residual. The last token's residual then goes through the decode kernel's
+//   final norm + LM head + argmax.
+//
+// GEMMs (gemm_kernel): C[M, N] = (A_hi + A_lo)[M, K] * B[N, K]^T with tcgen05.mma
+// (kind::f16, BF16 x BF16 -> FP32 in TMEM), 128 x 128 tiles, K in steps of 64,
+// operands brought in by TMA tiled loads with 128-byte swizzle through a 4-stage
+// shared-memory ring; one warp issues the loads, one thread the MMAs, four warps
+// read the accumulator back (tcgen05.ld) for the epilogue. Splitting the FP32
+// activation into two BF16 parts keeps the products to about 2^-16 relative,
+// the accuracy of the decode path's GEMVs.
+//
+// Attention (attn_kernel): causal flash attention on the warp-level tensor-core
+// MMA (mma.sync m16n8k16), q and p split the same way, K/V read back from the
+// BF16 cache the kernel before wrote, online softmax in the exp2 domain.
+
+#include <cstdint>
+#include <cstdio>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/mkb200.h"
+#include "mkb_config.cuh"
+#include "mkb_ptx.cuh"
+#include "mkb_tc.cuh"
+
+namespace mkb {
+namespace pf {
+
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4;
+constexpr int kTile = BM * BK * 2;  // 16 KB: one 128 x 64 BF16 operand tile
+constexpr int kGemmThreads = 192;   // warp 0 TMA, warp 1 MMA (+ TMEM), warps 2-5 epilogue
+
+struct GemmSmem {
+  uint8_t a_hi[STAGES][kTile];
+  uint8_t a_lo[STAGES][kTile];
+  uint8_t b[STAGES][kTile];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t done;
+  uint32_t tmem_base;
+  int err;
+};
+constexpr size_t kGemmSmem = sizeof(GemmSmem) + 1024;  // + alignment slack for the 1024-byte swizzle atoms
+
+enum EpiMode : int { kEpiStore = 0, kEpiAdd = 1, kEpiSwiGLU = 2 };
+
+struct GemmArgs {
+  int M, N, K;                 // C [M, N]; K a multiple of 64
+  float* c;                    // kEpiStore: C; kEpiAdd: residual += C (row stride ldc)
+  int ldc;
+  __nv_bfloat16* m_hi;         // kEpiSwiGLU: silu(gate) * up as high part / remainder
+  __nv_bfloat16* m_lo;
+  int ldm;
+  unsigned long long timeout_ns;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t ph, unsigned long long timeout, int* err) {
+  if (mbar_test(bar, ph)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_wait(bar, ph, 20000)) {
+    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+    if (global_ns() - t0 > timeout) {
+      *reinterpret_cast<volatile int*>(err) = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void split_store(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* v, int n8) {
+  // n8 groups of 8 values -> 16-byte stores of each part
+  for (int g = 0; g < n8; ++g) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = v[8 * g + 2 * i], b = v[8 * g + 2 * i + 1];
+      h[i] = pack_bf2(a, b);
+      l[i] = pack_bf2(a - bf_lo(h[i]), b - bf_hi(h[i]));
+    }
+    reinterpret_cast<uint4*>(hi)[g] = make_uint4(h[0], h[1], h[2], h[3]);
+    reinterpret_cast<uint4*>(lo)[g] = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
+                const __grid_constant__ CUtensorMap tb, const __grid_constant__ CUtensorMap tb2, const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  GemmSmem& sm = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM;
+  const int n0 = blockIdx.x * BN;   // kEpiSwiGLU: SwiGLU columns [n0 / 2, n0 / 2 + 64)
+  const int KT = g.K / BK;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    mbar_init(&sm.done, 1);
+    sm.err = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&sm.tmem_base, BN);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = sm.tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tensormap(&ta_hi);
+    tc::prefetch_tensormap(&ta_lo);
+    tc::prefetch_tensormap(&tb);
+    if (kMode == kEpiSwiGLU) tc::prefetch_tensormap(&tb2);
+    int issued = 0;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES && !wait_bounded(&sm.empty[s], ((kt / STAGES) - 1) & 1, g.timeout_ns, &sm.err)) break;
+      mbar_arrive_expect_tx(&sm.full[s], 3 * kTile);
+      tc::tma_load_2d(sm.a_hi[s], &ta_hi, kt * BK, m0, &sm.full[s]);
+      tc::tma_load_2d(sm.a_lo[s], &ta_lo, kt * BK, m0, &sm.full[s]);
+      if (kMode == kEpiSwiGLU) {
+        tc::tma_load_2d(sm.b[s], &tb, kt * BK, n0 / 2, &sm.full[s]);               // 64 gate rows
+        tc::tma_load_2d(sm.b[s] + kTile / 2, &tb2, kt * BK, n0 / 2, &sm.full[s]);  // 64 up rows
+      } else {
+        tc::tma_load_2d(sm.b[s], &tb, kt * BK, n0, &sm.full[s]);
+      }
+      ++issued;
+    }
+    // after a stop, wait (bounded) for the copies still in flight before leaving
+    for (int kt = issued - 1; kt >= 0 && kt >= issued - STAGES && sm.err; --kt) {
+      const uint64_t t0 = global_ns();
+      while (!mbar_wait(&sm.full[kt % STAGES], (kt / STAGES) & 1, 20000))
+        if (global_ns() - t0 > g.timeout_ns) break;
+    }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (!wait_bounded(&sm.full[s], (kt / STAGES) & 1, g.timeout_ns, &sm.err)) break;
+      tc::fence_after_sync();
+      const uint32_t ah = smem_addr(sm.a_hi[s]), al = smem_addr(sm.a_lo[s]), bb = smem_addr(sm.b[s]);
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk) {
+        const uint64_t db = tc::desc_sw128(bb + kk * 32);
+        tc::mma_bf16_ss(tbase, tc::desc_sw128(ah + kk * 32), db, idesc, (kt | kk) != 0);
+        tc::mma_bf16_ss(tbase, tc::desc_sw128(al + kk * 32), db, idesc, 1u);
+      }
+      tc::commit(&sm.empty[s]);  // the stage is free once these MMAs have read it
+    }
+    tc::commit(&sm.done);  // every MMA issued above has completed
+  } else if (warp >= 2) {
+    int go = wait_bounded(&sm.done, 0, g.timeout_ns, &sm.err) && *reinterpret_cast<volatile int*>(&sm.err) == 0;
+    go = __shfl_sync(0xffffffffu, go, 0);  // tcgen05.ld is warp-wide: one decision per warp
+    tc::fence_after_sync();
+    const int q = warp & 3;  // TMEM lanes 32q .. 32q + 31 = tile rows
+    const int row = m0 + 32 * q + lane;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(32 * q) << 16);
+    if (go) {
+      if (kMode == kEpiSwiGLU) {
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          float gv[32], uv[32];
+          tc::tmem_ld32(lane_addr + 32 * half, gv);       // gate columns
+          tc::tmem_ld32(lane_addr + 64 + 32 * half, uv);  // up columns
+          if (row < g.M) {
+            float mv[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mv[i] = gv[i] / (1.0f + expf(-gv[i])) * uv[i];  // silu(g) * u
+            const size_t o = (size_t)row * g.ldm + n0 / 2 + 32 * half;
+            split_store(g.m_hi + o, g.m_lo + o, mv, 4);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int cb = 0; cb < BN / 32; ++cb) {
+          float v[32];
+          tc::tmem_ld32(lane_addr + 32 * cb, v);
+          if (row < g.M) {
+            float4* dst = reinterpret_cast<float4*>(g.c + (size_t)row * g.ldc + n0 + 32 * cb);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float4 x = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              if (kMode == kEpiAdd) {
+                const float4 r = dst[i];
+                x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
+              }
+              dst[i] = x;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x == 0 && sm.err && g.err) atomicCAS(g.err, 0u, static_cast<uint32_t>(kErrTimeoutRing));
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tbase, BN);
+  }
+}
+
+// ---- the other prefill kernels --------------------------------------------------
+
+// h[i] = E[ids[i]] (FP32), ids clamped to the vocabulary.
+__global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ embed, float* h) {
+  const int i = blockIdx.x;
+  const int tok = min(max(ids[i], 0), kVocab - 1);
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(embed + (size_t)tok * kHidden) + threadIdx.x);
+  reinterpret_cast<float4*>(h + (size_t)i * kHidden)[threadIdx.x] = make_float4(bf_lo(u.x), bf_hi(u.x), bf_lo(u.y), bf_hi(u.y));
+}
+
+// RMSNorm of residual row i (megakernel.cu:704-739 formula), written as the
+// BF16 high part and the BF16 remainder (the two GEMM A operands). 256 threads.
+__global__ void rmsnorm_split_kernel(const float* __restrict__ h, const __nv_bfloat16* __restrict__ w,
+                                     __nv_bfloat16* xh, __nv_bfloat16* xl) {
+  __shared__ float red[8];
+  const int i = blockIdx.x, t = threadIdx.x;
+  const float4 v = reinterpret_cast<const float4*>(h + (size_t)i * kHidden)[t];
+  const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+  if ((t & 31) == 0) red[t >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) tot += red[k];
+  const float rstd = rsqrtf(tot * (1.0f / kHidden) + kEps);
+  const uint2 wv = __ldg(reinterpret_cast<const uint2*>(w) + t);
+  const float x[4] = {v.x * rstd * bf_lo(wv.x), v.y * rstd * bf_hi(wv.x), v.z * rstd * bf_lo(wv.y),
+                      v.w * rstd * bf_hi(wv.y)};
+  const uint32_t h01 = pack_bf2(x[0], x[1]), h23 = pack_bf2(x[2], x[3]);
+  reinterpret_cast<uint2*>(xh + (size_t)i * kHidden)[t] = make_uint2(h01, h23);
+  reinterpret_cast<uint2*>(xl + (size_t)i * kHidden)[t] =
+      make_uint2(pack_bf2(x[0] - bf_lo(h01), x[1] - bf_hi(h01)), pack_bf2(x[2] - bf_lo(h23), x[3] - bf_hi(h23)));
+}
+
+__device__ __forceinline__ float rope_val(const void* table, int fp32, size_t idx) {
+  return fp32 ? __ldg(static_cast<const float*>(table) + idx)
+              : __bfloat162float(static_cast<const __nv_bfloat16*>(table)[idx]);
+}
+
+// Per token (blockIdx.x) and head row (one warp per head: 16 q, 8 k, 8 v):
+// q/k RMSNorm over 128 dims + rotate-half RoPE at the token's position
+// (megakernel.cu:490-630), K/V rows into the BF16 cache, q pre-scaled by
+// log2(e) / sqrt(128) for the exp2-domain softmax. blockDim 256 = 8 heads;
+// blockIdx.y picks the group of 8.
+__global__ void qk_rope_kernel(const float* __restrict__ qkv, const __nv_bfloat16* __restrict__ qn,
+                               const __nv_bfloat16* __restrict__ kn, const void* cos_t, const void* sin_t, int fp32,
+                               int pos0, int layer, __nv_bfloat16* kc, __nv_bfloat16* vc, int max_seq, float* q_out) {
+  const int i = blockIdx.x;
+  const int head = blockIdx.y * 8 + (threadIdx.x >> 5);  // 0-15 q, 16-23 k, 24-31 v
+  const int lane = threadIdx.x & 31;
+  const int pos = pos0 + i;
+  const float* src = qkv + (size_t)i * kQKVRows + head * kHeadDim;  // q 0..2047, k 2048.., v 3072..
+  const int d0 = 2 * lane;
+  float x0 = src[d0], x1 = src[d0 + 1], x2 = src[d0 + 64], x3 = src[d0 + 65];
+  if (head < 24) {
+    const __nv_bfloat16* nw = head < 16 ? qn : kn;
+    const float ss = warp_sum(x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3);
+    const float rstd = rsqrtf(ss * (1.0f / kHeadDim) + kEps);
+    const float y0 = x0 * rstd * __bfloat162float(nw[d0]), y1 = x1 * rstd * __bfloat162float(nw[d0 + 1]);
+    const float y2 = x2 * rstd * __bfloat162float(nw[d0 + 64]), y3 = x3 * rstd * __bfloat162float(nw[d0 + 65]);
+    const size_t rb = (size_t)pos * kHeadDim;
+    const float c0 = rope_val(cos_t, fp32, rb + d0), s0 = rope_val(sin_t, fp32, rb + d0);
+    const float c1 = rope_val(cos_t, fp32, rb + d0 + 1), s1 = rope_val(sin_t, fp32, rb + d0 + 1);
+    x0 = y0 * c0 - y2 * s0;
+    x2 = y2 * c0 + y0 * s0;
+    x1 = y1 * c1 - y3 * s1;
+    x3 = y3 * c1 + y1 * s1;
+  }
+  if (head < 16) {
+    const float sc = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
+    float* q = q_out + (size_t)i * kQSize + head * kHeadDim;
+    q[d0] = x0 * sc;
+    q[d0 + 1] = x1 * sc;
+    q[d0 + 64] = x2 * sc;
+    q[d0 + 65] = x3 * sc;
+  } else {
+    const int h = (head - 16) & 7;
+    __nv_bfloat16* dst = (head < 24 ? kc : vc) + (((size_t)layer * kNKV + h) * max_seq + pos) * kHeadDim;
+    *reinterpret_cast<__nv_bfloat162*>(dst + d0) = __floats2bfloat162_rn(x0, x1);
+    *reinterpret_cast<__nv_bfloat162*>(dst + d0 + 64) = __floats2bfloat162_rn(x2, x3);
+  }
+}
+
+// Causal attention over the cache for query tokens [64 blockIdx.x, +64) of Q
+// head blockIdx.y; 4 warps x 16 query rows. Query token i sits at position
+// pos0 + i and attends to keys [0, pos0 + i]. S = Q K^T and O = P V on
+// mma.sync m16n8k16 (BF16 in, FP32 out) with Q and P split into high part +
+// remainder; K/V tiles of 64 keys in padded shared rows (conflict-free ldmatrix).
+constexpr int kAttRow = kHeadDim + 8;  // 136 BF16 = 272 bytes per shared K/V row
+__global__ void __launch_bounds__(128) attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
+                                                   const __nv_bfloat16* __restrict__ vc, int n, int pos0, int layer,
+                                                   int max_seq, __nv_bfloat16* oh, __nv_bfloat16* ol) {
+  __shared__ __align__(16) __nv_bfloat16 ks[64][kAttRow];
+  __shared__ __align__(16) __nv_bfloat16 vs[64][kAttRow];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hq = blockIdx.y, hk = hq >> 1;
+  const int i0 = blockIdx.x * 64;
+  const int g = lane >> 2, tq = lane & 3;
+  const int r0 = i0 + warp * 16 + g, r1 = r0 + 8;  // this thread's two query rows (tokens)
+  // Q fragments (A operand), high part and remainder, for the 8 k-steps of 16 dims
+  uint32_t qa_h[8][4], qa_l[8][4];
+  {
+    const float* qr0 = q + (size_t)min(r0, n - 1) * kQSize + hq * kHeadDim;
+    const float* qr1 = q + (size_t)min(r1, n - 1) * kQSize + hq * kHeadDim;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      const int c = 16 * s + 2 * tq;
+      const float a[8] = {qr0[c], qr0[c + 1], qr1[c], qr1[c + 1], qr0[c + 8], qr0[c + 9], qr1[c + 8], qr1[c + 9]};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t h = pack_bf2(a[2 * k], a[2 * k + 1]);
+        qa_h[s][k] = h;
+        qa_l[s][k] = pack_bf2(a[2 * k] - bf_lo(h), a[2 * k + 1] - bf_hi(h));
+      }
+    }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0r = -INFINITY, m1r = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const int last_key = pos0 + min(i0 + 63, n - 1);  // the block's last query attends up to here
+  const size_t head_base = ((size_t)layer * kNKV + hk) * max_seq;
+  for (int k0 = 0; k0 <= last_key; k0 += 64) {
+    __syncthreads();
+    // K and V rows k0 .. k0 + 63 (rows past the last key are loaded from the
+    // cache as they are and masked below)
+    for (int e = threadIdx.x; e < 64 * 16; e += 128) {
+      const int r = e >> 4, cidx = (e & 15) * 8;
+      const int key = min(k0 + r, max_seq - 1);
+      *reinterpret_cast<uint4*>(&ks[r][cidx]) = *reinterpret_cast<const uint4*>(kc + (head_base + key) * kHeadDim + cidx);
+      *reinterpret_cast<uint4*>(&vs[r][cidx]) = *reinterpret_cast<const uint4*>(vc + (head_base + key) * kHeadDim + cidx);
+    }
+    __syncthreads();
+    // S = Q K^T for 8 n-tiles of 8 keys
+    float sacc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < 4; ++s2) {  // two k-steps per ldmatrix.x4
+        uint32_t b0, b1, b2, b3;
+        const int key = 8 * j + (lane & 7), dim = 32 * s2 + 8 * (lane >> 3);
+        ldsm_x4(smem_addr(&ks[key][dim]), b0, b1, b2, b3);
+        mma_bf16(sacc[j], qa_h[2 * s2][0], qa_h[2 * s2][1], qa_h[2 * s2][2], qa_h[2 * s2][3], b0, b1);
+        mma_bf16(sacc[j], qa_l[2 * s2][0], qa_l[2 * s2][1], qa_l[2 * s2][2], qa_l[2 * s2][3], b0, b1);
+        mma_bf16(sacc[j], qa_h[2 * s2 + 1][0], qa_h[2 * s2 + 1][1], qa_h[2 * s2 + 1][2], qa_h[2 * s2 + 1][3], b2, b3);
+        mma_bf16(sacc[j], qa_l[2 * s2 + 1][0], qa_l[2 * s2 + 1][1], qa_l[2 * s2 + 1][2], qa_l[2 * s2 + 1][3], b2, b3);
+      }
+    }
+    // causal mask and online softmax (rows r0, r1)
+    const int lim0 = pos0 + r0, lim1 = pos0 + r1;
+    float mx0 = m0r, mx1 = m1r;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int kk = k0 + 8 * j + 2 * tq;
+      if (kk > lim0) sacc[j][0] = -INFINITY;
+      if (kk + 1 > lim0) sacc[j][1] = -INFINITY;
+      if (kk > lim1) sacc[j][2] = -INFINITY;
+      if (kk + 1 > lim1) sacc[j][3] = -INFINITY;
+      mx0 = fmaxf(mx0, fmaxf(sacc[j][0], sacc[j][1]));
+      mx1 = fmaxf(mx1, fmaxf(sacc[j][2], sacc[j][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float sc0 = mx0 > -INFINITY ? ex2_approx(m0r - mx0) : 1.f;
+    const float sc1 = mx1 > -INFINITY ? ex2_approx(m1r - mx1) : 1.f;
+    m0r = mx0;
+    m1r = mx1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sacc[j][0] = sacc[j][0] > -INFINITY ? ex2_approx(sacc[j][0] - mx0) : 0.f;
+      sacc[j][1] = sacc[j][1] > -INFINITY ? ex2_approx(sacc[j][1] - mx0) : 0.f;
+      sacc[j][2] = sacc[j][2] > -INFINITY ? ex2_approx(sacc[j][2] - mx1) : 0.f;
+      sacc[j][3] = sacc[j][3] > -INFINITY ? ex2_approx(sacc[j][3] - mx1) : 0.f;
+      ps0 += sacc[j][0] + sacc[j][1];
+      ps1 += sacc[j][2] + sacc[j][3];
+    }
+    ps0 += __shfl_xor_sync(0xffffffffu, ps0, 1);
+    ps0 += __shfl_xor_sync(0xffffffffu, ps0, 2);
+    ps1 += __shfl_xor_sync(0xffffffffu, ps1, 1);
+    ps1 += __shfl_xor_sync(0xffffffffu, ps1, 2);
+    l0 = l0 * sc0 + ps0;
+    l1 = l1 * sc1 + ps1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= sc0; o[j][1] *= sc0;
+      o[j][2] *= sc1; o[j][3] *= sc1;
+    }
+    // O += P V: the S accumulators of n-tiles 2s, 2s+1 are the A fragment of
+    // k-step s (16 keys); V^T fragments by ldmatrix.trans from the key rows
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      const float* pa = sacc[2 * s];
+      const float* pb = sacc[2 * s + 1];
+      const float pv[8] = {pa[0], pa[1], pa[2], pa[3], pb[0], pb[1], pb[2], pb[3]};
+      uint32_t ah[4], al[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t h = pack_bf2(pv[2 * k], pv[2 * k + 1]);
+        ah[k] = h;
+        al[k] = pack_bf2(pv[2 * k] - bf_lo(h), pv[2 * k + 1] - bf_hi(h));
+      }
+#pragma unroll
+      for (int j2 = 0; j2 < 8; ++j2) {  // two n-tiles of 8 dims per ldmatrix.x4.trans
+        uint32_t b0, b1, b2, b3;
+        const int key = 16 * s + (lane & 7) + 8 * ((lane >> 3) & 1), dim = 16 * j2 + 8 * (lane >> 4);
+        ldsm_x4_trans(smem_addr(&vs[key][dim]), b0, b1, b2, b3);
+        mma_bf16(o[2 * j2], ah[0], ah[1], ah[2], ah[3], b0, b1);
+        mma_bf16(o[2 * j2], al[0], al[1], al[2], al[3], b0, b1);
+        mma_bf16(o[2 * j2 + 1], ah[0], ah[1], ah[2], ah[3], b2, b3);
+        mma_bf16(o[2 * j2 + 1], al[0], al[1], al[2], al[3], b2, b3);
+      }
+    }
+  }
+  // O / l -> high part and remainder of the o_proj A operand
+  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int c = hq * kHeadDim + 8 * j + 2 * tq;
+    if (r0 < n) {
+      const float a = o[j][0] * inv0, b = o[j][1] * inv0;
+      const uint32_t h = pack_bf2(a, b);
+      *reinterpret_cast<uint32_t*>(oh + (size_t)r0 * kQSize + c) = h;
+      *reinterpret_cast<uint32_t*>(ol + (size_t)r0 * kQSize + c) = pack_bf2(a - bf_lo(h), b - bf_hi(h));
+    }
+    if (r1 < n) {
+      const float a = o[j][2] * inv1, b = o[j][3] * inv1;
+      const uint32_t h = pack_bf2(a, b);
+      *reinterpret_cast<uint32_t*>(oh + (size_t)r1 * kQSize + c) = h;
+      *reinterpret_cast<uint32_t*>(ol + (size_t)r1 * kQSize + c) = pack_bf2(a - bf_lo(h), b - bf_hi(h));
+    }
+  }
+}
+
+// ---- host side ---------------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  }
+  return fn;
+}
+
+// Row-major BF16 [rows, cols] as a 2-D tensor map with 64 x box_rows boxes and
+// 128-byte swizzle (the K-major operand layout of the GEMM). Rows past the end
+// read as zeros.
+cudaError_t map_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiled enc = encoder();
+  if (!enc) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (cols * 2) % 16 || cols % BK) return cudaErrorMisalignedAddress;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int kMode>
+cudaError_t gemm_launch(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& b, const CUtensorMap& b2,
+                        const GemmArgs& g, cudaStream_t stream) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(gemm_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  if (g.K % BK || g.N % BN || g.M < 1) return cudaErrorInvalidValue;
+  dim3 grid(g.N / BN, (g.M + BM - 1) / BM);
+  gemm_kernel<kMode><<<grid, kGemmThreads, kGemmSmem, stream>>>(ah, al, b, b2, g);
+  return cudaGetLastError();
+}
+
+}  // namespace pf
+
+// Prefill of n prompt tokens at positions pos0 .. pos0 + n - 1 for layers
+// [0, n_layers): called by the engine (mkb_host.cu) with its scratch buffers.
+cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const __nv_bfloat16* embed,
+                           const void* cos_t, const void* sin_t, int rope_fp32, __nv_bfloat16* kc, __nv_bfloat16* vc,
+                           int max_seq, const int* ids, int n, int pos0, const PrefillScratch& s, cudaStream_t stream) {
+  using namespace pf;
+  if (n < 1 || n > s.cap || pos0 < 0 || pos0 + n > max_seq) return cudaErrorInvalidValue;
+  cudaError_t e;
+  embed_kernel<<<n, kHidden / 4, 0, stream>>>(ids, embed, s.h);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  // activation operand maps over the scratch (K = 1024, 2048 or 3072 columns)
+  CUtensorMap a1h, a1l, a2h, a2l, a3h, a3l;
+  if ((e = map_2d(&a1h, s.ah, n, kHidden, BM)) != cudaSuccess) return e;
+  if ((e = map_2d(&a1l, s.al, n, kHidden, BM)) != cudaSuccess) return e;
+  if ((e = map_2d(&a2h, s.ah, n, kQSize, BM)) != cudaSuccess) return e;
+  if ((e = map_2d(&a2l, s.al, n, kQSize, BM)) != cudaSuccess) return e;
+  if ((e = map_2d(&a3h, s.mh, n, kInter, BM)) != cudaSuccess) return e;
+  if ((e = map_2d(&a3l, s.ml, n, kInter, BM)) != cudaSuccess) return e;
+  GemmArgs g = {};
+  g.M = n;
+  g.timeout_ns = 1000000000ull;
+  g.err = s.err;
+  for (int l = 0; l < n_layers; ++l) {
+    const LayerWeights& w = host_layers[l];
+    CUtensorMap bq, bk, bv, bo, bg, bu, bd;
+    if ((e = map_2d(&bq, w.q_weight, kQSize, kHidden, BN)) != cudaSuccess) return e;
+    if ((e = map_2d(&bk, w.k_weight, kKVSize, kHidden, BN)) != cudaSuccess) return e;
+    if ((e = map_2d(&bv, w.v_weight, kKVSize, kHidden, BN)) != cudaSuccess) return e;
+    if ((e = map_2d(&bo, w.o_proj_weight, kHidden, kQSize, BN)) != cudaSuccess) return e;
+    if ((e = map_2d(&bg, w.gate_proj_weight, kInter, kHidden, BN / 2)) != cudaSuccess) return e;
+    if ((e = map_2d(&bu, w.up_proj_weight, kInter, kHidden, BN / 2)) != cudaSuccess) return e;
+    if ((e = map_2d(&bd, w.down_proj_weight, kHidden, kInter, BN)) != cudaSuccess) return e;
+    // input RMSNorm -> QKV (three GEMMs into the [n, 4096] buffer)
+    rmsnorm_split_kernel<<<n, kHidden / 4, 0, stream>>>(s.h, w.norm_weight, s.ah, s.al);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    g.K = kHidden;
+    g.ldc = kQKVRows;
+    g.N = kQSize;
+    g.c = s.qkv;
+    if ((e = gemm_launch<kEpiStore>(a1h, a1l, bq, bq, g, stream)) != cudaSuccess) return e;
+    g.N = kKVSize;
+    g.c = s.qkv + kQSize;
+    if ((e = gemm_launch<kEpiStore>(a1h, a1l, bk, bk, g, stream)) != cudaSuccess) return e;
+    g.c = s.qkv + kQSize + kKVSize;
+    if ((e = gemm_launch<kEpiStore>(a1h, a1l, bv, bv, g, stream)) != cudaSuccess) return e;
+    // q/k norm + RoPE, K/V rows into the cache, then causal attention
+    qk_rope_kernel<<<dim3(n, 4), 256, 0, stream>>>(s.qkv, w.q_norm_weight, w.k_norm_weight, cos_t, sin_t, rope_fp32,
+                                                   pos0, l, kc, vc, max_seq, s.q);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    attn_kernel<<<dim3((n + 63) / 64, kNQ), 128, 0, stream>>>(s.q, kc, vc, n, pos0, l, max_seq, s.ah, s.al);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // o_proj added into the residual
+    g.K = kQSize;
+    g.N = kHidden;
+    g.ldc = kHidden;
+    g.c = s.h;
+    if ((e = gemm_launch<kEpiAdd>(a2h, a2l, bo, bo, g, stream)) != cudaSuccess) return e;
+    // post-attention RMSNorm -> gate/up with SwiGLU -> down added into the residual
+    rmsnorm_split_kernel<<<n, kHidden / 4, 0, stream>>>(s.h, w.post_attn_norm_weight, s.ah, s.al);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    g.K = kHidden;
+    g.N = 2 * kInter;  // 128-column tiles = 64 gate + 64 up columns
+    g.m_hi = s.mh;  // a separate buffer: the GEMM still reads s.ah / s.al
+    g.m_lo = s.ml;
+    g.ldm = kInter;
+    if ((e = gemm_launch<kEpiSwiGLU>(a1h, a1l, bg, bu, g, stream)) != cudaSuccess) return e;
+    g.K = kInter;
+    g.N = kHidden;
+    g.c = s.h;
+    g.ldc = kHidden;
+    if ((e = gemm_launch<kEpiAdd>(a3h, a3l, bd, bd, g, stream)) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// C[M, N] = (A_hi + A_lo) B^T through the prefill GEMM (test entry point).
+cudaError_t gemm_split(const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, const __nv_bfloat16* b, float* c, int M,
+                       int N, int K, uint32_t* err, cudaStream_t stream) {
+  using namespace pf;
+  CUtensorMap ah, al, bm;
+  cudaError_t e;
+  if ((e = map_2d(&ah, a_hi, M, K, BM)) != cudaSuccess) return e;
+  if ((e = map_2d(&al, a_lo, M, K, BM)) != cudaSuccess) return e;
+  if ((e = map_2d(&bm, b, N, K, BN)) != cudaSuccess) return e;
+  GemmArgs g = {};
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.c = c;
+  g.ldc = N;
+  g.timeout_ns = 1000000000ull;
+  g.err = err;
+  return gemm_launch<kEpiStore>(ah, al, bm, bm, g, stream);
+}
+
+}  // namespace mkb

@@ -120,6 +120,31 @@ __device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// ---- system-scope forms (tensor parallel: words other GPUs add into) ----------
+__device__ __forceinline__ void red_add_u64_sys(uint64_t* p, uint64_t v) {
+  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void red_max_u64_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.sys.global.max.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Orders every earlier write of this thread (to any GPU) before the add.
+__device__ __forceinline__ void red_release_add_sys(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ld_relaxed_u64_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void ld_relaxed2_sys(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 // Tagged 8-byte words: (tag << 32) | float bits, written and read as single
 // 64-bit accesses, so a reader that sees the expected tag also sees its value.
 __device__ __forceinline__ void st_tagged(uint64_t* p, float v, uint32_t tag) {
@@ -207,6 +232,12 @@ __device__ __forceinline__ uint32_t lds32(uint32_t a) {
 // Four 8x8 bf16 matrices; lane i supplies the shared address of one 16-byte row.
 __device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a));
+}
+// The same with each 8x8 matrix transposed on the way (B operands from row-major rows).
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(a));
 }

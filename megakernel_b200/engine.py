@@ -47,8 +47,9 @@ def check_tensor(t: torch.Tensor, name: str, shape=None, dtype=torch.bfloat16, d
         _require(t.device == device, f"{name} must be on {device}")
 
 
-def check_model(embed, final_norm, layer_weights, k_cache, v_cache, lm_head=None):
-    """Validation shared by every entry point (the reference checks nothing)."""
+def check_model(embed, final_norm, layer_weights, k_cache, v_cache, lm_head=None, tp_size: int = 1):
+    """Validation shared by every entry point (the reference checks nothing).
+    With tensor parallelism the caches are the rank's shard of 8 / tp_size KV heads."""
     check_tensor(embed, "embed_weight", (VOCAB, HIDDEN))
     dev = embed.device
     check_tensor(final_norm, "final_norm_weight", (HIDDEN,), device=dev)
@@ -59,8 +60,10 @@ def check_model(embed, final_norm, layer_weights, k_cache, v_cache, lm_head=None
     for i, t in enumerate(layer_weights):
         check_tensor(t, f"layer_weights[{i}]", LAYER_SHAPES[i % 11], device=dev)
     n_layers = len(layer_weights) // 11
-    _require(k_cache.dim() == 4 and k_cache.shape[0] == n_layers and k_cache.shape[1] == N_KV
-             and k_cache.shape[3] == HEAD_DIM, "k_cache must be [layers, 8, max_seq, 128]")
+    _require(tp_size in (1, 2, 4, 8), "tp_size must be 1, 2, 4 or 8")
+    heads = N_KV // tp_size
+    _require(k_cache.dim() == 4 and k_cache.shape[0] == n_layers and k_cache.shape[1] == heads
+             and k_cache.shape[3] == HEAD_DIM, f"k_cache must be [layers, {heads}, max_seq, 128]")
     check_tensor(k_cache, "k_cache", device=dev)
     check_tensor(v_cache, "v_cache", tuple(k_cache.shape), device=dev)
     return n_layers, int(k_cache.shape[2])
@@ -75,9 +78,11 @@ class DecodeEngine:
     """Resident batch-one decode engine over the reference's tensors."""
 
     def __init__(self, embed, final_norm, layer_weights, k_cache, v_cache, cos=None, sin=None,
-                 lm_head=None, fused_down: bool = True, use_graph: bool = True):
+                 lm_head=None, fused_down: bool = True, use_graph: bool = True, tp_size: int = 1):
         self.lib = _lib.load()
-        self.n_layers, self.max_seq = check_model(embed, final_norm, layer_weights, k_cache, v_cache, lm_head)
+        self.n_layers, self.max_seq = check_model(embed, final_norm, layer_weights, k_cache, v_cache, lm_head,
+                                                  tp_size)
+        self.tp_size = tp_size
         dev = embed.device
         if cos is None:
             cos, sin = rope_tables(self.max_seq, dev, torch.float32)
@@ -109,6 +114,7 @@ class DecodeEngine:
         m.fused_down = 1 if fused_down else 0
         m.use_graph = 1 if use_graph else 0
         m.logits = self.logits.data_ptr()
+        m.tp_size = tp_size
         h = c_void_p()
         with torch.cuda.device(dev):
             torch.cuda.synchronize()
@@ -150,11 +156,14 @@ class DecodeEngine:
         _lib.check(code, "mkb_engine_generate")
         return out
 
-    def prefill(self, ids, position: int = 0, stream=None) -> int:
-        """In-engine prefill of prompt ``ids`` at ``position``.. (one persistent launch
-        appends their K/V rows; model.py:72-87 did this with HF). Returns the argmax
-        of the last prompt token, the first generated token; ``logits`` holds its
-        logits."""
+    def prefill(self, ids, position: int = 0, stream=None, batched: bool = False) -> int:
+        """In-engine prefill of prompt ``ids`` at ``position``.. (model.py:72-87 did this
+        with HF). ``batched=False``: one persistent launch of the decode kernel feeds
+        the prompt token by token. ``batched=True``: every prompt token of a layer at
+        once -- tcgen05 tensor-core GEMMs for the projections, causal attention on
+        the tensor cores (mkb_engine_prefill_batched). Either way the K/V rows are
+        appended and the return value is the argmax of the last prompt token, the
+        first generated token; ``logits`` holds its logits."""
         ids = torch.as_tensor(ids, dtype=torch.int32).flatten()
         n = int(ids.numel())
         _require(n >= 1 and 0 <= position and position + n <= self.max_seq, "prefill range out of bounds")
@@ -162,8 +171,9 @@ class DecodeEngine:
         dev_ids = ids.to(self.device)
         nxt = torch.empty(1, dtype=torch.int32, device=self.device)
         with torch.cuda.device(self.device):
-            code = self.lib.mkb_engine_prefill(self._h, c_void_p(dev_ids.data_ptr()), n, int(position),
-                                               c_void_p(nxt.data_ptr()), c_void_p(_stream_ptr(stream)))
+            fn = self.lib.mkb_engine_prefill_batched if batched else self.lib.mkb_engine_prefill
+            code = fn(self._h, c_void_p(dev_ids.data_ptr()), n, int(position), c_void_p(nxt.data_ptr()),
+                      c_void_p(_stream_ptr(stream)))
         _lib.check(code, "mkb_engine_prefill")
         out = int(nxt.item())
         st = self.status()
@@ -173,6 +183,23 @@ class DecodeEngine:
 
     def status(self) -> list:
         return _lib.workspace_status(self.workspace_ptr)
+
+    def ipc_handle(self) -> bytes:
+        """64 bytes that let another process on this node map this engine's workspace."""
+        buf = ctypes.create_string_buffer(64)
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.mkb_ipc_export(c_void_p(self.workspace_ptr), buf), "mkb_ipc_export")
+        return buf.raw
+
+    def attach_tp(self, tp_rank: int, tp_size: int, peer_workspaces: list):
+        """Join a tensor-parallel group (see mkb_engine_tp_attach); peer_workspaces are
+        device addresses valid on this GPU, this engine's own at index tp_rank."""
+        _require(tp_size == self.tp_size, "tp_size differs from the one the engine was built for")
+        arr = (c_void_p * tp_size)(*peer_workspaces)
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.mkb_engine_tp_attach(self._h, int(tp_rank), int(tp_size), arr),
+                       "mkb_engine_tp_attach")
+        self.tp_rank = tp_rank
 
     def close(self):
         if getattr(self, "_h", None):

@@ -171,6 +171,7 @@ def test_decode_args_mirror_matches_the_header():
             continue
         head, _, rest = decl.rpartition(" ")
         # "int layer_begin, layer_end" declares several fields
+        decl = re.sub(r"\[\d+\]$", "", decl)  # arrays: "void* peer_workspaces[8]"
         first = decl.split(",")
         names.append(re.findall(r"\**(\w+)$", first[0].strip())[0])
         names += [re.sub(r"^\*+", "", x.strip()) for x in first[1:]]
