@@ -547,6 +547,31 @@ def test_long_cache_config3_all_256_steps(w_gpu, config3_hf):
     eng.close()
 
 
+def test_config3_batched_prefill(w_gpu, config3_hf):
+    """The 3584-token config-3 prompt through the batched tensor-core prefill:
+    last-token logits and greedy id against HF's prefill, the appended K/V rows,
+    and the first decode steps from that cache against HF's."""
+    ids, logits_hf, k, v, fed, steps = config3_hf
+    kg = torch.zeros((28, 8, 4096, 128), dtype=torch.bfloat16, device=DEV)
+    vg = torch.zeros_like(kg)
+    eng = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), kg, vg)
+    nxt = eng.prefill(ids.view(-1), batched=True)
+    lg = eng.logits.cpu()
+    assert (lg - logits_hf).abs().max().item() <= 2e-2
+    assert cosine(lg, logits_hf) > 0.999
+    t2 = torch.topk(logits_hf.double(), 2).values
+    if float(t2[0] - t2[1]) > 0.05:
+        assert nxt == int(torch.argmax(logits_hf))
+    n = ids.numel()
+    for got, ref in ((kg[:, :, :n], k[:, :, :n]), (vg[:, :, :n], v[:, :, :n])):
+        torch.testing.assert_close(got.float().cpu(), ref.float(), rtol=2e-2, atol=2e-2)
+    for i in range(4):
+        eng.step(fed[i], n + i)
+        assert (eng.logits.cpu() - steps[i]).abs().max().item() <= 2e-2, f"step {i}"
+    assert eng.status()[0] == 0
+    eng.close()
+
+
 def test_config3_in_engine_prefill(w_gpu, config3_hf):
     """The 3584-token prompt prefilled in one persistent launch (no HF): the last
     prompt token's logits and greedy id against HF's prefill, and the appended
