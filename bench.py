@@ -684,7 +684,22 @@ def tensor_parallel_run(rank, world, dev, embed, final_norm, layers, steps, warm
     except Exception as e:  # reported, never fatal for the replica measurement above
         ok = 0.0
         res = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
-    flags = max_over_ranks([1.0 - ok, res.get("device_ms_local", 0.0)], world, dev)
+    # the collective an NCCL form of the same split would need: an all_reduce of
+    # the 4 KB hidden state, twice per layer (56 per token)
+    ar_ms = 0.0
+    try:
+        x = torch.ones(1024, dtype=torch.float32, device=dev)
+        for _ in range(10):
+            dist.all_reduce(x)
+        torch.cuda.synchronize()
+        ar_ms, _, _ = timed_region(local, lambda: [dist.all_reduce(x) for _ in range(200)])
+        ar_ms /= 200
+    except Exception:
+        ar_ms = 0.0
+    flags = max_over_ranks([1.0 - ok, res.get("device_ms_local", 0.0), ar_ms], world, dev)
+    res["nccl_allreduce_4kb_us"] = flags[2] * 1000.0 if flags[2] > 0 else None
+    if flags[2] > 0:
+        res["nccl_allreduce_per_token_us"] = flags[2] * 1000.0 * 2 * LAYERS
     if flags[0] > 0:
         res = res if "unavailable" in res else {"unavailable": "failed on another rank"}
     else:
