@@ -67,6 +67,8 @@ def args_parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", type=int, choices=[0, 2, 3], default=0)
     ap.add_argument("--prefill", action="store_true", help="time the batched prefill (32 and 3584 tokens)")
+    ap.add_argument("--prefill-once", type=int, default=0, metavar="N",
+                    help="two batched prefills of N tokens and nothing else (for a profiler's launch list)")
     return ap.parse_args()
 
 
@@ -377,6 +379,21 @@ def prefill_flops(n: int, pos0: int = 0) -> float:
     return 2.0 * LINEAR_PARAMS * n + LAYERS * 16 * 512.0 * keys + 2.0 * 311_164_928 / 2
 
 
+def prefill_once(n: int, local: int):
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import megakernel_b200 as mk
+    embed, final_norm, layers = synthetic_weights(1000, dev)
+    k = torch.zeros((LAYERS, 8, 4096, 128), dtype=torch.bfloat16, device=dev)
+    v = torch.zeros_like(k)
+    eng = mk.DecodeEngine(embed, final_norm, layers, k, v)
+    ids = torch.randint(0, VOCAB, (n,), generator=torch.Generator().manual_seed(1))
+    for _ in range(2):
+        eng.prefill(ids, batched=True)
+    torch.cuda.synchronize()
+    eng.close()
+
+
 def run_prefill(a, rank, world, local):
     """Batched prefill (tcgen05 GEMMs, tensor-core attention) of a 32- and a
     3584-token prompt, against the token-by-token in-engine prefill."""
@@ -511,7 +528,11 @@ def reference_kernel_on_gpu(a):
         return None
     try:
         from oracle import ref_kernel
-        return ref_kernel.time_reference(steps=min(a.steps, 64), warmup=a.warmup)
+        out = ref_kernel.time_reference(steps=min(a.steps, 64), warmup=a.warmup)
+        # the same kernel without its binding's per-call allocation: table and
+        # scratch resident, events around the launch only
+        out["resident"] = ref_kernel.time_reference_resident(steps=min(a.steps, 64), warmup=a.warmup)
+        return out
     except Exception as e:  # the reference kernel is optional context, never the product
         return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
 
@@ -521,6 +542,9 @@ def main():
     rank, world, local = dist_env()
     if a.impl == "reference":
         run_reference(a, rank, world)
+        return
+    if a.prefill_once:
+        prefill_once(a.prefill_once, local)
         return
     if a.prefill:
         run_prefill(a, rank, world, local)
