@@ -965,6 +965,10 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   const bool tpx = tp.size > 1;
   const int lb = p.layer_begin, le = p.layer_end;
   const int zero_cta = G - 1;
+  // With 1 + kDownCopies CTAs outside the head groups (148 SMs: 4), those CTAs,
+  // idle during attention, clear the layer l-2 accumulators there; otherwise
+  // the last CTA clears them before its QKV rows (which then publish late).
+  const bool spare_clear = !(tp.size > 1) && G - tp.hl * p.group_size >= 1 + kDownCopies;
   // contributions that land in copy 0 of a down row: clusters k with k % kDownCopies == 0
   const int down_copy0 = (G / kCluster + kDownCopies - 1) / kDownCopies;
   uint32_t n = 0;
@@ -1063,7 +1067,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         }
         // Every CTA has finished layer l-1 (and so read the accumulators of
         // layer l-2): clear those for the next token.
-        if (c.cta == zero_cta && l >= lb + 2) {
+        if (!spare_clear && c.cta == zero_cta && l >= lb + 2) {
           acc_clear4(&ws->acc_mid[l - 2][0]);
 #pragma unroll
           for (int q = 0; q < kDownCopies; ++q) acc_clear4(&ws->acc_down[l - 2][q][0]);
@@ -1475,6 +1479,13 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           __syncwarp();
           if (lane == 0) release_add(&ws->kv_ready[l][h][0], 1u);
         }
+      }
+      if (!pl.in_bc && spare_clear && l >= lb + 2) {
+        // every CTA has read the layer l-2 sums (it has passed layer l-1's first
+        // exchange, which this CTA waited for): each spare CTA clears one row
+        const int sp = c.cta - tp.hl * p.group_size;
+        if (sp == 0) acc_clear4(&ws->acc_mid[l - 2][0]);
+        if (sp >= 1 && sp <= kDownCopies) acc_clear4(&ws->acc_down[l - 2][sp - 1][0]);
       }
 
       // ================= DE: post norm, SwiGLU rows, down partial ===============

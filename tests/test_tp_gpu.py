@@ -1,4 +1,4 @@
-"""Tensor-parallel decode on 2 GPUs (one process per GPU, gloo for the set-up's
+"""Tensor-parallel decode on 2, 4 or 8 GPUs (one process per GPU, gloo for the set-up's
 handle exchange) against the single-GPU engine on the same weights and prompt.
 
 Each rank checks its own vocabulary rows of the logits, its KV-cache shard, and
@@ -9,7 +9,7 @@ so the bound is not bit equality: logits within 1e-2 (half the HF parity bound;
 few BF16 ulp in the deep layers, 7.8e-3 measured),
 tokens equal wherever the top-2 margin exceeds 1e-3. Each rank also checks its
 rows of the logits against HF's FP32 golden logits of config 0 (2e-2) on the
-teacher-forced steps. Skipped with fewer than 2 GPUs.
+teacher-forced steps. Each size is skipped when the box has fewer GPUs.
 """
 import os
 import socket
@@ -20,7 +20,6 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-TP = 2
 MAX_SEQ = 128
 
 
@@ -106,8 +105,9 @@ def _worker(rank, world, port):
         dist.destroy_process_group()
 
 
-def test_tensor_parallel_matches_single_gpu():
-    if not torch.cuda.is_available() or torch.cuda.device_count() < TP:
-        pytest.skip(f"needs {TP} GPUs")
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_tensor_parallel_matches_single_gpu(tp):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < tp:
+        pytest.skip(f"needs {tp} GPUs")
     import torch.multiprocessing as mp
-    mp.spawn(_worker, args=(TP, _free_port()), nprocs=TP, join=True)
+    mp.spawn(_worker, args=(tp, _free_port()), nprocs=tp, join=True)
