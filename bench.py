@@ -94,6 +94,59 @@ def replica_throughput(world: int, steps: int, ms: float) -> float:
     return world * steps / (ms / 1000.0)
 
 
+def end_to_end(eng, first: int, pos0: int, steps: int, warm: int, span: int):
+    """Host wall-clock seconds for `steps` greedy tokens through the two public
+    per-token surfaces, from token `first` at position `pos0`:
+
+    - a serve session (mkb_engine_serve_open / _step / _close): one persistent
+      launch; per token the host writes {seq, token} (8 B) into pinned mapped
+      memory and reads {seq, argmax} (8 B) back; open and close are timed;
+    - mkb_engine_step: 8 B copied in, one graph replay, the kernel stores the
+      4 B argmax into pinned host memory.
+
+    A session covers at most `span` positions; longer runs are timed over
+    `span` tokens and scaled. Returns (serve_s, step_s)."""
+    n_serve = min(steps, span)
+    eng.serve_open(pos0, warm)
+    t = first
+    for _ in range(warm):
+        t = eng.serve_step(t)
+    eng.serve_close()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    eng.serve_open(pos0, n_serve)
+    t = first
+    for _ in range(n_serve):
+        t = eng.serve_step(t)
+    eng.serve_close()
+    serve_s = (time.perf_counter() - t0) * steps / n_serve
+    assert eng.status()[0] == 0, f"in-kernel error {eng.status()}"
+    for i in range(warm):
+        eng.step(first, pos0 + i)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    t = first
+    for i in range(steps):
+        t = eng.step(t, pos0 + (i % span))
+    torch.cuda.synchronize()
+    return serve_s, time.perf_counter() - t0
+
+
+def e2e_fields(world: int, steps: int, serve_ms: float, step_ms: float) -> dict:
+    """The bench line's `e2e` object: the serve session as the headline, the
+    per-call mkb_engine_step beside it."""
+    return {"value": replica_throughput(world, steps, serve_ms), "unit": "tok/s", "h2d_bytes_per_step": 8,
+            "d2h_bytes_per_step": 8, "us_per_token": serve_ms * 1000.0 / steps,
+            "api": "serve session (mkb_engine_serve_open / _step / _close): one persistent launch; per step the "
+                   "host writes {seq, token} (8 B) into pinned mapped memory and reads {seq, argmax} (8 B) back; "
+                   "open and close inside the timed region",
+            "per_call_step": {"value": replica_throughput(world, steps, step_ms), "unit": "tok/s",
+                              "us_per_token": step_ms * 1000.0 / steps, "h2d_bytes_per_step": 8,
+                              "d2h_bytes_per_step": 4,
+                              "api": "mkb_engine_step (8 B copied in from pinned memory, graph replay, the "
+                                     "kernel stores the 4 B argmax into pinned host memory)"}}
+
+
 def synthetic_weights(seed: int, device):
     """Random-init Qwen3-0.6B weights generated on the device (N(0, 0.02), norms 1)."""
     g = torch.Generator(device=device).manual_seed(seed)
@@ -480,15 +533,8 @@ def run_config3(a, rank, world, local):
     eng.generate(first, prompt_len, warm, out=out[:warm])
     dev_ms, clocks, _ = timed_region(local, lambda: eng.generate(first, prompt_len, steps, out=out))
     assert eng.status()[0] == 0
-    for i in range(warm):
-        eng.step(first, prompt_len + i)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    t = first
-    for i in range(steps):
-        t = eng.step(t, prompt_len + i)
-    e2e_s = time.perf_counter() - t0
-    dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_s * 1000.0], world, dev)
+    serve_s, step_s = end_to_end(eng, first, prompt_len, steps, warm, max_seq - prompt_len)
+    dev_ms, serve_ms, step_ms = max_over_ranks([dev_ms, serve_s * 1000.0, step_s * 1000.0], world, dev)
     alg = sum(WEIGHT_BYTES + KV_BYTES_PER_POS * (prompt_len + i + 1) for i in range(steps))
     achieved = alg / (dev_ms / 1000.0) / 1e9
     peak, peak_kind = measured_peak()
@@ -507,10 +553,7 @@ def run_config3(a, rank, world, local):
                        "l2": "inputs larger than L2: 1.6 GB streamed per token vs 126 MB L2",
                        "us_per_token": dev_ms * 1000.0 / steps, "batched_prefill_s_3584_tokens": prefill_s,
                        "kv_share_of_bytes": sum(KV_BYTES_PER_POS * (prompt_len + i + 1) for i in range(steps)) / alg},
-            "e2e": {"value": replica_throughput(world, steps, e2e_ms), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 4, "us_per_token": e2e_ms * 1000.0 / steps,
-                    "api": "mkb_engine_step (8 B copied in from pinned memory, graph replay, the kernel "
-                           "stores the 4 B argmax into pinned host memory)"},
+            "e2e": e2e_fields(world, steps, serve_ms, step_ms),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": peak_kind, "traffic": traffic, "kernel": "decode_kernel",
                          "algorithmic_bytes_per_launch": alg},
@@ -604,22 +647,8 @@ def main():
     st = eng.status()
     assert st[0] == 0, f"in-kernel error {st}"
 
-    # e2e through the public per-token call
-    for i in range(warm):
-        eng.step(first, PROMPT + i)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    t = first
-    for i in range(steps):
-        t = eng.step(t, PROMPT + (i % span))
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t0
-
-    dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_s * 1000.0], world, dev)
+    serve_s, step_s = end_to_end(eng, first, PROMPT, steps, warm, span)
+    dev_ms, serve_ms, step_ms = max_over_ranks([dev_ms, serve_s * 1000.0, step_s * 1000.0], world, dev)
 
     # algorithmic bytes of the timed launches (positions 32.. wrap every `span` tokens)
     alg = 0
@@ -648,10 +677,7 @@ def main():
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: 1.19 GB of weights streamed per token vs 126 MB L2",
                        "us_per_token": dev_ms * 1000.0 / steps, "tokens_per_launch": toks_per_launch},
-            "e2e": {"value": replica_throughput(world, steps, e2e_ms), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 4, "us_per_token": e2e_ms * 1000.0 / steps,
-                    "api": "mkb_engine_step (8 B copied in from pinned memory, graph replay, the kernel "
-                           "stores the 4 B argmax into pinned host memory)"},
+            "e2e": e2e_fields(world, steps, serve_ms, step_ms),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
                          "traffic": traffic,

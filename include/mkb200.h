@@ -155,6 +155,11 @@ typedef struct mkb_decode_args {
   void* peer_workspaces[8];    /* tp_size > 1: every rank's workspace as this GPU
                                   addresses it (peer_workspaces[tp_rank] == workspace;
                                   the others mapped with mkb_ipc_open) */
+  int* mailbox;                /* serve mode (with result): mapped pinned int[2] {seq, token};
+                                  token t of the launch is taken once seq == t + 1 (a
+                                  negative token ends the launch); NULL otherwise */
+  int* result;                 /* serve mode: mapped pinned int[2] {seq, argmax}: the argmax
+                                  of token t, then seq = t + 1 */
 } mkb_decode_args;
 
 void mkb_decode_args_init(mkb_decode_args* a);
@@ -222,6 +227,20 @@ cudaError_t mkb_engine_generate(mkb_engine* e, int token, int position, int n, i
  * model.py:102-105): that id is the last one written, later entries read -1. */
 cudaError_t mkb_engine_generate_until(mkb_engine* e, int token, int position, int n, int stop_token,
                                       int* out_tokens, cudaStream_t stream);
+/* Serve session (no counterpart in the reference): one persistent launch that
+ * decodes up to max_tokens tokens at positions position, position+1, ..., each
+ * input token handed over by the host through pinned mapped memory and each
+ * argmax handed back the same way, so a token costs no launch and no copy.
+ * serve_open launches it on `stream` and returns; serve_step gives token t and
+ * waits (host spin, bounded by timeout_ns) for its argmax; serve_close ends the
+ * launch (after fewer than max_tokens steps too) and synchronises the stream.
+ * Between steps the launch waits for the host at most timeout_ns (0 = 1 s),
+ * then fails with a status. No other call may use the engine while a session is
+ * open; TP engines are not supported. */
+cudaError_t mkb_engine_serve_open(mkb_engine* e, int position, int max_tokens, unsigned long long timeout_ns,
+                                  cudaStream_t stream);
+cudaError_t mkb_engine_serve_step(mkb_engine* e, int token, int* next_token);
+cudaError_t mkb_engine_serve_close(mkb_engine* e);
 /* In-engine prefill: the n prompt ids (device int[n]) enter at positions
  * position .. position+n-1 in one persistent launch that appends their K/V rows;
  * the LM head runs for the last one only, whose argmax (the first generated

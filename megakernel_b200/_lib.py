@@ -72,6 +72,8 @@ class DecodeArgs(Structure):
         ("tp_rank", c_int),
         ("tp_size", c_int),
         ("peer_workspaces", c_void_p * 8),
+        ("mailbox", c_void_p),
+        ("result", c_void_p),
     ]
 
 
@@ -120,6 +122,9 @@ SIGNATURES = [
     ("mkb_engine_step", c_int, [c_void_p, c_int, c_int, POINTER(c_int), c_void_p]),
     ("mkb_engine_generate", c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     ("mkb_engine_generate_until", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    ("mkb_engine_serve_open", c_int, [c_void_p, c_int, c_int, c_ulonglong, c_void_p]),
+    ("mkb_engine_serve_step", c_int, [c_void_p, c_int, POINTER(c_int)]),
+    ("mkb_engine_serve_close", c_int, [c_void_p]),
     ("mkb_engine_prefill", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     ("mkb_engine_prefill_batched", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     ("mkb_gemm_bf16_split", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),

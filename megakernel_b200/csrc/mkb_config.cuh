@@ -215,6 +215,12 @@ struct DecodeParams {
   int tp_rank, tp_size;              // tensor parallel position (size 1: single GPU)
   Workspace* peer_ws[kMaxTP];        // every rank's workspace as this GPU addresses it
                                      // (peer_ws[tp_rank] == ws)
+  // Serve mode (both non-null): each token's input comes from the host --
+  // mailbox {seq, token} in mapped pinned memory, token t taken once seq == t+1,
+  // a negative token ends the launch -- and its argmax goes back to result
+  // {seq, token} (token first, then seq = t+1).
+  volatile int* mailbox;
+  volatile int* result;
 };
 
 // Trace record: (code << 48) | (globaltimer ns & 0xffffffffffff). Row cta is

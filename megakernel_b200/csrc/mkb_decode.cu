@@ -194,6 +194,29 @@ __device__ __noinline__ void spin_geq_sys(const Ctl c, const uint32_t* ctr, uint
   }
 }
 
+// Serve mode: bounded wait (the launch's timeout) for the host's request of
+// token t in mapped pinned memory: {seq, token} with seq == t + 1. One thread.
+__device__ __noinline__ int host_token(const Ctl c, volatile int* mailbox, int t) {
+  const uint64_t t0 = global_ns();
+  uint32_t it = 0;
+  while (true) {
+    int seq;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(seq) : "l"(mailbox) : "memory");
+    if (seq == t + 1) return mailbox[1];
+    if ((++it & 15u) == 0u) {
+      if (aborted(c)) return -1;
+      if (ld_relaxed(&c.ws->error[0]) != 0u) {
+        *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
+        return -1;
+      }
+      if (global_ns() - t0 > c.timeout) {
+        raise_error(c, kErrTimeoutToken, -1, kStToken, t);
+        return -1;
+      }
+    }
+  }
+}
+
 // Consumer-side transition: thread 0 waits, then all consumers proceed.
 template <class TR>
 __device__ __forceinline__ void transition_wait(const Ctl& c, TR& tr, const uint32_t* ctr, uint32_t target,
@@ -965,6 +988,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   const bool tpx = tp.size > 1;
   const int lb = p.layer_begin, le = p.layer_end;
   const int zero_cta = G - 1;
+  const bool serve = p.mailbox != nullptr && p.result != nullptr;
   // With 1 + kDownCopies CTAs outside the head groups (148 SMs: 4), those CTAs,
   // idle during attention, clear the layer l-2 accumulators there; otherwise
   // the last CTA clears them before its QKV rows (which then publish late).
@@ -1009,7 +1033,45 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
     const bool lm_now = (p.flags & kFlagLmHead) && (p.prompt == nullptr || last_tok);
 
     // ---- token input: embedding gather (megakernel.cu:783-795) ----
-    if (t > 0) {
+    if (serve) {
+      // serve mode: CTA 0 takes the host's token t (mailbox seq == t + 1) and
+      // broadcasts it; a negative token ends the launch
+      if (c.cta == 0 && tid == 0) {
+        const int v = host_token(c, p.mailbox, t);
+        if (!aborted(c)) {
+          ws->tok_flag[1] = static_cast<uint32_t>(v);
+          st_release(&ws->tok_flag[0], static_cast<uint32_t>(t + 1));
+        }
+      }
+      if (tid == 0) spin_geq(c, &ws->tok_flag[0], static_cast<uint32_t>(t + 1), kErrTimeoutToken, -1, 9, t);
+      consumer_sync(kConsumerThreads);
+      if (tid == 0) sm.token = static_cast<int>(__ldcg(reinterpret_cast<const int*>(&ws->tok_flag[1])));
+      consumer_sync(kConsumerThreads);
+      token = sm.token;
+      if (token < 0 && !aborted(c)) {
+        // every CTA leaves here; the last one to see the end restores the
+        // workspace for the next launch (every earlier token left its
+        // accumulators cleared)
+        if (tid == 0) {
+          *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+          uint32_t old;
+          asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&ws->stop_seen[0]) : "memory");
+          if (old == static_cast<uint32_t>(G - 1)) {
+            for (int i = 0; i < kMaxLayers * 4; ++i) ws->sync[i >> 2][i & 3][0] = 0u;
+            for (int i = 0; i < kMaxLayers * kNKV; ++i) {
+              ws->kv_ready[i / kNKV][i % kNKV][0] = 0u;
+              ws->att_sync[i / kNKV][i % kNKV][0] = 0u;
+            }
+            ws->arrive[0] = 0u;
+            ws->arrive_x[0] = 0u;
+            ws->tag_base[0] = tag0 + static_cast<uint32_t>(t);
+            ws->stop_seen[0] = 0u;
+            ws->tok_flag[0] = 0u;
+          }
+        }
+        return;
+      }
+    } else if (t > 0) {
       // the previous token is complete (and its last CTA has reset the shared state)
       if (tid == 0) spin_geq(c, &ws->tok_flag[0], static_cast<uint32_t>(t), kErrTimeoutToken, -1, 9, t);
       consumer_sync(kConsumerThreads);
@@ -1737,6 +1799,11 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       consumer_sync(kConsumerThreads);
       if (tid == 0) {
         if (lm_now) {
+          if (serve) {
+            p.result[1] = best;
+            __threadfence_system();  // the token before its sequence number
+            p.result[0] = t + 1;
+          }
           if (p.out_tokens != nullptr) p.out_tokens[t] = best;
           if (p.step != nullptr && (p.flags & kFlagAdvanceStep)) {
             p.step[0] = best;
@@ -1749,6 +1816,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           ws->arrive_x[0] = 0u;
           ws->tok_flag[0] = 0u;
           ws->tag_base[0] = tag0 + static_cast<uint32_t>(p.n_tokens);
+        } else if (serve) {
+          // the host decides the next token (the mailbox), not the argmax
         } else if (stop_now) {
           // every CTA has arrived for this token and none adds again; tok_flag
           // still carries the stop id to the others (cleared by the last to see it)

@@ -8,6 +8,8 @@
 //    per-token launch stay alive across tokens (the reference rebuilt and freed
 //    its table on every call, pytorch_binding.cu:84-126).
 
+#include <atomic>
+#include <chrono>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -161,6 +163,9 @@ cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p, DeviceInfo** df
   p->prompt = a->prompt_tokens;
   p->err_flag = a->err_flag ? a->err_flag : (a->workspace == nullptr ? d->d_err : nullptr);
   p->stop_token = a->stop_token;
+  p->mailbox = a->mailbox;
+  p->result = a->result;
+  if ((a->mailbox == nullptr) != (a->result == nullptr)) return cudaErrorInvalidValue;
   if (p->stop_token >= kVocab) return cudaErrorInvalidValue;
   // Host-side validation of what the host can see (the kernel re-checks the rest).
   if (!p->embed || !p->layers || !p->k_cache || !p->v_cache || !p->cos_table || !p->sin_table)
@@ -377,6 +382,12 @@ struct mkb_engine {
   cudaStream_t cap_stream = nullptr;
   mkb_decode_args step_args;
   std::vector<LayerWeights> host_layers;      // the layer table as the host sees it (prefill tensor maps)
+  // serve session: mailbox = h_io[2..3] {seq, token}, result = h_io[6..7] {seq, argmax}
+  bool serving = false;
+  int serve_seq = 0;
+  int serve_max = 0;
+  unsigned long long serve_timeout = 0;
+  cudaStream_t serve_stream = nullptr;
   PrefillScratch pf = {};                     // batched prefill scratch, allocated on first use
   void* pf_block = nullptr;
 };
@@ -418,6 +429,7 @@ cudaError_t engine_check_status(mkb_engine* e) {
 // reset, cudaErrorLaunchFailure returned, nothing launched.
 cudaError_t engine_report_earlier(mkb_engine* e, cudaStream_t stream) {
   if (!e->tp_ready) return cudaErrorInvalidValue;  // a tensor-parallel rank before mkb_engine_tp_attach
+  if (e->serving) return cudaErrorInvalidValue;    // a serve session holds the engine
   if (reinterpret_cast<volatile int*>(e->h_io)[5] == 0) return cudaSuccess;
   cudaError_t err = cudaStreamSynchronize(stream);
   if (err != cudaSuccess) return err;
@@ -718,9 +730,94 @@ cudaError_t mkb_gemm_bf16_split(const void* a_hi, const void* a_lo, const void* 
                     static_cast<const __nv_bfloat16*>(b), c, m, n, k, nullptr, stream);
 }
 
+cudaError_t mkb_engine_serve_open(mkb_engine* e, int position, int max_tokens, unsigned long long timeout_ns,
+                                  cudaStream_t stream) {
+  if (!e || e->serving || max_tokens < 1 || position < 0 || position + max_tokens > e->max_seq)
+    return cudaErrorInvalidValue;
+  if (e->tp_size > 1) return cudaErrorNotSupported;
+  cudaError_t err = engine_report_earlier(e, stream);
+  if (err != cudaSuccess) return err;
+  volatile int* io = e->h_io;
+  io[2] = 0;
+  io[3] = 0;
+  io[6] = 0;
+  io[7] = -1;
+  mkb_decode_args a = e->step_args;
+  a.step = nullptr;
+  a.token = 0;  // every input comes from the mailbox
+  a.position = position;
+  a.cache_len = position + 1;
+  a.n_tokens = max_tokens;
+  a.out_tokens = nullptr;
+  a.mailbox = e->d_io + 2;
+  a.result = e->d_io + 6;
+  a.timeout_ns = timeout_ns ? timeout_ns : 1000000000ull;
+  err = mkb_decode(&a, stream);
+  if (err != cudaSuccess) return err;
+  e->serving = true;
+  e->serve_seq = 0;
+  e->serve_max = max_tokens;
+  e->serve_timeout = a.timeout_ns;
+  e->serve_stream = stream;
+  return cudaSuccess;
+}
+
+namespace {
+// Ends a session: stops the launch if it is still waiting for tokens, waits for
+// it, and reports an in-kernel failure (workspace reset) as cudaErrorLaunchFailure.
+cudaError_t serve_finish(mkb_engine* e) {
+  volatile int* io = e->h_io;
+  if (e->serve_seq < e->serve_max) {
+    io[3] = -1;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    io[2] = e->serve_seq + 1;
+  }
+  e->serving = false;
+  cudaError_t err = cudaStreamSynchronize(e->serve_stream);
+  if (err != cudaSuccess) return err;
+  if (io[5] != 0) {
+    const cudaError_t st = engine_check_status(e);
+    return st != cudaSuccess ? st : cudaErrorLaunchFailure;
+  }
+  return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t mkb_engine_serve_step(mkb_engine* e, int token, int* next_token) {
+  if (!e || !e->serving || e->serve_seq >= e->serve_max) return cudaErrorInvalidValue;
+  if (token < 0 || token >= kVocab) return cudaErrorInvalidValue;
+  volatile int* io = e->h_io;
+  const int seq = ++e->serve_seq;
+  io[3] = token;
+  std::atomic_thread_fence(std::memory_order_seq_cst);  // the token before its sequence number
+  io[2] = seq;
+  // the launch answers within a token's time; give up after the session timeout
+  const auto t0 = std::chrono::steady_clock::now();
+  while (io[6] != seq) {
+    if (io[5] != 0 ||
+        std::chrono::steady_clock::now() - t0 > std::chrono::nanoseconds(2 * e->serve_timeout)) {
+      const cudaError_t st = serve_finish(e);
+      return st != cudaSuccess ? st : cudaErrorLaunchFailure;
+    }
+  }
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  if (next_token) *next_token = io[7];
+  if (seq == e->serve_max) return serve_finish(e);  // the launch ends after its last token
+  return cudaSuccess;
+}
+
+cudaError_t mkb_engine_serve_close(mkb_engine* e) {
+  if (!e) return cudaErrorInvalidValue;
+  if (!e->serving) return cudaSuccess;
+  return serve_finish(e);
+}
+
 float* mkb_engine_logits(mkb_engine* e) { return e ? e->d_logits : nullptr; }
 void* mkb_engine_workspace(mkb_engine* e) { return e ? e->ws : nullptr; }
 int mkb_engine_grid(mkb_engine* e) { return e ? e->grid : 0; }
-void mkb_engine_destroy(mkb_engine* e) { engine_free(e); }
+void mkb_engine_destroy(mkb_engine* e) {
+  if (e && e->serving) serve_finish(e);
+  engine_free(e);
+}
 
 }  // extern "C"

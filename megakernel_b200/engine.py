@@ -184,6 +184,27 @@ class DecodeEngine:
     def status(self) -> list:
         return _lib.workspace_status(self.workspace_ptr)
 
+    # ---- serve session: one persistent launch, tokens through pinned memory ----
+    def serve_open(self, position: int, max_tokens: int, timeout_s: float = 1.0, stream=None):
+        """Start a session of up to ``max_tokens`` tokens at ``position``.. (see
+        mkb_engine_serve_open): each :meth:`serve_step` hands one input token to the
+        running launch and returns its argmax, without a launch or a copy."""
+        _require(max_tokens >= 1 and 0 <= position and position + max_tokens <= self.max_seq,
+                 "serve range out of bounds")
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.mkb_engine_serve_open(self._h, int(position), int(max_tokens),
+                                                      int(timeout_s * 1e9), c_void_p(_stream_ptr(stream))),
+                       "mkb_engine_serve_open")
+
+    def serve_step(self, token: int) -> int:
+        _require(0 <= token < VOCAB, "token_id out of range")
+        out = c_int(-1)
+        _lib.check(self.lib.mkb_engine_serve_step(self._h, int(token), byref(out)), "mkb_engine_serve_step")
+        return out.value
+
+    def serve_close(self):
+        _lib.check(self.lib.mkb_engine_serve_close(self._h), "mkb_engine_serve_close")
+
     def ipc_handle(self) -> bytes:
         """64 bytes that let another process on this node map this engine's workspace."""
         buf = ctypes.create_string_buffer(64)

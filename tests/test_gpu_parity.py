@@ -440,6 +440,49 @@ def test_generate_stops_on_stop_token(w_gpu, hf_model, config0_hf):
     eng.close()
 
 
+def test_serve_session_matches_generate(w_gpu, hf_model, config0_hf):
+    """A serve session (one persistent launch, each input token handed over by
+    the host through pinned memory) decodes exactly what a generate launch does
+    (same kernel path: tokens, K/V rows and logits bit-identical); closing it
+    early stops at the right row; a host that stops feeding it past the timeout
+    gets an error, and the engine recovers."""
+    import time
+    g, fed, _ = config0_hf
+    _, _, kg, vg = prefill_to_gpu(hf_model, torch.from_numpy(g["prompt"]), 512)
+    eng = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), kg, vg)
+    k0, v0 = kg.clone(), vg.clone()
+    gen = eng.generate(fed[0], 32, 24).cpu().tolist()
+    kgen, vgen, lgen = kg.clone(), vg.clone(), eng.logits.clone()
+    kg.copy_(k0)
+    vg.copy_(v0)
+    eng.serve_open(32, 24)
+    tok, got = fed[0], []
+    for _ in range(24):
+        tok = eng.serve_step(tok)
+        got.append(tok)
+    eng.serve_close()
+    assert got == gen
+    assert torch.equal(kg, kgen) and torch.equal(vg, vgen) and torch.equal(eng.logits, lgen)
+    assert eng.status()[0] == 0
+    # closed after 5 of 24 tokens: rows 32..36 appended, nothing after
+    kg.copy_(k0)
+    vg.copy_(v0)
+    eng.serve_open(32, 24)
+    tok = fed[0]
+    for _ in range(5):
+        tok = eng.serve_step(tok)
+    eng.serve_close()
+    assert torch.equal(kg[:, :, :37], kgen[:, :, :37]) and torch.equal(kg[:, :, 37:], k0[:, :, 37:])
+    assert eng.status()[0] == 0
+    # a host that goes quiet: the launch gives up after its timeout, the next step reports it
+    eng.serve_open(32, 8, timeout_s=0.02)
+    time.sleep(0.3)
+    with pytest.raises(_lib.MkbError):
+        eng.serve_step(fed[0])
+    assert eng.step(fed[0], 32) == gen[0]  # the engine works again
+    eng.close()
+
+
 # ---------------------------------------------------------------- failure reporting
 def _c_abi_call(lib, table, w_gpu, cos, sin, kg, vg, bufs, tok, pos):
     import ctypes
