@@ -7,9 +7,10 @@ memory and cover layers 8-15 plus the token-level marks. This module launches
 the kernel with such a buffer and reduces the stamps to per-stage wait and
 compute times.
 
-    python -m megakernel_b200.trace [--tokens N] [--position P] [--reference-layout]
+    python -m megakernel_b200.trace [--tokens N] [--position P] [--max-seq S] [--reference-layout]
 
-runs config 0 shapes (synthetic weights, 512-slot cache) and prints the summary.
+runs config 0 shapes (synthetic weights, a 512-slot cache unless --max-seq says
+otherwise) and prints the summary.
 """
 from __future__ import annotations
 
@@ -217,6 +218,7 @@ def main():
     ap.add_argument("--reference-layout", action="store_true")
     ap.add_argument("--repeat", type=int, default=3)
     ap.add_argument("--plain", action="store_true", help="launch without the trace buffer (for ncu)")
+    ap.add_argument("--max-seq", type=int, default=512, help="cache slots (4096 for config-3 lengths)")
     a = ap.parse_args()
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(1000)
@@ -230,8 +232,9 @@ def main():
     for _ in range(28):
         layers += [ones(1024), lin(2048, 1024), lin(1024, 1024), lin(1024, 1024), ones(128), ones(128),
                    lin(1024, 2048), ones(1024), lin(3072, 1024), lin(3072, 1024), lin(1024, 3072)]
-    k = torch.randn((28, 8, 512, 128), generator=g, device=dev).to(torch.bfloat16)
-    v = torch.randn((28, 8, 512, 128), generator=g, device=dev).to(torch.bfloat16)
+    assert 0 <= a.position and a.position + a.tokens <= a.max_seq, "positions past the cache"
+    k = torch.randn((28, 8, a.max_seq, 128), generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn((28, 8, a.max_seq, 128), generator=g, device=dev).to(torch.bfloat16)
     td = TracedDecoder(embed, ones(1024), layers, k, v, fused=not a.reference_layout)
     res = None
     for _ in range(a.repeat):
