@@ -127,7 +127,9 @@ struct alignas(128) Workspace {
   uint32_t sync[kMaxLayers][4][32];
   uint32_t att_sync[kMaxLayers][kNKV][32];   // split attention partials published
   uint32_t arrive[32];                       // end-of-token arrivals (last one reduces)
-  uint32_t tok_flag[32];                     // greedy token broadcast (multi-token launches)
+  // Token broadcast (multi-token launches): word 0 = sequence (t + 1) in the low
+  // 32 bits, the token id in the high 32 bits, published by one release store.
+  uint64_t tok_flag[16];
   uint32_t error[32];                        // [0] code, [1] cta, [2] layer, [3] stage, [4] token
   uint32_t tag_base[32];                     // [0]: tag of the last token decoded (tagged words)
   uint32_t stop_seen[32];                    // CTAs that saw a stop token (the last one resets tok_flag)

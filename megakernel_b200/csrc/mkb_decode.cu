@@ -64,7 +64,6 @@ struct __align__(128) Smem {
   alignas(16) float knew[kHeadDim];  // rotated new key (BF16-rounded)
   alignas(16) float vnew[kHeadDim];  // new value (BF16-rounded)
   alignas(16) float attn[2 * kHeadDim];
-  alignas(16) float gu[2][32];
   alignas(16) float m[32];
   alignas(16) float mrx[32];  // the cluster partner's SwiGLU values (down projection)
   alignas(16) float apeer[2][kHeadDim + 4];  // the partner's attention partial: o[128], m, l per head
@@ -171,6 +170,31 @@ __device__ __noinline__ void spin_geq(const Ctl c, const uint32_t* ctr, uint32_t
       }
     }
   }
+}
+
+// Bounded wait for token t's broadcast (sequence >= target in the low half of
+// the packed word); returns the token id it carries (-1 when the wait gave up).
+__device__ __noinline__ int spin_token(const Ctl c, const uint64_t* w, uint32_t target, int tok) {
+  const uint64_t t0 = global_ns();
+  uint32_t it = 0;
+  while (true) {
+    const uint64_t v = ld_acquire_u64(w);
+    if (static_cast<int>(static_cast<uint32_t>(v) - target) >= 0) return static_cast<int>(v >> 32);
+    if ((++it & 15u) == 0u) {
+      if (aborted(c)) return -1;
+      if (ld_relaxed(&c.ws->error[0]) != 0u) {
+        *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
+        return -1;
+      }
+      if (global_ns() - t0 > c.timeout) {
+        raise_error(c, kErrTimeoutToken, -1, 9, tok);
+        return -1;
+      }
+    }
+  }
+}
+__device__ __forceinline__ uint64_t tok_word(int t, int token) {
+  return (static_cast<uint64_t>(static_cast<uint32_t>(token)) << 32) | static_cast<uint32_t>(t + 1);
 }
 
 // spin_geq on a counter that other GPUs add into (tensor parallel).
@@ -1038,14 +1062,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       // broadcasts it; a negative token ends the launch
       if (c.cta == 0 && tid == 0) {
         const int v = host_token(c, p.mailbox, t);
-        if (!aborted(c)) {
-          ws->tok_flag[1] = static_cast<uint32_t>(v);
-          st_release(&ws->tok_flag[0], static_cast<uint32_t>(t + 1));
-        }
+        if (!aborted(c)) st_release_u64(&ws->tok_flag[0], tok_word(t, v));
       }
-      if (tid == 0) spin_geq(c, &ws->tok_flag[0], static_cast<uint32_t>(t + 1), kErrTimeoutToken, -1, 9, t);
-      consumer_sync(kConsumerThreads);
-      if (tid == 0) sm.token = static_cast<int>(__ldcg(reinterpret_cast<const int*>(&ws->tok_flag[1])));
+      if (tid == 0) sm.token = spin_token(c, &ws->tok_flag[0], static_cast<uint32_t>(t + 1), t);
       consumer_sync(kConsumerThreads);
       token = sm.token;
       if (token < 0 && !aborted(c)) {
@@ -1066,18 +1085,17 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             ws->arrive_x[0] = 0u;
             ws->tag_base[0] = tag0 + static_cast<uint32_t>(t);
             ws->stop_seen[0] = 0u;
-            ws->tok_flag[0] = 0u;
+            ws->tok_flag[0] = 0ull;
           }
         }
         return;
       }
     } else if (t > 0) {
-      // the previous token is complete (and its last CTA has reset the shared state)
-      if (tid == 0) spin_geq(c, &ws->tok_flag[0], static_cast<uint32_t>(t), kErrTimeoutToken, -1, 9, t);
+      // the previous token is complete (and its last CTA has reset the shared
+      // state); the broadcast word carries its argmax
+      if (tid == 0) sm.token = spin_token(c, &ws->tok_flag[0], static_cast<uint32_t>(t), t);
       consumer_sync(kConsumerThreads);
       if (p.prompt == nullptr) {
-        if (tid == 0) sm.token = static_cast<int>(__ldcg(reinterpret_cast<const int*>(&ws->tok_flag[1])));
-        consumer_sync(kConsumerThreads);
         token = sm.token;
         if (p.stop_token >= 0 && token == p.stop_token && !aborted(c)) {
           // The previous token was the stop id (model.py:102-105 ends its loop
@@ -1090,7 +1108,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&ws->stop_seen[0]) : "memory");
             if (old == static_cast<uint32_t>(G - 1)) {
               ws->stop_seen[0] = 0u;
-              ws->tok_flag[0] = 0u;
+              ws->tok_flag[0] = 0ull;
             }
             if (c.cta == 0 && p.out_tokens != nullptr)
               for (int i = t; i < p.n_tokens; ++i) p.out_tokens[i] = -1;
@@ -1155,7 +1173,6 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         mma_tile_1024(sa[0], ea0 - ra0, bfr, d0);
         if (na > 1) mma_tile_1024(sa[1], ea1 - ra1, bfr, d1);
         if (na > 2) mma_tile_1024(sa[2], ea2 - ra2, bfr, d2);
-        ring_done_all(c, n, na);
         tr.mark(kTrMark, kSubAMma, l, t);
         stash_tile(xred, 0, d0);
         stash_tile(xred, 1, d1);
@@ -1178,7 +1195,13 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             }
           }
         }
-        consumer_sync(kConsumerThreads);
+        // The slots go back to the producer after the publish: its next bulk
+        // copies would otherwise be issued ahead of the tagged stores (-2.7 us
+        // per token measured).
+        ring_done_all(c, n, na);
+        // xred is reused by the next pass; after the last one the next writer
+        // (attention, o_proj) is past the head-preparation barrier
+        if (rr < pl.qb) consumer_sync(kConsumerThreads);
       }
       tr.mark(kTrPublish, kStA, l, t);
       wD = load_w4(lwt(c, l, kWPost));  // post-attention norm, one stage ahead
@@ -1206,13 +1229,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           const int base = warp < 2 ? (2 * h + warp) * kHeadDim
                                     : (warp == 2 ? kQSize + h * kHeadDim : kQSize + kKVSize + h * kHeadDim);
           float x0, x1, x2, x3;  // dims d0, d0+1, d0+64, d0+65
-          // lane 0 polls the end of the range first, then every lane reads its
-          // words (few pollers; stragglers are polled by their readers)
-          if (lane == 0) {
-            float y0, y1;
-            poll_tagged2(c, &ws->qkv_tagged[l][base + kHeadDim - 2], tag, y0, y1, l, t);
-          }
-          __syncwarp();
+          // every lane polls its own words: a single poller per warp followed by
+          // the lanes' reads cost one more L2 round trip (+8.7 us per token measured)
           poll_tagged2(c, &ws->qkv_tagged[l][base + d0], tag, x0, x1, l, t);
           poll_tagged2(c, &ws->qkv_tagged[l][base + d0 + 64], tag, x2, x3, l, t);
           if (warp < 3) {
@@ -1517,7 +1535,6 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
                 mma_bf16(d[tt], a0, a1, a2, a3, ob[st][0], ob[st][1]);
               }
             }
-            ring_done(c, n);
             tr.mark(kTrMark, kSubBCOMma, l, t);
 #pragma unroll
             for (int tt = 0; tt < 4; ++tt) stash_tile(xred, tt, d[tt]);
@@ -1528,7 +1545,10 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
               acc_add(p, &ws->acc_mid[l][o0 + tid], acc_term(sum_warps(xred, tid), bad));
               if (bad) raise_error(c, kErrRange, l, kStBC, t);
             }
-            consumer_sync(kConsumerThreads);
+            ring_done(c, n);  // after the publish, as for QKV
+            // after the last chunk the next xred writer (gate/up) is past the
+            // post-attention norm's barrier
+            if (o0 + kORowsPerChunk < pl.ob) consumer_sync(kConsumerThreads);
           }
         }
         tr.mark(kTrPublish, kStBC, l, t);
@@ -1585,26 +1605,25 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         stash_tile(xred, 2, d2);
         consumer_sync(kConsumerThreads);
         tr.mark(kTrMark, kSubDEBar, l, t);
-        if (tid < 16 * ng) {
-          const int i = (tid & 15) & 7;
-          const int j = jb0 + (tid >> 4) * kGUPerChunk + i;
-          if (i < kGUPerChunk && j < nj) sm.gu[(tid & 15) >> 3][j] = sum_warps(xred, tid) * rstd_d;
+        // thread j of the pass sums gate row j and up row j over the warps (tile
+        // j / 7, rows j % 7 and 8 + j % 7) and forms silu(gate) * up at once
+        // (megakernel.cu:100-142, config.cuh:177-179)
+        const int jl = tid - jb0;
+        if (tid >= jb0 && jl < 3 * kGUPerChunk && tid < nj) {
+          const int xi = (jl / kGUPerChunk) * 16 + jl % kGUPerChunk;
+          const float g = sum_warps(xred, xi) * rstd_d, u = sum_warps(xred, xi + 8) * rstd_d;
+          const float mv = g / (1.0f + expf(-g)) * u;
+          sm.m[tid] = mv;
+          // The cluster partner reduces the other column block over these rows too:
+          // each value lands in its shared memory with 4 bytes of complete_tx on its
+          // rxbar, so no thread here waits on a release.
+          if constexpr (fused) {
+            if (*reinterpret_cast<volatile int*>(&sm.peer_gone) == 0) st_async_f32(rx_m_peer, mv, rx_bar_peer);
+          }
         }
         consumer_sync(kConsumerThreads);
       }
       tr.mark(kTrMark, kSubDEGU, l, t);
-      if (tid < nj) {
-        const float g = sm.gu[0][tid], u = sm.gu[1][tid];
-        const float mv = g / (1.0f + expf(-g)) * u;  // silu (config.cuh:177-179) * up
-        sm.m[tid] = mv;
-        // The cluster partner reduces the other column block over these rows too:
-        // each value lands in its shared memory with 4 bytes of complete_tx on its
-        // rxbar, so no thread here waits on a release.
-        if constexpr (fused) {
-          if (*reinterpret_cast<volatile int*>(&sm.peer_gone) == 0) st_async_f32(rx_m_peer, mv, rx_bar_peer);
-        }
-      }
-      consumer_sync(kConsumerThreads);
       tr.mark(kTrMark, kSubDESilu, l, t);
       if constexpr (fused) {
         // Down projection split by output columns within the cluster pair: rank r
@@ -1626,7 +1645,6 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           uint32_t sa[1];
           ring_wait_all(c, n, 1, sa, l, 5, t, &tr);
           down_rows(sa[0], sm.mrx, nj2, pa0, pa1);
-          ring_done_all(c, n, 1);
         }
         tr.mark(kTrMark, kSubDEDown, l, t);
         {
@@ -1636,6 +1654,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           red_add_u64(dst + 1, acc_term(pa1, bad));
           if (bad) raise_error(c, kErrRange, l, kStDE, t);
         }
+        ring_done_all(c, n, 1);  // the partner rows' slot, after the publish
         tr.mark(kTrPublish, kStDE, l, t);
         // Arm the next phase of rxbar, now that this one is seen complete (one
         // arrival per phase; the partner's bytes may land before or after it).
@@ -1814,7 +1833,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         if (last_tok) {
           ws->arrive[0] = 0u;
           ws->arrive_x[0] = 0u;
-          ws->tok_flag[0] = 0u;
+          ws->tok_flag[0] = 0ull;
           ws->tag_base[0] = tag0 + static_cast<uint32_t>(p.n_tokens);
         } else if (serve) {
           // the host decides the next token (the mailbox), not the argmax
@@ -1824,11 +1843,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           ws->arrive[0] = 0u;
           ws->arrive_x[0] = 0u;
           ws->tag_base[0] = tag0 + static_cast<uint32_t>(t) + 1u;
-          ws->tok_flag[1] = static_cast<uint32_t>(best);
-          st_release(&ws->tok_flag[0], static_cast<uint32_t>(t + 1));
+          st_release_u64(&ws->tok_flag[0], tok_word(t, best));
         } else {
-          ws->tok_flag[1] = static_cast<uint32_t>(best);
-          st_release(&ws->tok_flag[0], static_cast<uint32_t>(t + 1));  // covers the CTA's writes above
+          st_release_u64(&ws->tok_flag[0], tok_word(t, best));  // covers the CTA's writes above
         }
       }
     }
