@@ -80,6 +80,10 @@ constexpr uint64_t kAccLowMask = kAccOne - 1ull;
 // cut same-address atomic contention; readers add the copies.
 constexpr int kCluster = 2;  // 74 co-resident pairs use all 148 SMs
 constexpr int kSlice = 1024 / kCluster;  // output columns of the down projection per cluster rank
+// Transposed-down rows in a ring slot, padded so that the 8 rows of an
+// ldmatrix.trans 8x8 matrix fall in 8 different bank groups.
+constexpr int kDRowStride = kSlice * 2 + 16;
+constexpr int kDownKSteps = (kMaxJ + 15) / 16;  // MMA k-steps over a slot's rows
 #ifndef MKB_DOWN_COPIES
 #define MKB_DOWN_COPIES 2
 #endif

@@ -525,10 +525,13 @@ __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         const Plan pp = make_plan(static_cast<int>(blockIdx.x ^ 1u), p.grid, p.group_size, tp);
         const int rows[2][2] = {{pl.ja, pl.jb}, {pp.ja, pp.jb}};
         for (int q = 0; q < 2; ++q) {
-          const uint32_t bytes = static_cast<uint32_t>(rows[q][1] - rows[q][0]) * kSlice * 2u;
-          const int s = pr.begin(bytes);
+          const int nr = rows[q][1] - rows[q][0];
+          const int s = pr.begin(static_cast<uint32_t>(nr) * kSlice * 2u);
           if (s < 0) break;
-          if (pr.lane == 0) pr.copy(s, 0, wdt + (size_t)rows[q][0] * kSlice, bytes, pr.pol_w);
+          // one copy per row into kDRowStride-padded rows (ldmatrix.trans reads)
+          if (pr.lane < nr)
+            pr.copy(s, static_cast<uint32_t>(pr.lane) * kDRowStride, wdt + (size_t)(rows[q][0] + pr.lane) * kSlice,
+                    kSlice * 2u, pr.pol_w);
           pr.end();
         }
       } else {
@@ -641,39 +644,47 @@ __device__ __forceinline__ void mma_tile_gu(uint32_t base, int nrows, const uint
 #pragma unroll
   for (int i = 0; i < 4; ++i) d[i] += e[i];
 }
-// Down projection over the SwiGLU rows j < nj of one slot (row j at
-// j * kSlice * 2 bytes, this thread's two columns at 4 * tid), weighted by m[j]:
-// unrolled over the static bound kMaxJ so the shared loads issue back to back
-// ahead of the FMAs, with two accumulator chains per column. m[j] is zero for
-// j >= nj and the weight word is masked there, so stale slot bytes never enter.
-__device__ __forceinline__ void down_rows(uint32_t slot, const float* m, int nj, float& a0, float& a1) {
-  const uint32_t col = slot + (threadIdx.x & (kConsumerThreads - 1)) * 4;
-  float b0 = 0.f, b1 = 0.f;
+// Down projection on the tensor cores: this warp's 64 output columns
+// [64 w, 64 w + 64) of the CTA's kSlice block are four 16-column tiles (MMA M),
+// the SwiGLU rows of one slot the reduction (MMA K: kDownKSteps steps of 16,
+// rows >= nj masked because their slot bytes may be stale), m[] the B operand as
+// BF16 high part (column 0) and remainder (column 1). The slot holds transposed
+// down rows at kDRowStride bytes; ldmatrix.trans turns them into A fragments.
+// Results accumulate into d (D columns 0 and 1 of each tile).
+__device__ __forceinline__ void down_mma(uint32_t slot, const float* m, int nj, float (*d)[4]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, tq = lane & 3, q = lane >> 3;
 #pragma unroll
-  for (int jj = 0; jj < kMaxJ; jj += 4) {
-    const float4 mv = *reinterpret_cast<const float4*>(m + jj);
-    uint32_t w[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      // unconditional load (rows up to kMaxJ lie inside the slot), then mask:
-      // a conditional asm load would become a branch per row
-      const uint32_t v = lds32(col + (jj + q) * (kSlice * 2));
-      w[q] = jj + q < nj ? v : 0u;
+  for (int ks = 0; ks < kDownKSteps; ++ks) {
+    const int k0 = 16 * ks;
+    // this lane's ldmatrix row: matrices 0/1 rows k0.., 2/3 rows k0+8.., matrices
+    // 1/3 eight columns on; rows past kMaxJ (always masked) read a row of the
+    // same bank group inside the slot instead
+    int kr = k0 + (lane & 7) + 8 * (q >> 1);
+    if (kr >= kMaxJ) kr -= 8;
+    const uint32_t arow = slot + static_cast<uint32_t>(kr * kDRowStride + (64 * warp + 8 * (q & 1)) * 2);
+    uint32_t b0 = 0u, b1 = 0u;
+    if (g < 2) {
+      const float2 x01 = *reinterpret_cast<const float2*>(m + k0 + 2 * tq);
+      const float2 x89 = *reinterpret_cast<const float2*>(m + k0 + 2 * tq + 8);
+      const uint32_t h0 = pack_bf2(x01.x, x01.y), h8 = pack_bf2(x89.x, x89.y);
+      b0 = g == 0 ? h0 : pack_bf2(x01.x - bf_lo(h0), x01.y - bf_hi(h0));
+      b1 = g == 0 ? h8 : pack_bf2(x89.x - bf_lo(h8), x89.y - bf_hi(h8));
     }
-    a0 = fmaf(bf_lo(w[0]), mv.x, a0);
-    a1 = fmaf(bf_hi(w[0]), mv.x, a1);
-    b0 = fmaf(bf_lo(w[1]), mv.y, b0);
-    b1 = fmaf(bf_hi(w[1]), mv.y, b1);
-    a0 = fmaf(bf_lo(w[2]), mv.z, a0);
-    a1 = fmaf(bf_hi(w[2]), mv.z, a1);
-    b0 = fmaf(bf_lo(w[3]), mv.w, b0);
-    b1 = fmaf(bf_hi(w[3]), mv.w, b1);
+    const int ka = k0 + 2 * tq;
+    const uint32_t m01 = (ka < nj ? 0x0000ffffu : 0u) | (ka + 1 < nj ? 0xffff0000u : 0u);
+    const uint32_t m89 = (ka + 8 < nj ? 0x0000ffffu : 0u) | (ka + 9 < nj ? 0xffff0000u : 0u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_trans(arow + 32 * i, a0, a1, a2, a3);
+      mma_bf16(d[i], a0 & m01, a1 & m01, a2 & m89, a3 & m89, b0, b1);
+    }
   }
-  a0 += b0;
-  a1 += b1;
 }
-static_assert(kMaxJ % 4 == 0 && kMaxJ <= 32 && kMaxJ * kSlice * 2 <= kSlotBytes,
-              "down_rows reads m[0, kMaxJ) as float4 and kMaxJ rows of a slot");
+static_assert(kMaxJ > 8 * (kDownKSteps * 2 - 1) - 8 && kMaxJ <= 16 * kDownKSteps && kMaxJ <= 32 &&
+                  kMaxJ * kDRowStride <= kSlotBytes && kSlice == 64 * kConsumerWarps,
+              "down_mma: row redirect, m[] reads below 32, slot capacity, 64 columns per warp");
 
 // Lanes holding D column pairs write this warp's row partials of tile t.
 __device__ __forceinline__ void stash_tile(float (*xred)[64], int t, const float* d) {
@@ -1628,30 +1639,29 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       if constexpr (fused) {
         // Down projection split by output columns within the cluster pair: rank r
         // reduces columns [kSlice r, kSlice (r + 1)) over both CTAs' intermediate
-        // rows (megakernel.cu:53-90, split by K across pairs); thread i owns two
-        // columns. Own rows first, then the partner's once its SwiGLU values land.
-        float pa0 = 0.f, pa1 = 0.f;
+        // rows (megakernel.cu:53-90, split by K across pairs), on the tensor
+        // cores. Own rows first, then the partner's once its SwiGLU values land.
+        float dd[4][4] = {};
         {
-          uint32_t sa[1];
-          ring_wait_all(c, n, 1, sa, l, 5, t, &tr);
-          down_rows(sa[0], sm.m, nj, pa0, pa1);
-          ring_done_all(c, n, 1);
+          const uint32_t sa = ring_wait(c, n, l, 5, t, &tr);
+          down_mma(sa, sm.m, nj, dd);
+          ring_done(c, n);
         }
         tr.mark(kTrMark, kSubDEOwn, l, t);
         if (rx_live) rx_live = cluster_rx_wait(c, &sm.rxbar, xph, l, kStDE, t);
         xph ^= 1u;
         tr.mark(kTrMark, kSubDERx, l, t);
-        {
-          uint32_t sa[1];
-          ring_wait_all(c, n, 1, sa, l, 5, t, &tr);
-          down_rows(sa[0], sm.mrx, nj2, pa0, pa1);
-        }
+        down_mma(ring_wait(c, n, l, 5, t, &tr), sm.mrx, nj2, dd);
         tr.mark(kTrMark, kSubDEDown, l, t);
-        {
+        if ((lane & 3) == 0) {
+          // D columns 0 and 1 (high part and remainder) of rows g and g + 8
           bool bad = false;
-          uint64_t* dst = &ws->acc_down[l][down_copy][crank * kSlice + 2 * tid];
-          red_add_u64(dst, acc_term(pa0, bad));
-          red_add_u64(dst + 1, acc_term(pa1, bad));
+          uint64_t* dst = &ws->acc_down[l][down_copy][crank * kSlice + 64 * warp + (lane >> 2)];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            red_add_u64(dst + 16 * i, acc_term(dd[i][0] + dd[i][1], bad));
+            red_add_u64(dst + 16 * i + 8, acc_term(dd[i][2] + dd[i][3], bad));
+          }
           if (bad) raise_error(c, kErrRange, l, kStDE, t);
         }
         ring_done_all(c, n, 1);  // the partner rows' slot, after the publish

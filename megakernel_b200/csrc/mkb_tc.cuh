@@ -1,5 +1,5 @@
 // Blackwell tensor-core plumbing for the batched prefill: TMA tiled loads
-// (cp.async.bulk.tensor, no multicast), shared-memory matrix descriptors,
+// (cp.async.bulk.tensor, each CTA loading its own tiles), shared-memory matrix descriptors,
 // tcgen05.mma with the accumulator in tensor memory (TMEM), tcgen05.commit to
 // an mbarrier, and tcgen05.ld for the epilogue. Hand-written inline PTX; the
 // descriptor bit layouts follow the PTX ISA (tcgen05 "shared memory descriptor"
