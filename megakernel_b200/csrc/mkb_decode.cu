@@ -429,11 +429,11 @@ struct Producer {
   }
 };
 
-template <bool kFused, bool kTraced>
+template <bool kFused, bool kTraced, bool kTP>
 __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int pos0, int cl0,
                              int splits) {
   Producer pr(c);
-  const TpShape tp = tp_shape(p.tp_rank, p.tp_size, kVocab);
+  const TpShape tp = tp_shape(kTP ? p.tp_rank : 0, kTP ? p.tp_size : 1, kVocab);
   const bool pair_attn = pair_shares_head(static_cast<int>(blockIdx.x), p.grid, p.group_size, tp);
   for (int t = 0; t < p.n_tokens && !pr.stop; ++t) {
     const int pos = pos0 + t;
@@ -932,14 +932,16 @@ __device__ __forceinline__ T* peer_field(const DecodeParams& p, int g, T* local)
 // GPU; with tensor parallelism the same word on every GPU (each one sums all
 // GPUs' contributions). The loop over ranks is unrolled so that the peer table
 // is indexed statically.
-__device__ __forceinline__ void acc_add(const DecodeParams& p, uint64_t* local, uint64_t term) {
-  if (p.tp_size <= 1) {
+// `tps`: the launch's tensor-parallel size (the constant 1 in the single-GPU
+// kernel, which then carries none of the peer code).
+__device__ __forceinline__ void acc_add(const DecodeParams& p, int tps, uint64_t* local, uint64_t term) {
+  if (tps <= 1) {
     red_add_u64(local, term);
     return;
   }
 #pragma unroll
   for (int g = 0; g < kMaxTP; ++g)
-    if (g < p.tp_size) red_add_u64_sys(peer_field(p, g, local), term);
+    if (g < tps) red_add_u64_sys(peer_field(p, g, local), term);
 }
 
 static_assert(kCluster == 2 && kSlice == 2 * kConsumerThreads, "down projection: two columns per thread");
@@ -987,10 +989,10 @@ __device__ __forceinline__ void poison_outputs(const DecodeParams& p, int va, in
 // contribution per GPU, into every GPU's acc_x; every CTA then reads acc_x
 // (tp_size contributions). Forwarding keeps the cross-GPU traffic at one word
 // per element and GPU instead of one per cluster pair.
-__device__ __forceinline__ void down_sums(const DecodeParams& p, const Ctl& c, int l, int down_copy0, float d[4],
-                                          int stage, int tok) {
+__device__ __forceinline__ void down_sums(const DecodeParams& p, int tps, const Ctl& c, int l, int down_copy0,
+                                          float d[4], int stage, int tok) {
   const int G = p.grid;
-  if (p.tp_size <= 1) {
+  if (tps <= 1) {
     acc_wait4(c, &p.ws->acc_down[l][0][0], kDownCopies, static_cast<uint32_t>(G / kCluster),
               static_cast<uint32_t>(down_copy0), 0, d, l, stage, tok);
     return;
@@ -1001,14 +1003,14 @@ __device__ __forceinline__ void down_sums(const DecodeParams& p, const Ctl& c, i
               static_cast<uint32_t>(down_copy0), 0, v, l, stage, tok);
     bool bad = false;
 #pragma unroll
-    for (int i = 0; i < kE; ++i) acc_add(p, &p.ws->acc_x[l][threadIdx.x * kE + i], acc_term(v[i], bad));
+    for (int i = 0; i < kE; ++i) acc_add(p, tps, &p.ws->acc_x[l][threadIdx.x * kE + i], acc_term(v[i], bad));
     if (bad) raise_error(c, kErrRange, l, stage, tok);
   }
-  acc_wait4(c, &p.ws->acc_x[l][0], 1, static_cast<uint32_t>(p.tp_size), static_cast<uint32_t>(p.tp_size), 0, d, l,
+  acc_wait4(c, &p.ws->acc_x[l][0], 1, static_cast<uint32_t>(tps), static_cast<uint32_t>(tps), 0, d, l,
             stage, tok, true);
 }
 
-template <bool kFused, bool kTraced>
+template <bool kFused, bool kTraced, bool kTP>
 __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int token0, int pos0, int cl0,
                              int splits, uint32_t tag0) {
   Smem& sm = *c.sm;
@@ -1019,7 +1021,8 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   const int e0 = tid * kE;  // first element owned by this thread
   constexpr bool fused = kFused;
   const int G = p.grid;
-  const TpShape tp = tp_shape(p.tp_rank, p.tp_size, kVocab);
+  const int tps = kTP ? p.tp_size : 1;
+  const TpShape tp = tp_shape(kTP ? p.tp_rank : 0, tps, kVocab);
   const bool tpx = tp.size > 1;
   const int lb = p.layer_begin, le = p.layer_end;
   const int zero_cta = G - 1;
@@ -1147,7 +1150,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
         if constexpr (fused) {
           tr.mark(kTrWaitBegin, kStA, l, t);
           float d[4];
-          down_sums(p, c, l - 1, down_copy0, d, kStA, t);
+          down_sums(p, tps, c, l - 1, down_copy0, d, kStA, t);
           tr.mark(kTrWaitEnd, kStA, l, t);
           const float4 rm = *reinterpret_cast<const float4*>(&sm.rmid[e0]);
           r[0] = rm.x + d[0]; r[1] = rm.y + d[1]; r[2] = rm.z + d[2]; r[3] = rm.w + d[3];
@@ -1553,7 +1556,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             tr.mark(kTrMark, kSubBCOBar, l, t);
             if (tid < nrows) {
               bool bad = false;
-              acc_add(p, &ws->acc_mid[l][o0 + tid], acc_term(sum_warps(xred, tid), bad));
+              acc_add(p, tps, &ws->acc_mid[l][o0 + tid], acc_term(sum_warps(xred, tid), bad));
               if (bad) raise_error(c, kErrRange, l, kStBC, t);
             }
             ring_done(c, n);  // after the publish, as for QKV
@@ -1706,7 +1709,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       if constexpr (fused) {
         tr.mark(kTrWaitBegin, kStLM, le - 1, t);
         float d[4];
-        down_sums(p, c, le - 1, down_copy0, d, kStLM, t);
+        down_sums(p, tps, c, le - 1, down_copy0, d, kStLM, t);
         tr.mark(kTrWaitEnd, kStLM, le - 1, t);
         const float4 rm = *reinterpret_cast<const float4*>(&sm.rmid[e0]);
         r[0] = rm.x + d[0]; r[1] = rm.y + d[1]; r[2] = rm.z + d[2]; r[3] = rm.w + d[3];
@@ -1863,7 +1866,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
 }
 
 
-template <bool kFused, bool kTraced>
+// kTP: the tensor-parallel instantiation (peer accumulators, cross-GPU argmax);
+// the single-GPU kernels carry none of that code.
+template <bool kFused, bool kTraced, bool kTP>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem* sm = reinterpret_cast<Smem*>(smem_raw);
@@ -1883,7 +1888,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
 
   // tensor parallel shape: 1, 2, 4 or 8 ranks, every peer workspace present,
   // the fused (transposed-down) schedule
-  bool tp_ok = p.tp_size == 1 || ((p.tp_size == 2 || p.tp_size == 4 || p.tp_size == 8) && kFused);
+  bool tp_ok = kTP ? (p.tp_size == 2 || p.tp_size == 4 || p.tp_size == 8) && kFused : p.tp_size == 1;
   tp_ok = tp_ok && p.tp_rank >= 0 && p.tp_rank < p.tp_size;
   for (int g = 0; g < kMaxTP; ++g)
     if (g < p.tp_size && p.tp_size > 1) tp_ok = tp_ok && p.peer_ws[g] != nullptr;
@@ -1954,25 +1959,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
     if (threadIdx.x == 0) st_cluster_u32(mapa_shared(smem_addr(&sm->peer_gone), cluster_ctarank() ^ 1u), 1u);
     if (threadIdx.x < kConsumerThreads) poison_outputs(p, pl.va, pl.vb, 0);
   } else if (threadIdx.x >= kConsumerThreads) {
-    producer_run<kFused, kTraced>(p, pl, c, pos, cl, splits);
+    producer_run<kFused, kTraced, kTP>(p, pl, c, pos, cl, splits);
   } else {
-    consumer_run<kFused, kTraced>(p, pl, c, token, pos, cl, splits, tag0);
+    consumer_run<kFused, kTraced, kTP>(p, pl, c, token, pos, cl, splits, tag0);
   }
   cluster_sync_all();
 }
 
 // ---- host-side launch ----------------------------------------------------------
-// The four instantiations: transposed-down (fused) or reference-layout
-// schedule, with or without trace stamps.
-template <bool kFused, bool kTraced>
+// The instantiations: transposed-down (fused) or reference-layout schedule,
+// with or without trace stamps, and the fused tensor-parallel kernel.
+template <bool kFused, bool kTraced, bool kTP>
 cudaError_t set_smem_attr() {
-  return cudaFuncSetAttribute(decode_kernel<kFused, kTraced>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  return cudaFuncSetAttribute(decode_kernel<kFused, kTraced, kTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(kSmemBytes));
 }
 
 // Largest grid of kCluster-CTA clusters that can be resident at once (each CTA
 // holds a whole SM's shared memory).
-template <bool kFused, bool kTraced>
+template <bool kFused, bool kTraced, bool kTP>
 cudaError_t resident_ctas(int grid, int* out) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -1986,7 +1991,7 @@ cudaError_t resident_ctas(int grid, int* out) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int clusters = 0;
-  const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, decode_kernel<kFused, kTraced>, &cfg);
+  const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, decode_kernel<kFused, kTraced, kTP>, &cfg);
   *out = clusters * kCluster;
   return e;
 }
@@ -2002,16 +2007,22 @@ cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   if (dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    if ((e = set_smem_attr<true, false>()) != cudaSuccess) return e;
-    if ((e = set_smem_attr<false, false>()) != cudaSuccess) return e;
-    if ((e = set_smem_attr<true, true>()) != cudaSuccess) return e;
-    if ((e = set_smem_attr<false, true>()) != cudaSuccess) return e;
-    int r[4];
-    if ((e = resident_ctas<true, false>(p.grid, &r[0])) != cudaSuccess) return e;
-    if ((e = resident_ctas<false, false>(p.grid, &r[1])) != cudaSuccess) return e;
-    if ((e = resident_ctas<true, true>(p.grid, &r[2])) != cudaSuccess) return e;
-    if ((e = resident_ctas<false, true>(p.grid, &r[3])) != cudaSuccess) return e;
-    resident[dev] = min(min(r[0], r[1]), min(r[2], r[3]));
+    if ((e = set_smem_attr<true, false, false>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<false, false, false>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<true, true, false>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<false, true, false>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<true, false, true>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<true, true, true>()) != cudaSuccess) return e;
+    int r[6];
+    if ((e = resident_ctas<true, false, false>(p.grid, &r[0])) != cudaSuccess) return e;
+    if ((e = resident_ctas<false, false, false>(p.grid, &r[1])) != cudaSuccess) return e;
+    if ((e = resident_ctas<true, true, false>(p.grid, &r[2])) != cudaSuccess) return e;
+    if ((e = resident_ctas<false, true, false>(p.grid, &r[3])) != cudaSuccess) return e;
+    if ((e = resident_ctas<true, false, true>(p.grid, &r[4])) != cudaSuccess) return e;
+    if ((e = resident_ctas<true, true, true>(p.grid, &r[5])) != cudaSuccess) return e;
+    int m = r[0];
+    for (int i = 1; i < 6; ++i) m = min(m, r[i]);
+    resident[dev] = m;
     configured[dev] = 1;
   }
   if (p.grid > resident[dev]) return cudaErrorCooperativeLaunchTooLarge;
@@ -2028,12 +2039,16 @@ cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const bool fused = p.down_t != nullptr, traced = p.trace != nullptr;
-  if (fused) {
-    return traced ? cudaLaunchKernelEx(&cfg, decode_kernel<true, true>, p)
-                  : cudaLaunchKernelEx(&cfg, decode_kernel<true, false>, p);
+  if (fused && p.tp_size > 1) {
+    return traced ? cudaLaunchKernelEx(&cfg, decode_kernel<true, true, true>, p)
+                  : cudaLaunchKernelEx(&cfg, decode_kernel<true, false, true>, p);
   }
-  return traced ? cudaLaunchKernelEx(&cfg, decode_kernel<false, true>, p)
-                : cudaLaunchKernelEx(&cfg, decode_kernel<false, false>, p);
+  if (fused) {
+    return traced ? cudaLaunchKernelEx(&cfg, decode_kernel<true, true, false>, p)
+                  : cudaLaunchKernelEx(&cfg, decode_kernel<true, false, false>, p);
+  }
+  return traced ? cudaLaunchKernelEx(&cfg, decode_kernel<false, true, false>, p)
+                : cudaLaunchKernelEx(&cfg, decode_kernel<false, false, false>, p);
 }
 
 size_t decode_smem_bytes() { return kSmemBytes; }
