@@ -20,6 +20,7 @@ constexpr int kKVSize = kNKV * kHeadDim;       // 1024
 constexpr int kQKVRows = kQSize + 2 * kKVSize; // 4096
 constexpr int kVocab = 151936;
 constexpr int kMaxLayers = 28;
+static_assert(kMaxLayers <= 32, "split-attention tags carry the layer in 5 bits");
 constexpr float kEps = 1e-6f;
 
 // Execution shape: one CTA per SM, 8 consumer warps + 1 producer warp (at most
@@ -129,7 +130,6 @@ struct alignas(128) Workspace {
   // k=0 QKV done, 1 attention+o_proj done, 2 gate/up(+down) done, 3 down done
   // (separate-down schedule only).
   uint32_t sync[kMaxLayers][4][32];
-  uint32_t att_sync[kMaxLayers][kNKV][32];   // split attention partials published
   uint32_t arrive[32];                       // end-of-token arrivals (last one reduces)
   // Token broadcast (multi-token launches): word 0 = sequence (t + 1) in the low
   // 32 bits, the token id in the high 32 bits, published by one release store.
@@ -148,7 +148,9 @@ struct alignas(128) Workspace {
   // K/V append of (layer, KV head) published for a later token of the same
   // launch (two adds per token: the K and the V writer).
   uint32_t kv_ready[kMaxLayers][kNKV][32];
-  float att_part[kNKV][kMaxSplits][2][kHeadDim + 4];  // split attention (m, l, o[128])
+  // split attention partials as tagged words (value | tag << 32, the tag naming
+  // token and layer): o[128], then m and l, per (KV head, split, Q head)
+  uint64_t att_part[kNKV][kMaxSplits][2][kHeadDim + 2];
   float qkv[kQKVRows];
   // Raw QKV outputs of every layer as tagged words (value | tag << 32); the tag
   // of token t of a launch is tag_base + t + 1, so no reset is ever needed.
@@ -163,7 +165,8 @@ struct alignas(128) Workspace {
 // Fields read or cleared with 16-byte vector accesses.
 static_assert(offsetof(Workspace, acc_mid) % 16 == 0 && offsetof(Workspace, acc_down) % 16 == 0 &&
                   offsetof(Workspace, acc_x) % 16 == 0 &&
-                  offsetof(Workspace, resid) % 16 == 0 && offsetof(Workspace, qkv_tagged) % 16 == 0,
+                  offsetof(Workspace, resid) % 16 == 0 && offsetof(Workspace, qkv_tagged) % 16 == 0 &&
+                  offsetof(Workspace, att_part) % 16 == 0 && ((kHeadDim + 2) * 8) % 16 == 0,
               "workspace vector fields must be 16-byte aligned");
 
 // Scratch of the batched prefill (mkb_prefill.cu), owned by the engine; cap rows.

@@ -68,6 +68,7 @@ struct __align__(128) Smem {
   alignas(16) float mrx[32];  // the cluster partner's SwiGLU values (down projection)
   alignas(16) float apeer[2][kHeadDim + 4];  // the partner's attention partial: o[128], m, l per head
   alignas(16) float pbuf[kConsumerWarps][16];  // attention weights exchanged within a warp
+  alignas(16) float2 split_ml[2][kMaxSplits];   // m and l of every attention split (per Q head)
   float red[2 * kConsumerWarps];
   float best_v[kConsumerWarps];
   int best_i[kConsumerWarps];
@@ -1091,10 +1092,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&ws->stop_seen[0]) : "memory");
           if (old == static_cast<uint32_t>(G - 1)) {
             for (int i = 0; i < kMaxLayers * 4; ++i) ws->sync[i >> 2][i & 3][0] = 0u;
-            for (int i = 0; i < kMaxLayers * kNKV; ++i) {
-              ws->kv_ready[i / kNKV][i % kNKV][0] = 0u;
-              ws->att_sync[i / kNKV][i % kNKV][0] = 0u;
-            }
+            for (int i = 0; i < kMaxLayers * kNKV; ++i) ws->kv_ready[i / kNKV][i % kNKV][0] = 0u;
             ws->arrive[0] = 0u;
             ws->arrive_x[0] = 0u;
             ws->tag_base[0] = tag0 + static_cast<uint32_t>(t);
@@ -1223,6 +1221,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       // ================= BC: head norm + RoPE + KV append, attention, o_proj =====
       if (pl.in_bc) {
         const int h = pl.h;
+        const uint32_t stag = (tag << 5) | static_cast<uint32_t>(l);  // split partials: token and layer
         // Per-head norm weights and this position's RoPE row do not depend on
         // QKV: load them before polling. Lane owns dims 2l, 2l+1, 64+2l, 65+2l.
         float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f, cs0 = 0.f, sn0 = 0.f, cs1 = 0.f, sn1 = 0.f;
@@ -1462,12 +1461,11 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             } else if (splits <= 1) {
               sm.attn[tid] = O / L;
             } else {
-              float* dst = ws->att_part[h][pl.c][hh];
-              dst[d] = O;
-              if (d == 0) {
-                dst[kHeadDim] = M;
-                dst[kHeadDim + 1] = L;
-              }
+              // this split's partial as tagged words: no counter and no release,
+              // the readers poll the words themselves
+              uint64_t* dst = ws->att_part[h][pl.c][hh];
+              st_tagged(dst + d, O, stag);
+              if (d == 0) st_tagged2(dst + kHeadDim, M, L, stag);
             }
           }
           consumer_sync(kConsumerThreads);
@@ -1477,7 +1475,6 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             // expected bytes; the partner's next partial may land before or after)
             if (at_live && tid == 0) mbar_arrive_expect_tx(&sm.atbar, kPairAttnBytes);
           }
-          if (splits > 1 && tid == 0) release_add(&ws->att_sync[l][h][0], 1u);
         } else if (splits > 1 && pl.c < splits) {
           // The launch's split count comes from its longest cache: an earlier
           // token of the launch (a prefill, a generate that starts short) can
@@ -1485,28 +1482,49 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           // l = 0, o = 0), which the combine weighs by zero.
           if (tid < 2 * kHeadDim) {
             const int hh = tid >> 7, d = tid & (kHeadDim - 1);
-            float* dst = ws->att_part[h][pl.c][hh];
-            dst[d] = 0.f;
-            if (d == 0) {
-              dst[kHeadDim] = -INFINITY;
-              dst[kHeadDim + 1] = 0.f;
-            }
+            uint64_t* dst = ws->att_part[h][pl.c][hh];
+            st_tagged(dst + d, 0.f, stag);
+            if (d == 0) st_tagged2(dst + kHeadDim, -INFINITY, 0.f, stag);
           }
-          consumer_sync(kConsumerThreads);
-          if (tid == 0) release_add(&ws->att_sync[l][h][0], 1u);
         }
         if (splits > 1) {
-          transition_wait(c, tr, &ws->att_sync[l][h][0], static_cast<uint32_t>(splits * (t + 1)), l, kStSplit, t);
+          // every split's m and l: lane s of warp hh polls split s (one 16-byte
+          // word pair), shared through shared memory
+          tr.mark(kTrWaitBegin, kStSplit, l, t);
+          if (warp < 2 && lane < splits) {
+            float ms, ls;
+            poll_tagged2(c, &ws->att_part[h][lane][warp][kHeadDim], stag, ms, ls, l, t);
+            sm.split_ml[warp][lane] = make_float2(ms, ls);
+          }
+          consumer_sync(kConsumerThreads);
+          tr.mark(kTrWaitEnd, kStSplit, l, t);
           if (tid < 2 * kHeadDim) {
             const int hh = tid >> 7, d = tid & (kHeadDim - 1);
             float M = -INFINITY;
-            for (int s = 0; s < splits; ++s) M = fmaxf(M, __ldcg(&ws->att_part[h][s][hh][kHeadDim]));
+            for (int s = 0; s < splits; ++s) M = fmaxf(M, sm.split_ml[hh][s].x);
+            // o of every split, loaded in batches without a branch per word; a
+            // word not yet carrying the tag sends the thread to the polling loop
             float L = 0.f, O = 0.f;
+            bool all = true;
+#pragma unroll 8
             for (int s = 0; s < splits; ++s) {
-              const float ms = __ldcg(&ws->att_part[h][s][hh][kHeadDim]);
-              const float f = ms > -INFINITY ? ex2_approx(ms - M) : 0.f;
-              L = fmaf(__ldcg(&ws->att_part[h][s][hh][kHeadDim + 1]), f, L);
-              O = fmaf(__ldcg(&ws->att_part[h][s][hh][d]), f, O);
+              const float2 ml = sm.split_ml[hh][s];
+              const float f = ml.x > -INFINITY ? ex2_approx(ml.x - M) : 0.f;
+              const uint64_t w = ld_tagged(&ws->att_part[h][s][hh][d]);
+              all = all && static_cast<uint32_t>(w >> 32) == stag;
+              L = fmaf(ml.y, f, L);
+              O = fmaf(__uint_as_float(static_cast<uint32_t>(w)), f, O);
+            }
+            if (!all) {
+              O = 0.f;
+              for (int s = 0; s < splits; ++s) {
+                const float2 ml = sm.split_ml[hh][s];
+                const float f = ml.x > -INFINITY ? ex2_approx(ml.x - M) : 0.f;
+                float o, unused;
+                poll_tagged2(c, &ws->att_part[h][s][hh][d & ~1], stag, o, unused, l, t);
+                if (d & 1) o = unused;
+                O = fmaf(o, f, O);
+              }
             }
             sm.attn[tid] = O / L;
           }
@@ -1826,7 +1844,6 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       if (final_tok) {
         for (int i = tid; i < kMaxLayers * 4; i += kConsumerThreads) ws->sync[i >> 2][i & 3][0] = 0u;
         for (int i = tid; i < kMaxLayers * kNKV; i += kConsumerThreads) ws->kv_ready[i / kNKV][i % kNKV][0] = 0u;
-        for (int i = tid; i < kMaxLayers * kNKV; i += kConsumerThreads) ws->att_sync[i / kNKV][i % kNKV][0] = 0u;
       }
       consumer_sync(kConsumerThreads);
       if (tid == 0) {

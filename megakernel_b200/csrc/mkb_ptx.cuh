@@ -159,6 +159,17 @@ __device__ __forceinline__ void st_tagged(uint64_t* p, float v, uint32_t tag) {
   const uint64_t w = (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+// Two tagged words in one 16-byte store (p 16-byte aligned).
+__device__ __forceinline__ void st_tagged2(uint64_t* p, float v0, float v1, uint32_t tag) {
+  const uint64_t a = (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v0);
+  const uint64_t b = (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v1);
+  asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_tagged(const uint64_t* p) {
+  uint64_t a;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+  return a;
+}
 __device__ __forceinline__ void ld_tagged2(const uint64_t* p, uint64_t& a, uint64_t& b) {
   asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
