@@ -289,7 +289,10 @@ int mkb_plan_query(int grid, int cta, int32_t out[16]);
  * mapped to [Wq; Wk; Wv] rows by mkb_qkv_global_row. */
 int mkb_plan_query_tp(int grid, int cta, int tp_rank, int tp_size, int32_t out[16]);
 int mkb_qkv_global_row(int tp_rank, int tp_size, int local_row);
-int mkb_choose_splits(int max_cache_len, int group_size);
+/* Attention splits the kernel uses for a token at this cache length (when
+ * mkb_decode_args.splits is 0): 1 below 385 keys, else one split per 64-key
+ * chunk, at most group_size. */
+int mkb_choose_splits(int cache_len, int group_size);
 void mkb_key_range(int cache_len, int splits, int c, int32_t out[2]);
 /* Keys [out[0], out[1]) that CTA `cta` of a `grid`-CTA launch attends over at
  * this cache length (split across the head group, or halved between the two

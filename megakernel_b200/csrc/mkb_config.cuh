@@ -374,10 +374,17 @@ __host__ __device__ inline void attn_keys(int cache_len, int splits, int c, bool
   }
 }
 
-// Attention sequence splits for a launch whose longest cache is max_cache_len.
-__host__ __device__ inline int choose_splits(int max_cache_len, int group_size) {
-  if (max_cache_len <= 384) return 1;
-  int s = (max_cache_len + 255) / 256;
+// Attention sequence splits at a cache length: up to kSplitMinKeys - 1 keys
+// one range (halved between the CTAs of a cluster pair from kPairSplitKeys
+// on), beyond that ranges of at most one 64-key chunk over the head group's
+// CTAs (at most group_size of them), combined through tagged partials.
+// Measured per token against the pair split below 385 keys (split from 129 or
+// 257 keys on: +50 and +38 us/token at 200 and 300 keys) and against 256-key
+// ranges above (-74, -68 and -17 us/token at 450, 1,000 and 3,800 keys).
+constexpr int kSplitMinKeys = 385;
+__host__ __device__ inline int choose_splits(int cache_len, int group_size) {
+  if (cache_len < kSplitMinKeys) return 1;
+  int s = (cache_len + kKeysPerChunk - 1) / kKeysPerChunk;
   if (s > group_size) s = group_size;
   if (s > kMaxSplits) s = kMaxSplits;
   return s;

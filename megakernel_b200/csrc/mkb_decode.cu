@@ -432,13 +432,14 @@ struct Producer {
 
 template <bool kFused, bool kTraced, bool kTP>
 __device__ void producer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int pos0, int cl0,
-                             int splits) {
+                             int splits0) {
   Producer pr(c);
   const TpShape tp = tp_shape(kTP ? p.tp_rank : 0, kTP ? p.tp_size : 1, kVocab);
   const bool pair_attn = pair_shares_head(static_cast<int>(blockIdx.x), p.grid, p.group_size, tp);
   for (int t = 0; t < p.n_tokens && !pr.stop; ++t) {
     const int pos = pos0 + t;
     const int cl = cl0 + t;
+    const int splits = splits0 > 0 ? splits0 : choose_splits(cl, p.group_size);
     for (int l = p.layer_begin; l < p.layer_end && !pr.stop; ++l) {
       // A: QKV rows, one bulk copy per row into a padded row slot
       for (int r = pl.qa; r < pl.qb;) {
@@ -1013,7 +1014,7 @@ __device__ __forceinline__ void down_sums(const DecodeParams& p, int tps, const 
 
 template <bool kFused, bool kTraced, bool kTP>
 __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c, int token0, int pos0, int cl0,
-                             int splits, uint32_t tag0) {
+                             int splits0, uint32_t tag0) {
   Smem& sm = *c.sm;
   Workspace* ws = p.ws;
   const int tid = threadIdx.x;
@@ -1063,6 +1064,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   for (int t = 0; t < p.n_tokens; ++t) {
     const int pos = pos0 + t;
     const int cl = cl0 + t;
+    // attention splits of this token (every split range holds keys; a fixed
+    // count from the caller may leave some empty)
+    const int splits = splits0 > 0 ? splits0 : choose_splits(cl, p.group_size);
     const uint32_t tgtG = static_cast<uint32_t>(G * (t + 1));
     const uint32_t tag = tag0 + static_cast<uint32_t>(t) + 1u;
     tr.mark(kTrMark, kStToken, 0, t);
@@ -1947,14 +1951,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeParams 
   }
   __syncthreads();
 
-  // Attention splits: fixed for the launch, from its longest cache (the step
-  // state may supply the position, so this is decided on the device).
+  // Attention splits: a fixed count from the caller, or chosen per token from
+  // its cache length (0 here).
   const int last_cl = cl + p.n_tokens - 1;
-  const int splits = p.splits > 0 ? p.splits : choose_splits(last_cl, p.group_size);
+  const int splits = p.splits > 0 ? p.splits : 0;
   // Argument guard (uniform over the grid, before any wait).
   if (token < 0 || token >= kVocab || pos < 0 || pos + p.n_tokens > p.max_seq || cl < 1 ||
       last_cl > p.max_seq || p.grid != static_cast<int>(gridDim.x) || p.grid > kMaxGrid || p.grid < kMinGrid ||
-      p.group_size * (kNKV / max(p.tp_size, 1)) > p.grid || p.grid % kCluster != 0 || splits < 1 ||
+      p.group_size * (kNKV / max(p.tp_size, 1)) > p.grid || p.grid % kCluster != 0 || splits < 0 ||
       splits > kMaxSplits || (splits > 1 && splits > p.group_size) || misaligned || !tp_ok) {
     if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(c, kErrBadArgs, -1, -1, -1);
     // nothing was read or appended; the outputs say so

@@ -154,7 +154,7 @@ cudaError_t to_params(const mkb_decode_args* a, DecodeParams* p, DeviceInfo** df
     p->peer_ws[0] = w;
   }
   p->group_size = p->grid / (kNKV / p->tp_size);
-  p->splits = a->splits > 0 ? a->splits : 0;  // 0: chosen on the device per launch
+  p->splits = a->splits > 0 ? a->splits : 0;  // 0: chosen on the device per token
   if (p->splits > kMaxSplits || p->splits > p->group_size) return cudaErrorInvalidValue;
   p->timeout_ns = a->timeout_ns ? a->timeout_ns : kDefaultTimeoutNs;
   p->withhold_cta = a->withhold_cta;
@@ -320,7 +320,7 @@ int mkb_plan_query(int grid, int cta, int32_t out[16]) {
   for (int i = 0; i < 14; ++i) out[i] = v[i];
   return 0;
 }
-int mkb_choose_splits(int max_cache_len, int group_size) { return choose_splits(max_cache_len, group_size); }
+int mkb_choose_splits(int cache_len, int group_size) { return choose_splits(cache_len, group_size); }
 void mkb_key_range(int cache_len, int splits, int c, int32_t out[2]) {
   int a, b;
   key_range(cache_len, splits, c, &a, &b);
