@@ -1064,9 +1064,6 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
   for (int t = 0; t < p.n_tokens; ++t) {
     const int pos = pos0 + t;
     const int cl = cl0 + t;
-    // attention splits of this token (every split range holds keys; a fixed
-    // count from the caller may leave some empty)
-    const int splits = splits0 > 0 ? splits0 : choose_splits(cl, p.group_size);
     const uint32_t tgtG = static_cast<uint32_t>(G * (t + 1));
     const uint32_t tag = tag0 + static_cast<uint32_t>(t) + 1u;
     tr.mark(kTrMark, kStToken, 0, t);
@@ -1226,6 +1223,9 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
       if (pl.in_bc) {
         const int h = pl.h;
         const uint32_t stag = (tag << 5) | static_cast<uint32_t>(l);  // split partials: token and layer
+        // attention splits of this token (every split range holds keys; a fixed
+        // count from the caller may leave some empty)
+        const int splits = splits0 > 0 ? splits0 : choose_splits(cl, p.group_size);
         // Per-head norm weights and this position's RoPE row do not depend on
         // QKV: load them before polling. Lane owns dims 2l, 2l+1, 64+2l, 65+2l.
         float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f, cs0 = 0.f, sn0 = 0.f, cs1 = 0.f, sn1 = 0.f;
