@@ -19,8 +19,10 @@
 // the accuracy of the decode path's GEMVs.
 //
 // Attention (attn_kernel): causal flash attention on the warp-level tensor-core
-// MMA (mma.sync m16n8k16), q and p split the same way, K/V read back from the
-// BF16 cache the kernel before wrote, online softmax in the exp2 domain.
+// MMA (mma.sync m16n8k16), q split into a BF16 high part and remainder (the
+// scores keep ~16 bits of q), the probabilities in [0, 1] as one BF16 operand,
+// K/V read back from the BF16 cache the kernel before wrote (double-buffered
+// cp.async tiles), online softmax in the exp2 domain.
 
 #include <cstdint>
 #include <cstdio>
@@ -303,14 +305,30 @@ __global__ void qk_rope_kernel(const float* __restrict__ qkv, const __nv_bfloat1
 // mma.sync m16n8k16 (BF16 in, FP32 out) with Q and P split into high part +
 // remainder; K/V tiles of 64 keys in padded shared rows (conflict-free ldmatrix).
 constexpr int kAttRow = kHeadDim + 8;  // 136 BF16 = 272 bytes per shared K/V row
+// K/V tiles double-buffered: the next 64 keys are copied (cp.async, 16 bytes a
+// thread at a time) while the tensor cores work on the current ones.
+constexpr int kAttStages = 2;
+constexpr size_t kAttSmem = size_t(kAttStages) * 2 * 64 * kAttRow * 2;  // 69,632 B
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __global__ void __launch_bounds__(128) attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
                                                    const __nv_bfloat16* __restrict__ vc, int n, int pos0, int layer,
                                                    int max_seq, __nv_bfloat16* oh, __nv_bfloat16* ol) {
-  __shared__ __align__(16) __nv_bfloat16 ks[64][kAttRow];
-  __shared__ __align__(16) __nv_bfloat16 vs[64][kAttRow];
+  extern __shared__ __align__(16) uint8_t att_smem[];
+  auto ks = reinterpret_cast<__nv_bfloat16(*)[64][kAttRow]>(att_smem);
+  auto vs = reinterpret_cast<__nv_bfloat16(*)[64][kAttRow]>(att_smem + size_t(kAttStages) * 64 * kAttRow * 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hq = blockIdx.y, hk = hq >> 1;
-  const int i0 = blockIdx.x * 64;
+  // causal work grows with the query block: the longest blocks go first, so
+  // the short ones fill the tail of the grid
+  const int i0 = (gridDim.x - 1 - blockIdx.x) * 64;
   const int g = lane >> 2, tq = lane & 3;
   const int r0 = i0 + warp * 16 + g, r1 = r0 + 8;  // this thread's two query rows (tokens)
   // Q fragments (A operand), high part and remainder, for the 8 k-steps of 16 dims
@@ -336,15 +354,26 @@ __global__ void __launch_bounds__(128) attn_kernel(const float* __restrict__ q, 
   float m0r = -INFINITY, m1r = -INFINITY, l0 = 0.f, l1 = 0.f;
   const int last_key = pos0 + min(i0 + 63, n - 1);  // the block's last query attends up to here
   const size_t head_base = ((size_t)layer * kNKV + hk) * max_seq;
-  for (int k0 = 0; k0 <= last_key; k0 += 64) {
-    __syncthreads();
-    // K and V rows k0 .. k0 + 63 (rows past the last key are loaded from the
-    // cache as they are and masked below)
+  // K and V rows k0 .. k0 + 63 into stage st (rows past the last key are
+  // copied from the cache as they are and masked below)
+  auto load_tile = [&](int k0, int st) {
     for (int e = threadIdx.x; e < 64 * 16; e += 128) {
       const int r = e >> 4, cidx = (e & 15) * 8;
       const int key = min(k0 + r, max_seq - 1);
-      *reinterpret_cast<uint4*>(&ks[r][cidx]) = *reinterpret_cast<const uint4*>(kc + (head_base + key) * kHeadDim + cidx);
-      *reinterpret_cast<uint4*>(&vs[r][cidx]) = *reinterpret_cast<const uint4*>(vc + (head_base + key) * kHeadDim + cidx);
+      cp_async16(&ks[st][r][cidx], kc + (head_base + key) * kHeadDim + cidx);
+      cp_async16(&vs[st][r][cidx], vc + (head_base + key) * kHeadDim + cidx);
+    }
+    cp_async_commit();
+  };
+  const int ntiles = last_key / 64 + 1;
+  load_tile(0, 0);
+  for (int it = 0; it < ntiles; ++it) {
+    const int k0 = it * 64, st = it & 1;
+    if (it + 1 < ntiles) {
+      load_tile(k0 + 64, st ^ 1);
+      cp_async_wait<1>();  // this tile's group has landed; the next one stays in flight
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
     // S = Q K^T for 8 n-tiles of 8 keys
@@ -356,7 +385,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const float* __restrict__ q, 
       for (int s2 = 0; s2 < 4; ++s2) {  // two k-steps per ldmatrix.x4
         uint32_t b0, b1, b2, b3;
         const int key = 8 * j + (lane & 7), dim = 32 * s2 + 8 * (lane >> 3);
-        ldsm_x4(smem_addr(&ks[key][dim]), b0, b1, b2, b3);
+        ldsm_x4(smem_addr(&ks[st][key][dim]), b0, b1, b2, b3);
         mma_bf16(sacc[j], qa_h[2 * s2][0], qa_h[2 * s2][1], qa_h[2 * s2][2], qa_h[2 * s2][3], b0, b1);
         mma_bf16(sacc[j], qa_l[2 * s2][0], qa_l[2 * s2][1], qa_l[2 * s2][2], qa_l[2 * s2][3], b0, b1);
         mma_bf16(sacc[j], qa_h[2 * s2 + 1][0], qa_h[2 * s2 + 1][1], qa_h[2 * s2 + 1][2], qa_h[2 * s2 + 1][3], b2, b3);
@@ -412,24 +441,19 @@ __global__ void __launch_bounds__(128) attn_kernel(const float* __restrict__ q, 
       const float* pa = sacc[2 * s];
       const float* pb = sacc[2 * s + 1];
       const float pv[8] = {pa[0], pa[1], pa[2], pa[3], pb[0], pb[1], pb[2], pb[3]};
-      uint32_t ah[4], al[4];
+      uint32_t ah[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t h = pack_bf2(pv[2 * k], pv[2 * k + 1]);
-        ah[k] = h;
-        al[k] = pack_bf2(pv[2 * k] - bf_lo(h), pv[2 * k + 1] - bf_hi(h));
-      }
+      for (int k = 0; k < 4; ++k) ah[k] = pack_bf2(pv[2 * k], pv[2 * k + 1]);
 #pragma unroll
       for (int j2 = 0; j2 < 8; ++j2) {  // two n-tiles of 8 dims per ldmatrix.x4.trans
         uint32_t b0, b1, b2, b3;
         const int key = 16 * s + (lane & 7) + 8 * ((lane >> 3) & 1), dim = 16 * j2 + 8 * (lane >> 4);
-        ldsm_x4_trans(smem_addr(&vs[key][dim]), b0, b1, b2, b3);
+        ldsm_x4_trans(smem_addr(&vs[st][key][dim]), b0, b1, b2, b3);
         mma_bf16(o[2 * j2], ah[0], ah[1], ah[2], ah[3], b0, b1);
-        mma_bf16(o[2 * j2], al[0], al[1], al[2], al[3], b0, b1);
         mma_bf16(o[2 * j2 + 1], ah[0], ah[1], ah[2], ah[3], b2, b3);
-        mma_bf16(o[2 * j2 + 1], al[0], al[1], al[2], al[3], b2, b3);
       }
     }
+    __syncthreads();  // every warp is done with stage st before it is refilled
   }
   // O / l -> high part and remainder of the o_proj A operand
   const float inv0 = 1.f / l0, inv1 = 1.f / l1;
@@ -513,7 +537,8 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
                            int max_seq, const int* ids, int n, int pos0, const PrefillScratch& s, cudaStream_t stream) {
   using namespace pf;
   if (n < 1 || n > s.cap || pos0 < 0 || pos0 + n > max_seq) return cudaErrorInvalidValue;
-  cudaError_t e;
+  cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttSmem);
+  if (e != cudaSuccess) return e;
   embed_kernel<<<n, kHidden / 4, 0, stream>>>(ids, embed, s.h);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   // activation operand maps over the scratch (K = 1024, 2048 or 3072 columns)
@@ -555,7 +580,7 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
     qk_rope_kernel<<<dim3(n, 4), 256, 0, stream>>>(s.qkv, w.q_norm_weight, w.k_norm_weight, cos_t, sin_t, rope_fp32,
                                                    pos0, l, kc, vc, max_seq, s.q);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    attn_kernel<<<dim3((n + 63) / 64, kNQ), 128, 0, stream>>>(s.q, kc, vc, n, pos0, l, max_seq, s.ah, s.al);
+    attn_kernel<<<dim3((n + 63) / 64, kNQ), 128, kAttSmem, stream>>>(s.q, kc, vc, n, pos0, l, max_seq, s.ah, s.al);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     // o_proj added into the residual
     g.K = kQSize;
