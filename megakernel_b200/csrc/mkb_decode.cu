@@ -835,28 +835,6 @@ __device__ __forceinline__ float acc_value(const uint64_t* w, int copies, uint32
   count = static_cast<uint32_t>(cnt);
   return acc_decode(low, cnt);
 }
-// Bounded poll of one element until it holds `expect` contributions.
-__device__ __noinline__ float acc_wait_slow(const Ctl c, const uint64_t* w, int copies, uint32_t expect, int layer,
-                                            int stage, int tok, bool sys) {
-  const uint64_t t0 = global_ns();
-  uint32_t it = 0, cnt = 0;
-  float v = 0.f;
-  while (true) {
-    v = acc_value(w, copies, cnt, sys);
-    if (cnt == expect) break;
-    if ((++it & 15u) == 0u) {
-      if (aborted(c) || ld_relaxed(&c.ws->error[0]) != 0u) {
-        *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
-        break;
-      }
-      if (global_ns() - t0 > c.timeout) {
-        raise_error(c, kErrTimeoutTransition, layer, stage, tok);
-        break;
-      }
-    }
-  }
-  return v;
-}
 // Bounded poll by one thread until elements e0 and e1 of an accumulator row
 // (e1 < 0: e0 only) both hold `expect` contributions; both are loaded in every
 // round, so the second costs no extra round trip.
@@ -887,7 +865,46 @@ __device__ __noinline__ void acc_wait_pair(const Ctl c, const uint64_t* row, int
 // another warp the same element of copy 1 when there is one, and the others
 // wait at a barrier: every poll competes with the atomics landing on the same
 // L2 lines, so the fewer poll loads the faster the exchange (measured).
-// Elements still incomplete after the barrier are polled by their owners.
+// Elements still incomplete after the barrier are polled by their owners, all
+// four together (one round trip per poll, not one per element).
+__device__ __noinline__ void acc_wait4_slow(const Ctl c, const uint64_t* w, int copies, uint32_t expect, float* v,
+                                            int layer, int stage, int tok, bool sys) {
+  const uint64_t t0 = global_ns();
+  uint32_t it = 0;
+  while (true) {
+    uint64_t low[4] = {0, 0, 0, 0}, cn[4] = {0, 0, 0, 0};
+    for (int q = 0; q < copies; ++q) {
+      uint64_t a, b, x, y;
+      if (sys) {
+        ld_relaxed2_sys(w + q * kHidden, a, b);
+        ld_relaxed2_sys(w + q * kHidden + 2, x, y);
+      } else {
+        ld_tagged2(w + q * kHidden, a, b);
+        ld_tagged2(w + q * kHidden + 2, x, y);
+      }
+      cn[0] += a >> 56; low[0] += a & kAccLowMask;
+      cn[1] += b >> 56; low[1] += b & kAccLowMask;
+      cn[2] += x >> 56; low[2] += x & kAccLowMask;
+      cn[3] += y >> 56; low[3] += y & kAccLowMask;
+    }
+    bool done = true;
+    for (int i = 0; i < 4; ++i) {
+      v[i] = acc_decode(low[i], cn[i]);
+      done = done && cn[i] == expect;
+    }
+    if (done) return;
+    if ((++it & 15u) == 0u) {
+      if (aborted(c) || ld_relaxed(&c.ws->error[0]) != 0u) {
+        *reinterpret_cast<volatile int*>(&c.sm->abort) = 1;
+        return;
+      }
+      if (global_ns() - t0 > c.timeout) {
+        raise_error(c, kErrTimeoutTransition, layer, stage, tok);
+        return;
+      }
+    }
+  }
+}
 __device__ __forceinline__ void acc_wait4(const Ctl& c, const uint64_t* row, int copies, uint32_t expect,
                                           uint32_t expect0, int s0, float v[4], int layer, int stage, int tok,
                                           bool sys = false) {
@@ -911,10 +928,14 @@ __device__ __forceinline__ void acc_wait4(const Ctl& c, const uint64_t* row, int
     cn[2] += x >> 56; low[2] += x & kAccLowMask;
     cn[3] += y >> 56; low[3] += y & kAccLowMask;
   }
+  if (cn[0] == expect && cn[1] == expect && cn[2] == expect && cn[3] == expect) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[i] = acc_decode(low[i], cn[i]);
-    if (cn[i] != expect) v[i] = acc_wait_slow(c, w + i, copies, expect, layer, stage, tok, sys);
+    for (int i = 0; i < 4; ++i) v[i] = acc_decode(low[i], cn[i]);
+  } else {
+    float u[4];
+    acc_wait4_slow(c, w, copies, expect, u, layer, stage, tok, sys);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = u[i];
   }
 }
 // Clear this thread's 4 elements of an accumulator row.
@@ -1248,8 +1269,24 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           float x0, x1, x2, x3;  // dims d0, d0+1, d0+64, d0+65
           // every lane polls its own words: a single poller per warp followed by
           // the lanes' reads cost one more L2 round trip (+8.7 us per token measured)
-          poll_tagged2(c, &ws->qkv_tagged[l][base + d0], tag, x0, x1, l, t);
-          poll_tagged2(c, &ws->qkv_tagged[l][base + d0 + 64], tag, x2, x3, l, t);
+          // both word pairs are loaded before either is checked (one L2 round
+          // trip when they are already there, not two)
+          {
+            uint64_t a, b, e, f;
+            ld_tagged2(&ws->qkv_tagged[l][base + d0], a, b);
+            ld_tagged2(&ws->qkv_tagged[l][base + d0 + 64], e, f);
+            const bool ok = static_cast<uint32_t>(a >> 32) == tag && static_cast<uint32_t>(b >> 32) == tag &&
+                            static_cast<uint32_t>(e >> 32) == tag && static_cast<uint32_t>(f >> 32) == tag;
+            if (ok) {
+              x0 = __uint_as_float(static_cast<uint32_t>(a));
+              x1 = __uint_as_float(static_cast<uint32_t>(b));
+              x2 = __uint_as_float(static_cast<uint32_t>(e));
+              x3 = __uint_as_float(static_cast<uint32_t>(f));
+            } else {
+              poll_tagged2(c, &ws->qkv_tagged[l][base + d0], tag, x0, x1, l, t);
+              poll_tagged2(c, &ws->qkv_tagged[l][base + d0 + 64], tag, x2, x3, l, t);
+            }
+          }
           if (warp < 3) {
             // q_norm / k_norm + rotate-half RoPE (megakernel.cu:490-630)
             const float ss = warp_sum(x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3);
