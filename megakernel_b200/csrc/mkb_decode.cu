@@ -16,7 +16,8 @@
 //        DE : post RMSNorm + gate/up SwiGLU rows, SwiGLU values swapped with
 //             the cluster partner (st.async), down partial of this CTA's 512
 //             output columns over both CTAs' rows of the transposed down
-//             weight -> counted red.add into acc_down (complete at G/2 adds)
+//             weight (mma.sync, ldmatrix.trans) -> counted red.add into
+//             acc_down (complete at G/2 adds)
 //        (reference-layout down weight: D writes the SwiGLU vector and
 //         publishes a counter, E computes whole down rows and writes the
 //         residual, then publishes the next counter)
@@ -967,7 +968,7 @@ __device__ __forceinline__ void acc_add(const DecodeParams& p, int tps, uint64_t
     if (g < tps) red_add_u64_sys(peer_field(p, g, local), term);
 }
 
-static_assert(kCluster == 2 && kSlice == 2 * kConsumerThreads, "down projection: two columns per thread");
+static_assert(kCluster == 2 && kSlice == 64 * kConsumerWarps, "down projection: 64 output columns per warp");
 // bytes of one pair attention exchange: o[128], m and l for each of the two heads
 constexpr uint32_t kPairAttnBytes = 2u * (kHeadDim + 2) * 4u;
 static_assert(2 * kHeadDim == kConsumerThreads, "one consumer thread per (head, dim) in the combine");
