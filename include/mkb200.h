@@ -172,6 +172,12 @@ cudaError_t mkb_workspace_reset(void* workspace, cudaStream_t stream);
 /* Synchronous read of the in-kernel status: out[0] error code (0 = ok),
  * out[1] CTA, out[2] layer, out[3] stage, out[4] token. */
 cudaError_t mkb_workspace_status(const void* workspace, uint32_t out[8]);
+/* Read (and, when `set` is not NULL, first write) the workspace's tag base: the
+ * tag of the last token decoded, from which tagged words are stamped. The
+ * kernel restarts it at 0 (clearing every tagged word) once it passes 2^26;
+ * writing it lets a test reach that point. Synchronous; no launch may be in
+ * flight on the workspace. */
+cudaError_t mkb_workspace_tag_base(void* workspace, const uint32_t* set, uint32_t* get);
 /* The per-device workspace used when mkb_decode_args.workspace is NULL and by
  * launch_decode_kernel (allocated and zeroed on first use). */
 cudaError_t mkb_default_workspace(int device, void** out);

@@ -115,6 +115,7 @@ SIGNATURES = [
     ("mkb_workspace_bytes", c_size_t, []),
     ("mkb_workspace_reset", c_int, [c_void_p, c_void_p]),
     ("mkb_workspace_status", c_int, [c_void_p, POINTER(c_uint32)]),
+    ("mkb_workspace_tag_base", c_int, [c_void_p, POINTER(c_uint32), POINTER(c_uint32)]),
     ("mkb_default_workspace", c_int, [c_int, POINTER(c_void_p)]),
     ("mkb_error_name", c_char_p, [c_uint32]),
     ("mkb_transpose_down", c_int, [c_void_p, c_void_p, c_void_p]),

@@ -199,6 +199,22 @@ __device__ __forceinline__ uint64_t tok_word(int t, int token) {
   return (static_cast<uint64_t>(static_cast<uint32_t>(token)) << 32) | static_cast<uint32_t>(t + 1);
 }
 
+// The tag base the next launch starts from (one thread, at the end of a launch,
+// when no CTA reads tagged words any more). The split-attention tags carry the
+// layer in their low 5 bits ((tag << 5) | layer), so they would repeat after
+// 2^27 tokens; long before that every tagged word is cleared and the tags
+// restart, so a stale word can never carry a current tag (once per 2^26 tokens,
+// a few hundred microseconds).
+constexpr uint32_t kTagRestart = 1u << 26;
+__device__ __noinline__ uint32_t next_tag_base(Workspace* ws, uint32_t next) {
+  if (next < kTagRestart) return next;
+  ulonglong2* a = reinterpret_cast<ulonglong2*>(&ws->qkv_tagged[0][0]);
+  for (size_t i = 0; i < sizeof(ws->qkv_tagged) / sizeof(ulonglong2); ++i) a[i] = make_ulonglong2(0ull, 0ull);
+  ulonglong2* b = reinterpret_cast<ulonglong2*>(&ws->att_part[0][0][0][0]);
+  for (size_t i = 0; i < sizeof(ws->att_part) / sizeof(ulonglong2); ++i) b[i] = make_ulonglong2(0ull, 0ull);
+  return 0u;
+}
+
 // spin_geq on a counter that other GPUs add into (tensor parallel).
 __device__ __noinline__ void spin_geq_sys(const Ctl c, const uint32_t* ctr, uint32_t target, uint32_t code,
                                           int layer, int stage, int tok) {
@@ -1118,7 +1134,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
             for (int i = 0; i < kMaxLayers * kNKV; ++i) ws->kv_ready[i / kNKV][i % kNKV][0] = 0u;
             ws->arrive[0] = 0u;
             ws->arrive_x[0] = 0u;
-            ws->tag_base[0] = tag0 + static_cast<uint32_t>(t);
+            ws->tag_base[0] = next_tag_base(ws, tag0 + static_cast<uint32_t>(t));
             ws->stop_seen[0] = 0u;
             ws->tok_flag[0] = 0ull;
           }
@@ -1906,7 +1922,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           ws->arrive[0] = 0u;
           ws->arrive_x[0] = 0u;
           ws->tok_flag[0] = 0ull;
-          ws->tag_base[0] = tag0 + static_cast<uint32_t>(p.n_tokens);
+          ws->tag_base[0] = next_tag_base(ws, tag0 + static_cast<uint32_t>(p.n_tokens));
         } else if (serve) {
           // the host decides the next token (the mailbox), not the argmax
         } else if (stop_now) {
@@ -1914,7 +1930,7 @@ __device__ void consumer_run(const DecodeParams& p, const Plan& pl, const Ctl& c
           // still carries the stop id to the others (cleared by the last to see it)
           ws->arrive[0] = 0u;
           ws->arrive_x[0] = 0u;
-          ws->tag_base[0] = tag0 + static_cast<uint32_t>(t) + 1u;
+          ws->tag_base[0] = next_tag_base(ws, tag0 + static_cast<uint32_t>(t) + 1u);
           st_release_u64(&ws->tok_flag[0], tok_word(t, best));
         } else {
           st_release_u64(&ws->tok_flag[0], tok_word(t, best));  // covers the CTA's writes above

@@ -293,6 +293,15 @@ cudaError_t mkb_workspace_status(const void* workspace, uint32_t out[8]) {
   return cudaMemcpy(out, w->error, 8 * sizeof(uint32_t), cudaMemcpyDeviceToHost);
 }
 
+cudaError_t mkb_workspace_tag_base(void* workspace, const uint32_t* set, uint32_t* get) {
+  if (workspace == nullptr) return cudaErrorInvalidValue;
+  Workspace* w = static_cast<Workspace*>(workspace);
+  cudaError_t e = cudaSuccess;
+  if (set != nullptr) e = cudaMemcpy(w->tag_base, set, sizeof(uint32_t), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && get != nullptr) e = cudaMemcpy(get, w->tag_base, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  return e;
+}
+
 const char* mkb_error_name(uint32_t code) {
   switch (code) {
     case kErrNone: return "ok";

@@ -440,6 +440,36 @@ def test_generate_stops_on_stop_token(w_gpu, hf_model, config0_hf):
     eng.close()
 
 
+def test_tag_restart_keeps_results(w_gpu):
+    """Tagged words (QKV hand-off, split-attention partials) carry the token in
+    their tag, the split partials as (tag << 5) | layer. Before those could
+    repeat (2^27 tokens) the kernel clears every tagged word and restarts the
+    tag base at 0: a launch that crosses that point and the launch after it
+    decode exactly what a fresh workspace does (cache 1,000+: split attention)."""
+    from ctypes import byref, c_uint32, c_void_p
+    gen = torch.Generator(device=DEV).manual_seed(11)
+    kg = torch.randn((28, 8, 1024, 128), generator=gen, device=DEV).to(torch.bfloat16)
+    vg = torch.randn((28, 8, 1024, 128), generator=gen, device=DEV).to(torch.bfloat16)
+    k0, v0 = kg.clone(), vg.clone()
+    eng = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), kg, vg)
+    ref = eng.generate(1234, 1000, 8).cpu().tolist()
+    kref = kg.clone()
+    lib = _lib.load()
+    ws = c_void_p(eng.workspace_ptr)
+    start = c_uint32((1 << 26) - 3)
+    _lib.check(lib.mkb_workspace_tag_base(ws, byref(start), None), "mkb_workspace_tag_base")
+    for _ in range(2):  # across the restart, then from tag 0
+        kg.copy_(k0)
+        vg.copy_(v0)
+        assert eng.generate(1234, 1000, 8).cpu().tolist() == ref
+        assert torch.equal(kg, kref)
+        now = c_uint32(1)
+        _lib.check(lib.mkb_workspace_tag_base(ws, None, byref(now)), "mkb_workspace_tag_base")
+        assert now.value < (1 << 26)
+    assert eng.status()[0] == 0
+    eng.close()
+
+
 def test_serve_session_matches_generate(w_gpu, hf_model, config0_hf):
     """A serve session (one persistent launch, each input token handed over by
     the host through pinned memory) decodes exactly what a generate launch does
