@@ -739,6 +739,14 @@ cudaError_t mkb_gemm_bf16_split(const void* a_hi, const void* a_lo, const void* 
                     static_cast<const __nv_bfloat16*>(b), c, m, n, k, nullptr, stream);
 }
 
+// Serve mailbox and result words: {seq, value} written and read as one 8-byte
+// word of pinned, mapped memory (the device reads and writes them the same way).
+static inline void put_pair(volatile int* p, int seq, int value) {
+  *reinterpret_cast<volatile uint64_t*>(p) =
+      (static_cast<uint64_t>(static_cast<uint32_t>(value)) << 32) | static_cast<uint32_t>(seq);
+}
+static inline uint64_t get_pair(volatile int* p) { return *reinterpret_cast<volatile uint64_t*>(p); }
+
 cudaError_t mkb_engine_serve_open(mkb_engine* e, int position, int max_tokens, unsigned long long timeout_ns,
                                   cudaStream_t stream) {
   if (!e || e->serving || max_tokens < 1 || position < 0 || position + max_tokens > e->max_seq)
@@ -747,10 +755,8 @@ cudaError_t mkb_engine_serve_open(mkb_engine* e, int position, int max_tokens, u
   cudaError_t err = engine_report_earlier(e, stream);
   if (err != cudaSuccess) return err;
   volatile int* io = e->h_io;
-  io[2] = 0;
-  io[3] = 0;
-  io[6] = 0;
-  io[7] = -1;
+  put_pair(io + 2, 0, 0);
+  put_pair(io + 6, 0, -1);
   mkb_decode_args a = e->step_args;
   a.step = nullptr;
   a.token = 0;  // every input comes from the mailbox
@@ -776,11 +782,7 @@ namespace {
 // it, and reports an in-kernel failure (workspace reset) as cudaErrorLaunchFailure.
 cudaError_t serve_finish(mkb_engine* e) {
   volatile int* io = e->h_io;
-  if (e->serve_seq < e->serve_max) {
-    io[3] = -1;
-    std::atomic_thread_fence(std::memory_order_seq_cst);
-    io[2] = e->serve_seq + 1;
-  }
+  if (e->serve_seq < e->serve_max) put_pair(io + 2, e->serve_seq + 1, -1);  // ends the launch
   e->serving = false;
   cudaError_t err = cudaStreamSynchronize(e->serve_stream);
   if (err != cudaSuccess) return err;
@@ -797,20 +799,18 @@ cudaError_t mkb_engine_serve_step(mkb_engine* e, int token, int* next_token) {
   if (token < 0 || token >= kVocab) return cudaErrorInvalidValue;
   volatile int* io = e->h_io;
   const int seq = ++e->serve_seq;
-  io[3] = token;
-  std::atomic_thread_fence(std::memory_order_seq_cst);  // the token before its sequence number
-  io[2] = seq;
+  put_pair(io + 2, seq, token);  // {seq, token} in one 8-byte store
   // the launch answers within a token's time; give up after the session timeout
   const auto t0 = std::chrono::steady_clock::now();
-  while (io[6] != seq) {
+  uint64_t r;
+  while (static_cast<int>(static_cast<uint32_t>(r = get_pair(io + 6))) != seq) {
     if (io[5] != 0 ||
         std::chrono::steady_clock::now() - t0 > std::chrono::nanoseconds(2 * e->serve_timeout)) {
       const cudaError_t st = serve_finish(e);
       return st != cudaSuccess ? st : cudaErrorLaunchFailure;
     }
   }
-  std::atomic_thread_fence(std::memory_order_seq_cst);
-  if (next_token) *next_token = io[7];
+  if (next_token) *next_token = static_cast<int>(static_cast<uint32_t>(r >> 32));
   if (seq == e->serve_max) return serve_finish(e);  // the launch ends after its last token
   return cudaSuccess;
 }
