@@ -265,7 +265,8 @@ cudaError_t mkb_engine_prefill_batched(mkb_engine* e, const int* prompt_tokens, 
                                       cudaStream_t stream);
 /* The prefill's GEMM on its own: c[m, n] (FP32, row-major) = (a_hi + a_lo)[m, k]
  * b[n, k]^T with a_hi / a_lo / b BF16 row-major (16-byte aligned), n a multiple
- * of 128, k a multiple of 64. Asynchronous. */
+ * of 128 (256-column tiles when n is a multiple of 256), k a multiple of 64.
+ * Asynchronous. */
 cudaError_t mkb_gemm_bf16_split(const void* a_hi, const void* a_lo, const void* b, float* c, int m, int n, int k,
                                 cudaStream_t stream);
 float* mkb_engine_logits(mkb_engine* e);   /* device [vocab], last token's logits */

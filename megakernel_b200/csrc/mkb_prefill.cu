@@ -38,21 +38,31 @@
 namespace mkb {
 namespace pf {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4;
-constexpr int kTile = BM * BK * 2;  // 16 KB: one 128 x 64 BF16 operand tile
+constexpr int BM = 128, BK = 64;
+constexpr int kTile = BM * BK * 2;  // 16 KB: one 128 x 64 BF16 A-operand tile
 constexpr int kGemmThreads = 192;   // warp 0 TMA, warp 1 MMA (+ TMEM), warps 2-5 epilogue
 
+// Output tiles of BM x kBN: kBN = 256 (N a multiple of 256, 3 stages of 64 KB)
+// reads 1.5x fewer operand bytes per FLOP than kBN = 128 (4 stages of 48 KB).
+template <int kBN>
+struct GemmCfg {
+  static constexpr int kStages = kBN == 256 ? 3 : 4;
+  static constexpr int kTileB = kBN * BK * 2;
+};
+template <int kBN>
 struct GemmSmem {
-  uint8_t a_hi[STAGES][kTile];
-  uint8_t a_lo[STAGES][kTile];
-  uint8_t b[STAGES][kTile];
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint8_t a_hi[GemmCfg<kBN>::kStages][kTile];
+  uint8_t a_lo[GemmCfg<kBN>::kStages][kTile];
+  uint8_t b[GemmCfg<kBN>::kStages][GemmCfg<kBN>::kTileB];
+  uint64_t full[GemmCfg<kBN>::kStages];
+  uint64_t empty[GemmCfg<kBN>::kStages];
   uint64_t done;
   uint32_t tmem_base;
   int err;
 };
-constexpr size_t kGemmSmem = sizeof(GemmSmem) + 1024;  // + alignment slack for the 1024-byte swizzle atoms
+template <int kBN>
+constexpr size_t gemm_smem() { return sizeof(GemmSmem<kBN>) + 1024; }  // + slack for the 1024-byte swizzle atoms
+static_assert(gemm_smem<256>() <= 232448 && gemm_smem<128>() <= 232448, "GEMM shared memory");
 
 enum EpiMode : int { kEpiStore = 0, kEpiAdd = 1, kEpiSwiGLU = 2 };
 
@@ -95,15 +105,17 @@ __device__ __forceinline__ void split_store(__nv_bfloat16* hi, __nv_bfloat16* lo
   }
 }
 
-template <int kMode>
+template <int kMode, int kBN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                 const __grid_constant__ CUtensorMap tb, const __grid_constant__ CUtensorMap tb2, const GemmArgs g) {
+  constexpr int STAGES = GemmCfg<kBN>::kStages, kTileB = GemmCfg<kBN>::kTileB, BN = kBN;
   extern __shared__ uint8_t smem_raw[];
-  GemmSmem& sm = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  GemmSmem<kBN>& sm =
+      *reinterpret_cast<GemmSmem<kBN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * BM;
-  const int n0 = blockIdx.x * BN;   // kEpiSwiGLU: SwiGLU columns [n0 / 2, n0 / 2 + 64)
+  const int n0 = blockIdx.x * BN;   // kEpiSwiGLU: SwiGLU columns [n0 / 2, n0 / 2 + BN / 2)
   const int KT = g.K / BK;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -132,12 +144,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int kt = 0; kt < KT; ++kt) {
       const int s = kt % STAGES;
       if (kt >= STAGES && !wait_bounded(&sm.empty[s], ((kt / STAGES) - 1) & 1, g.timeout_ns, &sm.err)) break;
-      mbar_arrive_expect_tx(&sm.full[s], 3 * kTile);
+      mbar_arrive_expect_tx(&sm.full[s], 2 * kTile + kTileB);
       tc::tma_load_2d(sm.a_hi[s], &ta_hi, kt * BK, m0, &sm.full[s]);
       tc::tma_load_2d(sm.a_lo[s], &ta_lo, kt * BK, m0, &sm.full[s]);
       if (kMode == kEpiSwiGLU) {
-        tc::tma_load_2d(sm.b[s], &tb, kt * BK, n0 / 2, &sm.full[s]);               // 64 gate rows
-        tc::tma_load_2d(sm.b[s] + kTile / 2, &tb2, kt * BK, n0 / 2, &sm.full[s]);  // 64 up rows
+        tc::tma_load_2d(sm.b[s], &tb, kt * BK, n0 / 2, &sm.full[s]);                // BN/2 gate rows
+        tc::tma_load_2d(sm.b[s] + kTileB / 2, &tb2, kt * BK, n0 / 2, &sm.full[s]);  // BN/2 up rows
       } else {
         tc::tma_load_2d(sm.b[s], &tb, kt * BK, n0, &sm.full[s]);
       }
@@ -175,10 +187,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (go) {
       if (kMode == kEpiSwiGLU) {
 #pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
+        for (int half = 0; half < BN / 64; ++half) {
           float gv[32], uv[32];
-          tc::tmem_ld32(lane_addr + 32 * half, gv);       // gate columns
-          tc::tmem_ld32(lane_addr + 64 + 32 * half, uv);  // up columns
+          tc::tmem_ld32(lane_addr + 32 * half, gv);           // gate columns
+          tc::tmem_ld32(lane_addr + BN / 2 + 32 * half, uv);  // up columns
           if (row < g.M) {
             float mv[32];
 #pragma unroll
@@ -302,8 +314,9 @@ __global__ void qk_rope_kernel(const float* __restrict__ qkv, const __nv_bfloat1
 // Causal attention over the cache for query tokens [64 blockIdx.x, +64) of Q
 // head blockIdx.y; 4 warps x 16 query rows. Query token i sits at position
 // pos0 + i and attends to keys [0, pos0 + i]. S = Q K^T and O = P V on
-// mma.sync m16n8k16 (BF16 in, FP32 out) with Q and P split into high part +
-// remainder; K/V tiles of 64 keys in padded shared rows (conflict-free ldmatrix).
+// mma.sync m16n8k16 (BF16 in, FP32 out) with Q split into high part +
+// remainder and P as one BF16 part; K/V tiles of 64 keys in padded shared rows
+// (conflict-free ldmatrix).
 constexpr int kAttRow = kHeadDim + 8;  // 136 BF16 = 272 bytes per shared K/V row
 // K/V tiles double-buffered: the next 64 keys are copied (cp.async, 16 bytes a
 // thread at a time) while the tensor cores work on the current ones.
@@ -509,7 +522,7 @@ cudaError_t map_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t col
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int kMode>
+template <int kMode, int kBN>
 cudaError_t gemm_launch(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& b, const CUtensorMap& b2,
                         const GemmArgs& g, cudaStream_t stream) {
   static int configured[64] = {0};
@@ -518,15 +531,17 @@ cudaError_t gemm_launch(const CUtensorMap& ah, const CUtensorMap& al, const CUte
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(gemm_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
+    e = cudaFuncSetAttribute(gemm_kernel<kMode, kBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)gemm_smem<kBN>());
     if (e != cudaSuccess) return e;
     configured[dev] = 1;
   }
-  if (g.K % BK || g.N % BN || g.M < 1) return cudaErrorInvalidValue;
-  dim3 grid(g.N / BN, (g.M + BM - 1) / BM);
-  gemm_kernel<kMode><<<grid, kGemmThreads, kGemmSmem, stream>>>(ah, al, b, b2, g);
+  if (g.K % BK || g.N % kBN || g.M < 1) return cudaErrorInvalidValue;
+  dim3 grid(g.N / kBN, (g.M + BM - 1) / BM);
+  gemm_kernel<kMode, kBN><<<grid, kGemmThreads, gemm_smem<kBN>(), stream>>>(ah, al, b, b2, g);
   return cudaGetLastError();
 }
+constexpr int kPfBN = 256;  // the prefill's GEMMs (every N a multiple of 256)
 
 }  // namespace pf
 
@@ -556,13 +571,13 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
   for (int l = 0; l < n_layers; ++l) {
     const LayerWeights& w = host_layers[l];
     CUtensorMap bq, bk, bv, bo, bg, bu, bd;
-    if ((e = map_2d(&bq, w.q_weight, kQSize, kHidden, BN)) != cudaSuccess) return e;
-    if ((e = map_2d(&bk, w.k_weight, kKVSize, kHidden, BN)) != cudaSuccess) return e;
-    if ((e = map_2d(&bv, w.v_weight, kKVSize, kHidden, BN)) != cudaSuccess) return e;
-    if ((e = map_2d(&bo, w.o_proj_weight, kHidden, kQSize, BN)) != cudaSuccess) return e;
-    if ((e = map_2d(&bg, w.gate_proj_weight, kInter, kHidden, BN / 2)) != cudaSuccess) return e;
-    if ((e = map_2d(&bu, w.up_proj_weight, kInter, kHidden, BN / 2)) != cudaSuccess) return e;
-    if ((e = map_2d(&bd, w.down_proj_weight, kHidden, kInter, BN)) != cudaSuccess) return e;
+    if ((e = map_2d(&bq, w.q_weight, kQSize, kHidden, kPfBN)) != cudaSuccess) return e;
+    if ((e = map_2d(&bk, w.k_weight, kKVSize, kHidden, kPfBN)) != cudaSuccess) return e;
+    if ((e = map_2d(&bv, w.v_weight, kKVSize, kHidden, kPfBN)) != cudaSuccess) return e;
+    if ((e = map_2d(&bo, w.o_proj_weight, kHidden, kQSize, kPfBN)) != cudaSuccess) return e;
+    if ((e = map_2d(&bg, w.gate_proj_weight, kInter, kHidden, kPfBN / 2)) != cudaSuccess) return e;
+    if ((e = map_2d(&bu, w.up_proj_weight, kInter, kHidden, kPfBN / 2)) != cudaSuccess) return e;
+    if ((e = map_2d(&bd, w.down_proj_weight, kHidden, kInter, kPfBN)) != cudaSuccess) return e;
     // input RMSNorm -> QKV (three GEMMs into the [n, 4096] buffer)
     rmsnorm_split_kernel<<<n, kHidden / 4, 0, stream>>>(s.h, w.norm_weight, s.ah, s.al);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -570,12 +585,12 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
     g.ldc = kQKVRows;
     g.N = kQSize;
     g.c = s.qkv;
-    if ((e = gemm_launch<kEpiStore>(a1h, a1l, bq, bq, g, stream)) != cudaSuccess) return e;
+    if ((e = gemm_launch<kEpiStore, kPfBN>(a1h, a1l, bq, bq, g, stream)) != cudaSuccess) return e;
     g.N = kKVSize;
     g.c = s.qkv + kQSize;
-    if ((e = gemm_launch<kEpiStore>(a1h, a1l, bk, bk, g, stream)) != cudaSuccess) return e;
+    if ((e = gemm_launch<kEpiStore, kPfBN>(a1h, a1l, bk, bk, g, stream)) != cudaSuccess) return e;
     g.c = s.qkv + kQSize + kKVSize;
-    if ((e = gemm_launch<kEpiStore>(a1h, a1l, bv, bv, g, stream)) != cudaSuccess) return e;
+    if ((e = gemm_launch<kEpiStore, kPfBN>(a1h, a1l, bv, bv, g, stream)) != cudaSuccess) return e;
     // q/k norm + RoPE, K/V rows into the cache, then causal attention
     qk_rope_kernel<<<dim3(n, 4), 256, 0, stream>>>(s.qkv, w.q_norm_weight, w.k_norm_weight, cos_t, sin_t, rope_fp32,
                                                    pos0, l, kc, vc, max_seq, s.q);
@@ -587,7 +602,7 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
     g.N = kHidden;
     g.ldc = kHidden;
     g.c = s.h;
-    if ((e = gemm_launch<kEpiAdd>(a2h, a2l, bo, bo, g, stream)) != cudaSuccess) return e;
+    if ((e = gemm_launch<kEpiAdd, kPfBN>(a2h, a2l, bo, bo, g, stream)) != cudaSuccess) return e;
     // post-attention RMSNorm -> gate/up with SwiGLU -> down added into the residual
     rmsnorm_split_kernel<<<n, kHidden / 4, 0, stream>>>(s.h, w.post_attn_norm_weight, s.ah, s.al);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -596,12 +611,12 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
     g.m_hi = s.mh;  // a separate buffer: the GEMM still reads s.ah / s.al
     g.m_lo = s.ml;
     g.ldm = kInter;
-    if ((e = gemm_launch<kEpiSwiGLU>(a1h, a1l, bg, bu, g, stream)) != cudaSuccess) return e;
+    if ((e = gemm_launch<kEpiSwiGLU, kPfBN>(a1h, a1l, bg, bu, g, stream)) != cudaSuccess) return e;
     g.K = kInter;
     g.N = kHidden;
     g.c = s.h;
     g.ldc = kHidden;
-    if ((e = gemm_launch<kEpiAdd>(a3h, a3l, bd, bd, g, stream)) != cudaSuccess) return e;
+    if ((e = gemm_launch<kEpiAdd, kPfBN>(a3h, a3l, bd, bd, g, stream)) != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
@@ -614,7 +629,8 @@ cudaError_t gemm_split(const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, con
   cudaError_t e;
   if ((e = map_2d(&ah, a_hi, M, K, BM)) != cudaSuccess) return e;
   if ((e = map_2d(&al, a_lo, M, K, BM)) != cudaSuccess) return e;
-  if ((e = map_2d(&bm, b, N, K, BN)) != cudaSuccess) return e;
+  const bool wide = N % 256 == 0;  // 256-column tiles where N allows, else 128
+  if ((e = map_2d(&bm, b, N, K, wide ? 256 : 128)) != cudaSuccess) return e;
   GemmArgs g = {};
   g.M = M;
   g.N = N;
@@ -623,7 +639,8 @@ cudaError_t gemm_split(const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, con
   g.ldc = N;
   g.timeout_ns = 1000000000ull;
   g.err = err;
-  return gemm_launch<kEpiStore>(ah, al, bm, bm, g, stream);
+  return wide ? gemm_launch<kEpiStore, 256>(ah, al, bm, bm, g, stream)
+              : gemm_launch<kEpiStore, 128>(ah, al, bm, bm, g, stream);
 }
 
 }  // namespace mkb
