@@ -178,6 +178,8 @@ struct PrefillScratch {
   __nv_bfloat16* ml;         //              remainder
   float* qkv;                // [cap, 4096]
   float* q;                  // [cap, 2048] rotated, scaled queries
+  __nv_bfloat16* vt;         // [8, 128, vt_cols] one layer's V cache transposed (key-contiguous)
+  int vt_cols;               // max_seq rounded up to 128 keys
   uint32_t* err;             // device error word (a GEMM wait that expired)
   int cap;
 };

@@ -685,11 +685,12 @@ cudaError_t mkb_engine_prefill_batched(mkb_engine* e, const int* prompt_tokens, 
   if (err != cudaSuccess) return err;
   const mkb_decode_args& sa = e->step_args;
   if (e->pf_block == nullptr) {
-    // one block: residual, GEMM operands, SwiGLU output, QKV, rotated q, error word
+    // one block: residual, GEMM operands, SwiGLU output, QKV, rotated q, V^T
     const size_t cap = static_cast<size_t>(e->max_seq);
+    const int vt_cols = (e->max_seq + 127) / 128 * 128;
     const size_t b_h = cap * kHidden * 4, b_a = cap * kQSize * 2, b_m = cap * kInter * 2, b_qkv = cap * kQKVRows * 4,
-                 b_q = cap * kQSize * 4;
-    const size_t total = b_h + 2 * b_a + 2 * b_m + b_qkv + b_q + 256;
+                 b_q = cap * kQSize * 4, b_vt = static_cast<size_t>(kNKV) * kHeadDim * vt_cols * 2;
+    const size_t total = b_h + 2 * b_a + 2 * b_m + b_qkv + b_q + b_vt + 256;
     err = cudaMalloc(&e->pf_block, total);
     if (err != cudaSuccess) return err;
     char* p = static_cast<char*>(e->pf_block);
@@ -707,6 +708,9 @@ cudaError_t mkb_engine_prefill_batched(mkb_engine* e, const int* prompt_tokens, 
     p += b_qkv;
     e->pf.q = reinterpret_cast<float*>(p);
     p += b_q;
+    e->pf.vt = reinterpret_cast<__nv_bfloat16*>(p);
+    e->pf.vt_cols = vt_cols;
+    p += b_vt;
     e->pf.cap = e->max_seq;
   }
   // a GEMM wait that expires is recorded in the workspace's status word (the

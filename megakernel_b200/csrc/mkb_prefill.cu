@@ -38,6 +38,11 @@
 namespace mkb {
 namespace pf {
 
+// Prefill attention: tcgen05 kernel (1) or the mma.sync kernel (0).
+#ifndef MKB_PF_ATTN_TC
+#define MKB_PF_ATTN_TC 1
+#endif
+
 constexpr int BM = 128, BK = 64;
 constexpr int kTile = BM * BK * 2;  // 16 KB: one 128 x 64 BF16 A-operand tile
 constexpr int kGemmThreads = 192;   // warp 0 TMA, warp 1 MMA (+ TMEM), warps 2-5 epilogue
@@ -270,11 +275,13 @@ __device__ __forceinline__ float rope_val(const void* table, int fp32, size_t id
 // Per token (blockIdx.x) and head row (one warp per head: 16 q, 8 k, 8 v):
 // q/k RMSNorm over 128 dims + rotate-half RoPE at the token's position
 // (megakernel.cu:490-630), K/V rows into the BF16 cache, q pre-scaled by
-// log2(e) / sqrt(128) for the exp2-domain softmax. blockDim 256 = 8 heads;
-// blockIdx.y picks the group of 8.
+// log2(e) / sqrt(128) for the exp2-domain softmax, written either as FP32
+// (q_out) or as a BF16 high part and remainder (q_hi / q_lo, when not null).
+// blockDim 256 = 8 heads; blockIdx.y picks the group of 8.
 __global__ void qk_rope_kernel(const float* __restrict__ qkv, const __nv_bfloat16* __restrict__ qn,
                                const __nv_bfloat16* __restrict__ kn, const void* cos_t, const void* sin_t, int fp32,
-                               int pos0, int layer, __nv_bfloat16* kc, __nv_bfloat16* vc, int max_seq, float* q_out) {
+                               int pos0, int layer, __nv_bfloat16* kc, __nv_bfloat16* vc, int max_seq, float* q_out,
+                               __nv_bfloat16* q_hi, __nv_bfloat16* q_lo) {
   const int i = blockIdx.x;
   const int head = blockIdx.y * 8 + (threadIdx.x >> 5);  // 0-15 q, 16-23 k, 24-31 v
   const int lane = threadIdx.x & 31;
@@ -298,11 +305,20 @@ __global__ void qk_rope_kernel(const float* __restrict__ qkv, const __nv_bfloat1
   }
   if (head < 16) {
     const float sc = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
-    float* q = q_out + (size_t)i * kQSize + head * kHeadDim;
-    q[d0] = x0 * sc;
-    q[d0 + 1] = x1 * sc;
-    q[d0 + 64] = x2 * sc;
-    q[d0 + 65] = x3 * sc;
+    const size_t o = (size_t)i * kQSize + head * kHeadDim + d0;
+    if (q_hi != nullptr) {
+      const uint32_t h01 = pack_bf2(x0 * sc, x1 * sc), h23 = pack_bf2(x2 * sc, x3 * sc);
+      *reinterpret_cast<uint32_t*>(q_hi + o) = h01;
+      *reinterpret_cast<uint32_t*>(q_hi + o + 64) = h23;
+      *reinterpret_cast<uint32_t*>(q_lo + o) = pack_bf2(x0 * sc - bf_lo(h01), x1 * sc - bf_hi(h01));
+      *reinterpret_cast<uint32_t*>(q_lo + o + 64) = pack_bf2(x2 * sc - bf_lo(h23), x3 * sc - bf_hi(h23));
+    } else {
+      float* q = q_out + o;
+      q[0] = x0 * sc;
+      q[1] = x1 * sc;
+      q[64] = x2 * sc;
+      q[65] = x3 * sc;
+    }
   } else {
     const int h = (head - 16) & 7;
     __nv_bfloat16* dst = (head < 24 ? kc : vc) + (((size_t)layer * kNKV + h) * max_seq + pos) * kHeadDim;
@@ -321,7 +337,7 @@ constexpr int kAttRow = kHeadDim + 8;  // 136 BF16 = 272 bytes per shared K/V ro
 // K/V tiles double-buffered: the next 64 keys are copied (cp.async, 16 bytes a
 // thread at a time) while the tensor cores work on the current ones.
 constexpr int kAttStages = 2;
-constexpr size_t kAttSmem = size_t(kAttStages) * 2 * 64 * kAttRow * 2;  // 69,632 B
+[[maybe_unused]] constexpr size_t kAttSmem = size_t(kAttStages) * 2 * 64 * kAttRow * 2;  // 69,632 B
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
@@ -488,6 +504,270 @@ __global__ void __launch_bounds__(128) attn_kernel(const float* __restrict__ q, 
   }
 }
 
+// ---- causal attention on tcgen05 ---------------------------------------------------
+//
+// attn_tc_kernel: one CTA per (Q head, 128 query tokens). S = Q K^T and O = P V run
+// on tcgen05.mma (M = 128 query rows, N = 128 keys or dims, accumulators in TMEM);
+// q enters as a BF16 high part and remainder (two MMAs per k-step, as in the
+// GEMMs), P as one BF16 operand. Keys come in tiles of 128: K rows straight from
+// the cache (K-major for S), V from a per-layer transposed copy (v_transpose_kernel)
+// so that V^T is K-major for O. Warp 0 issues the TMA loads (2-stage K and V^T
+// rings), one thread of warp 1 the MMAs, warps 2-5 own one query row per thread:
+// they read S from TMEM, keep the online softmax (exp2 domain; the reference max
+// only moves when a row's maximum grows by more than 8, so O is rescaled in TMEM
+// rarely and P stays within [0, 256]), and write P into shared memory in the
+// MMA's 128-byte-swizzled layout. Two S buffers in TMEM let the tensor cores
+// compute the next tile's scores while the softmax works on this one.
+constexpr int kTcThreads = 192;
+constexpr int kAtom = 128 * 128;  // 16 KB: 128 rows x 64 BF16, 128-byte swizzle
+struct AttnTcSmem {
+  uint8_t qh[2][kAtom];     // [dim half]: query rows
+  uint8_t ql[2][kAtom];
+  uint8_t k[2][2][kAtom];   // [stage][dim half]: key rows
+  uint8_t vt[2][2][kAtom];  // [stage][key half]: dim rows
+  uint8_t p[2][kAtom];      // [key half]: query rows
+  uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full, o_done;
+  uint32_t tmem_base;
+  int err;
+};
+constexpr size_t kAttTcSmem = sizeof(AttnTcSmem) + 1024;
+static_assert(kAttTcSmem <= 232448, "attention shared memory");
+constexpr uint32_t kAttTmemCols = 512;  // S buffers at columns 0 and 128, O at 256
+
+// Every lane of a warp waits; the warp goes on only if all of them saw the phase.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t ph, unsigned long long timeout, int* err) {
+  return __all_sync(0xffffffffu, wait_bounded(bar, ph, timeout, err));
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tq_hi, const __grid_constant__ CUtensorMap tq_lo,
+                   const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tvt, int n, int pos0,
+                   int max_seq, __nv_bfloat16* oh, __nv_bfloat16* ol, unsigned long long timeout_ns, uint32_t* err) {
+  extern __shared__ uint8_t smem_raw[];
+  AttnTcSmem& sm = *reinterpret_cast<AttnTcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hq = blockIdx.x, hk = hq >> 1;
+  // causal work grows with the query block: the longest blocks (of every head) go first
+  const int i0 = (gridDim.y - 1 - blockIdx.y) * 128;
+  const int nt = (pos0 + min(i0 + 127, n - 1)) / 128 + 1;  // key tiles up to the block's last query
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
+      mbar_init(&sm.s_full[s], 1);
+    }
+    mbar_init(&sm.p_full, 128);
+    mbar_init(&sm.o_done, 1);
+    sm.err = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&sm.tmem_base, kAttTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = sm.tmem_base, t_o = tbase + 256;
+
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tensormap(&tq_hi);
+    tc::prefetch_tensormap(&tq_lo);
+    tc::prefetch_tensormap(&tk);
+    tc::prefetch_tensormap(&tvt);
+    mbar_arrive_expect_tx(&sm.q_full, 4 * kAtom);
+    for (int h = 0; h < 2; ++h) {
+      tc::tma_load_2d(sm.qh[h], &tq_hi, hq * kHeadDim + 64 * h, i0, &sm.q_full);
+      tc::tma_load_2d(sm.ql[h], &tq_lo, hq * kHeadDim + 64 * h, i0, &sm.q_full);
+    }
+    const int krow = hk * max_seq;  // this KV head's first cache row in the layer's map
+    int k_issued = 0, v_issued = 0;
+    for (int j = 0; j < nt; ++j) {
+      const int st = j & 1;
+      const uint32_t ph = ((j >> 1) - 1) & 1;
+      if (j >= 2 && !wait_bounded(&sm.k_empty[st], ph, timeout_ns, &sm.err)) break;
+      mbar_arrive_expect_tx(&sm.k_full[st], 2 * kAtom);
+      tc::tma_load_2d(sm.k[st][0], &tk, 0, krow + 128 * j, &sm.k_full[st]);
+      tc::tma_load_2d(sm.k[st][1], &tk, 64, krow + 128 * j, &sm.k_full[st]);
+      ++k_issued;
+      if (j >= 2 && !wait_bounded(&sm.v_empty[st], ph, timeout_ns, &sm.err)) break;
+      mbar_arrive_expect_tx(&sm.v_full[st], 2 * kAtom);
+      tc::tma_load_2d(sm.vt[st][0], &tvt, 128 * j, hk * kHeadDim, &sm.v_full[st]);
+      tc::tma_load_2d(sm.vt[st][1], &tvt, 128 * j + 64, hk * kHeadDim, &sm.v_full[st]);
+      ++v_issued;
+    }
+    // after a stop, wait (bounded) for the copies still in flight before leaving
+    if (sm.err) {
+      const uint64_t t0 = global_ns();
+      while (!mbar_wait(&sm.q_full, 0, 20000) && global_ns() - t0 < timeout_ns) {
+      }
+      for (int j = max(k_issued - 2, 0); j < k_issued; ++j)
+        while (!mbar_wait(&sm.k_full[j & 1], (j >> 1) & 1, 20000) && global_ns() - t0 < timeout_ns) {
+        }
+      for (int j = max(v_issued - 2, 0); j < v_issued; ++j)
+        while (!mbar_wait(&sm.v_full[j & 1], (j >> 1) & 1, 20000) && global_ns() - t0 < timeout_ns) {
+        }
+    }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = tc::idesc_bf16_f32(128, 128);
+    const uint32_t qh = smem_addr(sm.qh[0]), ql = smem_addr(sm.ql[0]), pa = smem_addr(sm.p[0]);
+    // S(j) = (Q_hi + Q_lo) K(j)^T into S buffer j & 1
+    auto issue_s = [&](int j) -> bool {
+      const int st = j & 1;
+      if (!wait_bounded(&sm.k_full[st], (j >> 1) & 1, timeout_ns, &sm.err)) return false;
+      tc::fence_after_sync();
+      const uint32_t kb = smem_addr(sm.k[st][0]);
+#pragma unroll
+      for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
+        const uint64_t db = tc::desc_sw128(kb + off);
+        tc::mma_bf16_ss(tbase + 128 * st, tc::desc_sw128(qh + off), db, idesc, kk != 0);
+        tc::mma_bf16_ss(tbase + 128 * st, tc::desc_sw128(ql + off), db, idesc, 1u);
+      }
+      tc::commit(&sm.k_empty[st]);
+      tc::commit(&sm.s_full[st]);
+      return true;
+    };
+    if (wait_bounded(&sm.q_full, 0, timeout_ns, &sm.err) && issue_s(0)) {
+      for (int j = 0; j < nt; ++j) {
+        if (j + 1 < nt && !issue_s(j + 1)) break;
+        // O (+)= P(j) V(j) once the softmax has written P(j) (and rescaled O)
+        if (!wait_bounded(&sm.p_full, j & 1, timeout_ns, &sm.err)) break;
+        if (!wait_bounded(&sm.v_full[j & 1], (j >> 1) & 1, timeout_ns, &sm.err)) break;
+        tc::fence_after_sync();
+        const uint32_t vb = smem_addr(sm.vt[j & 1][0]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
+          tc::mma_bf16_ss(t_o, tc::desc_sw128(pa + off), tc::desc_sw128(vb + off), idesc, (j | kk) != 0);
+        }
+        tc::commit(&sm.v_empty[j & 1]);
+        tc::commit(&sm.o_done);
+      }
+    }
+  } else if (warp >= 2) {
+    const int q4 = warp & 3;  // TMEM lanes 32 q4 .. + 31 = query rows
+    const int row = 32 * q4 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * q4) << 16;
+    const int lim = pos0 + i0 + row;  // this query's last key
+    float m = 0.f, l = 0.f;           // reference max (exp2 domain) and row sum
+    bool go = true;
+    for (int j = 0; j < nt && go; ++j) {
+      const int st = j & 1;
+      go = warp_wait(&sm.s_full[st], (j >> 1) & 1, timeout_ns, &sm.err);
+      if (!go) break;
+      tc::fence_after_sync();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld32(tbase + lane_off + 128 * st + 32 * c, s + 32 * c);
+      const int k0 = 128 * j;
+      if (k0 + 127 > lim) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (k0 + i > lim) s[i] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);  // finite: key 0 <= lim, and tile 0 holds it
+      if (j > 0) {
+        // PV(j - 1) has completed: the P buffer is free and O may be rescaled
+        go = warp_wait(&sm.o_done, (j - 1) & 1, timeout_ns, &sm.err);
+        if (!go) break;
+        tc::fence_after_sync();
+        if (__any_sync(0xffffffffu, mx > m + 8.f)) {
+          const float sc = mx > m ? ex2_approx(m - mx) : 1.f;
+          m = fmaxf(m, mx);
+          l *= sc;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tc::tmem_ld32(t_o + lane_off + 32 * c, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= sc;
+            tc::tmem_st32(t_o + lane_off + 32 * c, o);
+          }
+        }
+      } else {
+        m = mx;
+      }
+      // P = 2^(S - m) in BF16, row r of each 64-key atom at r * 128 bytes with the
+      // 16-byte chunks swizzled by r & 7 (the layout a 128-byte-swizzle TMA writes)
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float a = s[8 * c + 2 * t], b = s[8 * c + 2 * t + 1];
+          const float pa = a > -INFINITY ? ex2_approx(a - m) : 0.f;
+          const float pb = b > -INFINITY ? ex2_approx(b - m) : 0.f;
+          rs += pa + pb;
+          w[t] = pack_bf2(pa, pb);
+        }
+        *reinterpret_cast<uint4*>(sm.p[c >> 3] + row * 128 + (((c & 7) ^ (row & 7)) << 4)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l += rs;
+      fence_proxy_async_shared();  // P is read by the tensor cores (async proxy)
+      tc::fence_before_sync();
+      mbar_arrive(&sm.p_full);
+    }
+    if (go) go = warp_wait(&sm.o_done, (nt - 1) & 1, timeout_ns, &sm.err);
+    if (go) {
+      tc::fence_after_sync();
+      const int qi = i0 + row;
+      const float inv = 1.f / l;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        tc::tmem_ld32(t_o + lane_off + 32 * c, o);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] *= inv;
+        if (qi < n) {
+          const size_t off = (size_t)qi * kQSize + hq * kHeadDim + 32 * c;
+          split_store(oh + off, ol + off, o, 4);
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x == 0 && sm.err && err) atomicCAS(err, 0u, static_cast<uint32_t>(kErrTimeoutRing));
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tbase, kAttTmemCols);
+  }
+}
+
+// V^T of one layer: vt[hk][d][key] = v_cache[hk][key][d] for keys
+// [64 blockIdx.x, +64) of KV head blockIdx.y, zeros at keys >= kv_len (the
+// attention reads whole 128-key tiles; P is 0 there and so must V be).
+__global__ void __launch_bounds__(256) v_transpose_kernel(const __nv_bfloat16* __restrict__ vc, int max_seq,
+                                                           int kv_len, int vt_cols, __nv_bfloat16* __restrict__ vt) {
+  __shared__ __align__(16) __nv_bfloat16 t[64][kHeadDim + 8];
+  const int hk = blockIdx.y, k0 = blockIdx.x * 64;
+  for (int e = threadIdx.x; e < 64 * 16; e += 256) {
+    const int r = e >> 4, c = (e & 15) * 8;
+    const int key = k0 + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (key < kv_len) v = *reinterpret_cast<const uint4*>(vc + ((size_t)hk * max_seq + key) * kHeadDim + c);
+    *reinterpret_cast<uint4*>(&t[r][c]) = v;
+  }
+  __syncthreads();
+  const unsigned short* tu = reinterpret_cast<const unsigned short*>(&t[0][0]);
+  for (int e = threadIdx.x; e < kHeadDim * 8; e += 256) {
+    const int d = e >> 3, kc = (e & 7) * 8;
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      w[i] = uint32_t(tu[(kc + 2 * i) * (kHeadDim + 8) + d]) | (uint32_t(tu[(kc + 2 * i + 1) * (kHeadDim + 8) + d]) << 16);
+    *reinterpret_cast<uint4*>(vt + ((size_t)hk * kHeadDim + d) * vt_cols + k0 + kc) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // ---- host side ---------------------------------------------------------------------
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -552,7 +832,18 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
                            int max_seq, const int* ids, int n, int pos0, const PrefillScratch& s, cudaStream_t stream) {
   using namespace pf;
   if (n < 1 || n > s.cap || pos0 < 0 || pos0 + n > max_seq) return cudaErrorInvalidValue;
+#if MKB_PF_ATTN_TC
+  if (s.vt_cols < pos0 + n || s.vt_cols % 128) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttTcSmem);
+  // queries as BF16 high part / remainder in the SwiGLU buffers (free until the gate/up GEMM)
+  CUtensorMap tqh, tql, tvt;
+  if (e == cudaSuccess) e = map_2d(&tqh, s.mh, n, kQSize, 128);
+  if (e == cudaSuccess) e = map_2d(&tql, s.ml, n, kQSize, 128);
+  if (e == cudaSuccess) e = map_2d(&tvt, s.vt, kNKV * kHeadDim, s.vt_cols, 128);
+  const int kv_tiles = (pos0 + n + 127) / 128;
+#else
   cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttSmem);
+#endif
   if (e != cudaSuccess) return e;
   embed_kernel<<<n, kHidden / 4, 0, stream>>>(ids, embed, s.h);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -592,10 +883,24 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
     g.c = s.qkv + kQSize + kKVSize;
     if ((e = gemm_launch<kEpiStore, kPfBN>(a1h, a1l, bv, bv, g, stream)) != cudaSuccess) return e;
     // q/k norm + RoPE, K/V rows into the cache, then causal attention
+#if MKB_PF_ATTN_TC
     qk_rope_kernel<<<dim3(n, 4), 256, 0, stream>>>(s.qkv, w.q_norm_weight, w.k_norm_weight, cos_t, sin_t, rope_fp32,
-                                                   pos0, l, kc, vc, max_seq, s.q);
+                                                   pos0, l, kc, vc, max_seq, nullptr, s.mh, s.ml);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const size_t layer_rows = (size_t)l * kNKV * max_seq;  // this layer's first cache row
+    v_transpose_kernel<<<dim3(2 * kv_tiles, kNKV), 256, 0, stream>>>(vc + layer_rows * kHeadDim, max_seq, pos0 + n,
+                                                                     s.vt_cols, s.vt);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    CUtensorMap tk;
+    if ((e = map_2d(&tk, kc + layer_rows * kHeadDim, (uint64_t)kNKV * max_seq, kHeadDim, 128)) != cudaSuccess) return e;
+    attn_tc_kernel<<<dim3(kNQ, (n + 127) / 128), kTcThreads, kAttTcSmem, stream>>>(
+        tqh, tql, tk, tvt, n, pos0, max_seq, s.ah, s.al, g.timeout_ns, s.err);
+#else
+    qk_rope_kernel<<<dim3(n, 4), 256, 0, stream>>>(s.qkv, w.q_norm_weight, w.k_norm_weight, cos_t, sin_t, rope_fp32,
+                                                   pos0, l, kc, vc, max_seq, s.q, nullptr, nullptr);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     attn_kernel<<<dim3((n + 63) / 64, kNQ), 128, kAttSmem, stream>>>(s.q, kc, vc, n, pos0, l, max_seq, s.ah, s.al);
+#endif
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     // o_proj added into the residual
     g.K = kQSize;
