@@ -506,7 +506,7 @@ def run_prefill(a, rank, world, local):
                              "flops_per_prefill": fl,
                              "note": "model FLOPs; the GEMMs run each activation as two BF16 parts, "
                                      "so the tensor cores execute about twice these FLOPs"},
-                "gpu_launches": 28 * 10 + 2, "clocks": res[n]["clocks"]}
+                "gpu_launches": 28 * 7 + 2, "clocks": res[n]["clocks"]}
         print(json.dumps(line), flush=True)
     eng.close()
 

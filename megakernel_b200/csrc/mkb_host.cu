@@ -711,6 +711,10 @@ cudaError_t mkb_engine_prefill_batched(mkb_engine* e, const int* prompt_tokens, 
     e->pf.vt = reinterpret_cast<__nv_bfloat16*>(p);
     e->pf.vt_cols = vt_cols;
     p += b_vt;
+    // V^T past the keys a prefill writes is read as whole 128-key tiles (with
+    // zero weights): it must hold finite values, zeros to begin with
+    err = cudaMemsetAsync(e->pf.vt, 0, b_vt, stream);
+    if (err != cudaSuccess) return err;
     e->pf.cap = e->max_seq;
   }
   // a GEMM wait that expires is recorded in the workspace's status word (the

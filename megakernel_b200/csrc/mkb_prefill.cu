@@ -4,25 +4,25 @@
 //
 // Per layer, for the n prompt tokens (M = n rows):
 //   RMSNorm (FP32 residual -> activation split into a BF16 high part and the BF16
-//   remainder) -> QKV GEMMs -> q/k RMSNorm + RoPE, K/V rows into the cache ->
-//   causal attention -> o_proj GEMM added into the residual -> RMSNorm ->
-//   gate/up GEMM with the SwiGLU in its epilogue -> down GEMM added into the
-//   residual. The last token's residual then goes through the decode kernel's
-//   final norm + LM head + argmax.
+//   remainder) -> one QKV GEMM whose epilogue applies the q/k RMSNorm + RoPE and
+//   writes q, the K/V cache rows and V^T -> causal attention -> o_proj GEMM added
+//   into the residual -> RMSNorm -> gate/up GEMM with the SwiGLU in its epilogue
+//   -> down GEMM added into the residual. The last token's residual then goes
+//   through the decode kernel's final norm + LM head + argmax.
 //
 // GEMMs (gemm_kernel): C[M, N] = (A_hi + A_lo)[M, K] * B[N, K]^T with tcgen05.mma
-// (kind::f16, BF16 x BF16 -> FP32 in TMEM), 128 x 128 tiles, K in steps of 64,
-// operands brought in by TMA tiled loads with 128-byte swizzle through a 4-stage
-// shared-memory ring; one warp issues the loads, one thread the MMAs, four warps
-// read the accumulator back (tcgen05.ld) for the epilogue. Splitting the FP32
-// activation into two BF16 parts keeps the products to about 2^-16 relative,
-// the accuracy of the decode path's GEMVs.
+// (kind::f16, BF16 x BF16 -> FP32 in TMEM), persistent CTAs over 128 x 256 output
+// tiles, K in steps of 64, operands brought in by TMA tiled loads with 128-byte
+// swizzle through a 3-stage shared-memory ring; one warp issues the loads, one
+// thread the MMAs into two TMEM accumulators, four warps read the finished one
+// back (tcgen05.ld) for the epilogue while the next tile accumulates. Splitting
+// the FP32 activation into two BF16 parts keeps the products to about 2^-16
+// relative, the accuracy of the decode path's GEMVs.
 //
-// Attention (attn_kernel): causal flash attention on the warp-level tensor-core
-// MMA (mma.sync m16n8k16), q split into a BF16 high part and remainder (the
-// scores keep ~16 bits of q), the probabilities in [0, 1] as one BF16 operand,
-// K/V read back from the BF16 cache the kernel before wrote (double-buffered
-// cp.async tiles), online softmax in the exp2 domain.
+// Attention (attn_tc_kernel): causal flash attention on tcgen05.mma, S and O in
+// TMEM, q as BF16 high part + remainder, the probabilities as one BF16 operand,
+// online softmax in the exp2 domain. attn_kernel (mma.sync m16n8k16) is the
+// earlier kernel, kept behind MKB_PF_ATTN_TC=0 with the unfused QKV path.
 
 #include <cstdint>
 #include <cstdio>
@@ -61,7 +61,8 @@ struct GemmSmem {
   uint8_t b[GemmCfg<kBN>::kStages][GemmCfg<kBN>::kTileB];
   uint64_t full[GemmCfg<kBN>::kStages];
   uint64_t empty[GemmCfg<kBN>::kStages];
-  uint64_t done;
+  uint64_t acc_full[2];   // accumulator b holds a finished tile
+  uint64_t acc_empty[2];  // the epilogue has read accumulator b
   uint32_t tmem_base;
   int err;
 };
@@ -69,7 +70,18 @@ template <int kBN>
 constexpr size_t gemm_smem() { return sizeof(GemmSmem<kBN>) + 1024; }  // + slack for the 1024-byte swizzle atoms
 static_assert(gemm_smem<256>() <= 232448 && gemm_smem<128>() <= 232448, "GEMM shared memory");
 
-enum EpiMode : int { kEpiStore = 0, kEpiAdd = 1, kEpiSwiGLU = 2 };
+enum EpiMode : int { kEpiStore = 0, kEpiAdd = 1, kEpiSwiGLU = 2, kEpiQKV = 3 };
+
+__device__ __forceinline__ float rope_val(const void* table, int fp32, size_t idx) {
+  return fp32 ? __ldg(static_cast<const float*>(table) + idx)
+              : __bfloat162float(static_cast<const __nv_bfloat16*>(table)[idx]);
+}
+// entries idx .. idx + 3 (idx a multiple of 4) of an FP32 or BF16 table
+__device__ __forceinline__ float4 table4(const void* table, int fp32, size_t idx) {
+  if (fp32) return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(table) + idx));
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(table) + idx));
+  return make_float4(bf_lo(u.x), bf_hi(u.x), bf_lo(u.y), bf_hi(u.y));
+}
 
 struct GemmArgs {
   int M, N, K;                 // C [M, N]; K a multiple of 64
@@ -78,6 +90,20 @@ struct GemmArgs {
   __nv_bfloat16* m_hi;         // kEpiSwiGLU: silu(gate) * up as high part / remainder
   __nv_bfloat16* m_lo;
   int ldm;
+  // kEpiQKV (N = 4096: q, k, v columns of token rows at positions pos0 + row):
+  // q/k RMSNorm + rotate-half RoPE, q scaled by log2(e) / sqrt(128) into q_hi /
+  // q_lo [M, 2048], K and V rows into this layer's cache [8, max_seq, 128], V
+  // also transposed into vt [8, 128, vt_cols]
+  const __nv_bfloat16* qn;
+  const __nv_bfloat16* kn;
+  const void* cos_t;
+  const void* sin_t;
+  int rope_fp32, pos0, max_seq, vt_cols;
+  __nv_bfloat16* kc_layer;
+  __nv_bfloat16* vc_layer;
+  __nv_bfloat16* q_hi;
+  __nv_bfloat16* q_lo;
+  __nv_bfloat16* vt;
   unsigned long long timeout_ns;
   uint32_t* err;
 };
@@ -110,29 +136,36 @@ __device__ __forceinline__ void split_store(__nv_bfloat16* hi, __nv_bfloat16* lo
   }
 }
 
+// Persistent: CTA c computes output tiles c, c + gridDim.x, ... (row-block
+// major). The TMA ring runs across tile boundaries, and TMEM holds two
+// accumulators (2 x kBN columns), so the epilogue of one tile overlaps the MMAs
+// of the next.
 template <int kMode, int kBN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
-                const __grid_constant__ CUtensorMap tb, const __grid_constant__ CUtensorMap tb2, const GemmArgs g) {
+                const __grid_constant__ CUtensorMap tb, const __grid_constant__ CUtensorMap tb2,
+                const __grid_constant__ CUtensorMap tb3, const GemmArgs g) {
   constexpr int STAGES = GemmCfg<kBN>::kStages, kTileB = GemmCfg<kBN>::kTileB, BN = kBN;
   extern __shared__ uint8_t smem_raw[];
   GemmSmem<kBN>& sm =
       *reinterpret_cast<GemmSmem<kBN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM;
-  const int n0 = blockIdx.x * BN;   // kEpiSwiGLU: SwiGLU columns [n0 / 2, n0 / 2 + BN / 2)
   const int KT = g.K / BK;
+  const int n_tiles_n = g.N / BN, n_tiles = n_tiles_n * ((g.M + BM - 1) / BM);
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
-    mbar_init(&sm.done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 4);  // one arrival per epilogue warp
+    }
     sm.err = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tc::tmem_alloc(&sm.tmem_base, BN);
+    tc::tmem_alloc(&sm.tmem_base, 2 * BN);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -144,53 +177,152 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc::prefetch_tensormap(&ta_hi);
     tc::prefetch_tensormap(&ta_lo);
     tc::prefetch_tensormap(&tb);
-    if (kMode == kEpiSwiGLU) tc::prefetch_tensormap(&tb2);
-    int issued = 0;
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES;
-      if (kt >= STAGES && !wait_bounded(&sm.empty[s], ((kt / STAGES) - 1) & 1, g.timeout_ns, &sm.err)) break;
-      mbar_arrive_expect_tx(&sm.full[s], 2 * kTile + kTileB);
-      tc::tma_load_2d(sm.a_hi[s], &ta_hi, kt * BK, m0, &sm.full[s]);
-      tc::tma_load_2d(sm.a_lo[s], &ta_lo, kt * BK, m0, &sm.full[s]);
-      if (kMode == kEpiSwiGLU) {
-        tc::tma_load_2d(sm.b[s], &tb, kt * BK, n0 / 2, &sm.full[s]);                // BN/2 gate rows
-        tc::tma_load_2d(sm.b[s] + kTileB / 2, &tb2, kt * BK, n0 / 2, &sm.full[s]);  // BN/2 up rows
-      } else {
-        tc::tma_load_2d(sm.b[s], &tb, kt * BK, n0, &sm.full[s]);
+    if (kMode == kEpiSwiGLU || kMode == kEpiQKV) tc::prefetch_tensormap(&tb2);
+    if (kMode == kEpiQKV) tc::prefetch_tensormap(&tb3);
+    int it = 0;  // k-steps issued, over all of this CTA's tiles
+    for (int t = blockIdx.x; t < n_tiles && !sm.err; t += gridDim.x) {
+      const int m0 = (t / n_tiles_n) * BM;
+      const int n0 = (t % n_tiles_n) * BN;  // kEpiSwiGLU: SwiGLU columns [n0 / 2, n0 / 2 + BN / 2)
+      for (int kt = 0; kt < KT; ++kt, ++it) {
+        const int s = it % STAGES;
+        if (it >= STAGES && !wait_bounded(&sm.empty[s], ((it / STAGES) - 1) & 1, g.timeout_ns, &sm.err)) break;
+        mbar_arrive_expect_tx(&sm.full[s], 2 * kTile + kTileB);
+        tc::tma_load_2d(sm.a_hi[s], &ta_hi, kt * BK, m0, &sm.full[s]);
+        tc::tma_load_2d(sm.a_lo[s], &ta_lo, kt * BK, m0, &sm.full[s]);
+        if (kMode == kEpiSwiGLU) {
+          tc::tma_load_2d(sm.b[s], &tb, kt * BK, n0 / 2, &sm.full[s]);                // BN/2 gate rows
+          tc::tma_load_2d(sm.b[s] + kTileB / 2, &tb2, kt * BK, n0 / 2, &sm.full[s]);  // BN/2 up rows
+        } else if (kMode == kEpiQKV) {  // q, k or v weight rows (tiles never straddle two)
+          const CUtensorMap* m = n0 < kQSize ? &tb : n0 < kQSize + kKVSize ? &tb2 : &tb3;
+          const int r0 = n0 < kQSize ? n0 : n0 < kQSize + kKVSize ? n0 - kQSize : n0 - kQSize - kKVSize;
+          tc::tma_load_2d(sm.b[s], m, kt * BK, r0, &sm.full[s]);
+        } else {
+          tc::tma_load_2d(sm.b[s], &tb, kt * BK, n0, &sm.full[s]);
+        }
       }
-      ++issued;
     }
     // after a stop, wait (bounded) for the copies still in flight before leaving
-    for (int kt = issued - 1; kt >= 0 && kt >= issued - STAGES && sm.err; --kt) {
+    for (int k = it - 1; k >= 0 && k >= it - STAGES && sm.err; --k) {
       const uint64_t t0 = global_ns();
-      while (!mbar_wait(&sm.full[kt % STAGES], (kt / STAGES) & 1, 20000))
+      while (!mbar_wait(&sm.full[k % STAGES], (k / STAGES) & 1, 20000))
         if (global_ns() - t0 > g.timeout_ns) break;
     }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES;
-      if (!wait_bounded(&sm.full[s], (kt / STAGES) & 1, g.timeout_ns, &sm.err)) break;
+    int it = 0, lt = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++lt) {
+      const int b = lt & 1;
+      if (lt >= 2 && !wait_bounded(&sm.acc_empty[b], ((lt >> 1) - 1) & 1, g.timeout_ns, &sm.err)) break;
       tc::fence_after_sync();
-      const uint32_t ah = smem_addr(sm.a_hi[s]), al = smem_addr(sm.a_lo[s]), bb = smem_addr(sm.b[s]);
+      const uint32_t acc = tbase + b * BN;
+      for (int kt = 0; kt < KT; ++kt, ++it) {
+        const int s = it % STAGES;
+        if (!wait_bounded(&sm.full[s], (it / STAGES) & 1, g.timeout_ns, &sm.err)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t ah = smem_addr(sm.a_hi[s]), al = smem_addr(sm.a_lo[s]), bb = smem_addr(sm.b[s]);
 #pragma unroll
-      for (int kk = 0; kk < BK / 16; ++kk) {
-        const uint64_t db = tc::desc_sw128(bb + kk * 32);
-        tc::mma_bf16_ss(tbase, tc::desc_sw128(ah + kk * 32), db, idesc, (kt | kk) != 0);
-        tc::mma_bf16_ss(tbase, tc::desc_sw128(al + kk * 32), db, idesc, 1u);
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t db = tc::desc_sw128(bb + kk * 32);
+          tc::mma_bf16_ss(acc, tc::desc_sw128(ah + kk * 32), db, idesc, (kt | kk) != 0);
+          tc::mma_bf16_ss(acc, tc::desc_sw128(al + kk * 32), db, idesc, 1u);
+        }
+        tc::commit(&sm.empty[s]);  // the stage is free once these MMAs have read it
       }
-      tc::commit(&sm.empty[s]);  // the stage is free once these MMAs have read it
+      if (ok) tc::commit(&sm.acc_full[b]);  // the tile's MMAs have all completed
     }
-    tc::commit(&sm.done);  // every MMA issued above has completed
   } else if (warp >= 2) {
-    int go = wait_bounded(&sm.done, 0, g.timeout_ns, &sm.err) && *reinterpret_cast<volatile int*>(&sm.err) == 0;
-    go = __shfl_sync(0xffffffffu, go, 0);  // tcgen05.ld is warp-wide: one decision per warp
-    tc::fence_after_sync();
     const int q = warp & 3;  // TMEM lanes 32q .. 32q + 31 = tile rows
-    const int row = m0 + 32 * q + lane;
-    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(32 * q) << 16);
-    if (go) {
-      if (kMode == kEpiSwiGLU) {
+    const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
+    int lt = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
+      const int b = lt & 1;
+      // tcgen05.ld is warp-wide: one decision per warp
+      if (!__all_sync(0xffffffffu, wait_bounded(&sm.acc_full[b], (lt >> 1) & 1, g.timeout_ns, &sm.err))) break;
+      tc::fence_after_sync();
+      const int m0 = (t / n_tiles_n) * BM;
+      const int n0 = (t % n_tiles_n) * BN;
+      const int row = m0 + 32 * q + lane;
+      const uint32_t lane_addr = tbase + b * BN + lane_off;
+      if (kMode == kEpiQKV) {
+        const int pos = g.pos0 + row;
+#pragma unroll 1
+        for (int hh = 0; hh < BN / kHeadDim; ++hh) {
+          const int head = n0 / kHeadDim + hh;  // 0-15 q, 16-23 k, 24-31 v
+          float x[kHeadDim];
+#pragma unroll
+          for (int c = 0; c < kHeadDim / 32; ++c) tc::tmem_ld32(lane_addr + kHeadDim * hh + 32 * c, x + 32 * c);
+          if (row >= g.M) continue;
+          if (head < kNQ + kNKV) {
+            // the same arithmetic, in the same order, as qk_rope_kernel (whose
+            // warp_sum adds the lanes' partials in a butterfly)
+            const __nv_bfloat16* nw = head < kNQ ? g.qn : g.kn;
+            float p[32];
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              const float x0 = x[2 * t], x1 = x[2 * t + 1], x2 = x[2 * t + 64], x3 = x[2 * t + 65];
+              p[t] = x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+              for (int t = 0; t < o; ++t) p[t] = p[t] + p[t + o];
+            const float rstd = rsqrtf(p[0] * (1.0f / kHeadDim) + kEps);
+#pragma unroll
+            for (int d = 0; d < kHeadDim; d += 4) {
+              const uint2 w = __ldg(reinterpret_cast<const uint2*>(nw + d));
+              x[d] = x[d] * rstd * bf_lo(w.x);
+              x[d + 1] = x[d + 1] * rstd * bf_hi(w.x);
+              x[d + 2] = x[d + 2] * rstd * bf_lo(w.y);
+              x[d + 3] = x[d + 3] * rstd * bf_hi(w.y);
+            }
+            const size_t rb = (size_t)pos * kHeadDim;
+#pragma unroll
+            for (int d = 0; d < kHeadDim / 2; d += 4) {  // rotate-half: (d, d + 64) pairs
+              const float4 c4 = table4(g.cos_t, g.rope_fp32, rb + d), s4 = table4(g.sin_t, g.rope_fp32, rb + d);
+              const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float a = x[d + e], bv = x[d + e + 64];
+                x[d + e] = a * cs[e] - bv * sn[e];
+                x[d + e + 64] = bv * cs[e] + a * sn[e];
+              }
+            }
+          }
+          if (head < kNQ) {
+            const float sc = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
+            const size_t o = (size_t)row * kQSize + head * kHeadDim;
+#pragma unroll
+            for (int d = 0; d < kHeadDim; d += 8) {
+              uint32_t h[4], lo[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float a = x[d + 2 * e], bv = x[d + 2 * e + 1];
+                h[e] = pack_bf2(a * sc, bv * sc);
+                lo[e] = pack_bf2(a * sc - bf_lo(h[e]), bv * sc - bf_hi(h[e]));
+              }
+              *reinterpret_cast<uint4*>(g.q_hi + o + d) = make_uint4(h[0], h[1], h[2], h[3]);
+              *reinterpret_cast<uint4*>(g.q_lo + o + d) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+          } else {
+            const int h = (head - kNQ) % kNKV;
+            __nv_bfloat16* dst =
+                (head < kNQ + kNKV ? g.kc_layer : g.vc_layer) + ((size_t)h * g.max_seq + pos) * kHeadDim;
+#pragma unroll
+            for (int d = 0; d < kHeadDim; d += 8)
+              *reinterpret_cast<uint4*>(dst + d) = make_uint4(pack_bf2(x[d], x[d + 1]), pack_bf2(x[d + 2], x[d + 3]),
+                                                              pack_bf2(x[d + 4], x[d + 5]), pack_bf2(x[d + 6], x[d + 7]));
+            if (head >= kNQ + kNKV && g.vt != nullptr) {  // V^T: lanes hold consecutive keys
+              __nv_bfloat16* col = g.vt + (size_t)h * kHeadDim * g.vt_cols + pos;
+#pragma unroll
+              for (int d = 0; d < kHeadDim; ++d) col[(size_t)d * g.vt_cols] = __float2bfloat16_rn(x[d]);
+            }
+          }
+        }
+      } else if (kMode == kEpiSwiGLU) {
 #pragma unroll 1
         for (int half = 0; half < BN / 64; ++half) {
           float gv[32], uv[32];
@@ -223,6 +355,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
+      // the accumulator has been read (tcgen05.ld waited): the MMAs may reuse it
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
     }
   }
   tc::fence_before_sync();
@@ -230,7 +366,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0 && sm.err && g.err) atomicCAS(g.err, 0u, static_cast<uint32_t>(kErrTimeoutRing));
   if (warp == 1) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tbase, BN);
+    tc::tmem_dealloc(tbase, 2 * BN);
   }
 }
 
@@ -267,10 +403,6 @@ __global__ void rmsnorm_split_kernel(const float* __restrict__ h, const __nv_bfl
       make_uint2(pack_bf2(x[0] - bf_lo(h01), x[1] - bf_hi(h01)), pack_bf2(x[2] - bf_lo(h23), x[3] - bf_hi(h23)));
 }
 
-__device__ __forceinline__ float rope_val(const void* table, int fp32, size_t idx) {
-  return fp32 ? __ldg(static_cast<const float*>(table) + idx)
-              : __bfloat162float(static_cast<const __nv_bfloat16*>(table)[idx]);
-}
 
 // Per token (blockIdx.x) and head row (one warp per head: 16 q, 8 k, 8 v):
 // q/k RMSNorm over 128 dims + rotate-half RoPE at the token's position
@@ -512,13 +644,15 @@ __global__ void __launch_bounds__(128) attn_kernel(const float* __restrict__ q, 
 // GEMMs), P as one BF16 operand. Keys come in tiles of 128: K rows straight from
 // the cache (K-major for S), V from a per-layer transposed copy (v_transpose_kernel)
 // so that V^T is K-major for O. Warp 0 issues the TMA loads (2-stage K and V^T
-// rings), one thread of warp 1 the MMAs, warps 2-5 own one query row per thread:
-// they read S from TMEM, keep the online softmax (exp2 domain; the reference max
-// only moves when a row's maximum grows by more than 8, so O is rescaled in TMEM
+// rings), one thread of warp 1 the MMAs, warps 2-9 the softmax: each query row
+// has two threads (warps w and w + 4 share TMEM lanes 32 (w % 4)..), each over
+// 64 keys of a tile, exchanging their row maxima through shared memory. They
+// read S from TMEM, keep the online softmax (exp2 domain; the reference max only
+// moves when a row's maximum grows by more than 8, so O is rescaled in TMEM
 // rarely and P stays within [0, 256]), and write P into shared memory in the
 // MMA's 128-byte-swizzled layout. Two S buffers in TMEM let the tensor cores
 // compute the next tile's scores while the softmax works on this one.
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;
 constexpr int kAtom = 128 * 128;  // 16 KB: 128 rows x 64 BF16, 128-byte swizzle
 struct AttnTcSmem {
   uint8_t qh[2][kAtom];     // [dim half]: query rows
@@ -526,11 +660,16 @@ struct AttnTcSmem {
   uint8_t k[2][2][kAtom];   // [stage][dim half]: key rows
   uint8_t vt[2][2][kAtom];  // [stage][key half]: dim rows
   uint8_t p[2][kAtom];      // [key half]: query rows
+  float red[2][2][128];     // [tile parity][key half][row]: partial row maxima, then the row sums
   uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full, o_done;
+  uint64_t xbar[4];         // per row quarter: both softmax threads of its rows have posted
   uint32_t tmem_base;
   int err;
 };
-constexpr size_t kAttTcSmem = sizeof(AttnTcSmem) + 1024;
+// No alignment slack fits beside the 224 KB of tiles: the kernel checks that the
+// dynamic shared memory starts on a 1024-byte boundary (the swizzle atom) and
+// reports an error otherwise.
+constexpr size_t kAttTcSmem = sizeof(AttnTcSmem);
 static_assert(kAttTcSmem <= 232448, "attention shared memory");
 constexpr uint32_t kAttTmemCols = 512;  // S buffers at columns 0 and 128, O at 256
 
@@ -544,7 +683,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tvt, int n, int pos0,
                    int max_seq, __nv_bfloat16* oh, __nv_bfloat16* ol, unsigned long long timeout_ns, uint32_t* err) {
   extern __shared__ uint8_t smem_raw[];
-  AttnTcSmem& sm = *reinterpret_cast<AttnTcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (smem_addr(smem_raw) & 1023u) {
+    if (threadIdx.x == 0 && err) atomicCAS(err, 0u, static_cast<uint32_t>(kErrTimeoutRing));
+    return;
+  }
+  AttnTcSmem& sm = *reinterpret_cast<AttnTcSmem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hq = blockIdx.x, hk = hq >> 1;
   // causal work grows with the query block: the longest blocks (of every head) go first
@@ -559,8 +702,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&sm.v_empty[s], 1);
       mbar_init(&sm.s_full[s], 1);
     }
-    mbar_init(&sm.p_full, 128);
+    mbar_init(&sm.p_full, 8);  // one arrival per softmax warp
     mbar_init(&sm.o_done, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&sm.xbar[q], 64);
     sm.err = 0;
     fence_mbar_init();
   }
@@ -585,19 +729,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     const int krow = hk * max_seq;  // this KV head's first cache row in the layer's map
     int k_issued = 0, v_issued = 0;
-    for (int j = 0; j < nt; ++j) {
+    // K(j) once S(j - 2) has read its stage, V(j) once PV(j - 2) has; issued in
+    // the order the MMAs consume them (S(j + 1) runs before PV(j)), so a K tile
+    // never queues behind the release of a V stage
+    auto load_k = [&](int j) -> bool {
       const int st = j & 1;
-      const uint32_t ph = ((j >> 1) - 1) & 1;
-      if (j >= 2 && !wait_bounded(&sm.k_empty[st], ph, timeout_ns, &sm.err)) break;
+      if (j >= 2 && !wait_bounded(&sm.k_empty[st], ((j >> 1) - 1) & 1, timeout_ns, &sm.err)) return false;
       mbar_arrive_expect_tx(&sm.k_full[st], 2 * kAtom);
       tc::tma_load_2d(sm.k[st][0], &tk, 0, krow + 128 * j, &sm.k_full[st]);
       tc::tma_load_2d(sm.k[st][1], &tk, 64, krow + 128 * j, &sm.k_full[st]);
       ++k_issued;
-      if (j >= 2 && !wait_bounded(&sm.v_empty[st], ph, timeout_ns, &sm.err)) break;
-      mbar_arrive_expect_tx(&sm.v_full[st], 2 * kAtom);
-      tc::tma_load_2d(sm.vt[st][0], &tvt, 128 * j, hk * kHeadDim, &sm.v_full[st]);
-      tc::tma_load_2d(sm.vt[st][1], &tvt, 128 * j + 64, hk * kHeadDim, &sm.v_full[st]);
-      ++v_issued;
+      return true;
+    };
+    if (load_k(0)) {
+      for (int j = 0; j < nt; ++j) {
+        if (j + 1 < nt && !load_k(j + 1)) break;
+        const int st = j & 1;
+        if (j >= 2 && !wait_bounded(&sm.v_empty[st], ((j >> 1) - 1) & 1, timeout_ns, &sm.err)) break;
+        mbar_arrive_expect_tx(&sm.v_full[st], 2 * kAtom);
+        tc::tma_load_2d(sm.vt[st][0], &tvt, 128 * j, hk * kHeadDim, &sm.v_full[st]);
+        tc::tma_load_2d(sm.vt[st][1], &tvt, 128 * j + 64, hk * kHeadDim, &sm.v_full[st]);
+        ++v_issued;
+      }
     }
     // after a stop, wait (bounded) for the copies still in flight before leaving
     if (sm.err) {
@@ -649,85 +802,115 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   } else if (warp >= 2) {
-    const int q4 = warp & 3;  // TMEM lanes 32 q4 .. + 31 = query rows
+    const int q4 = warp & 3;        // TMEM lanes 32 q4 .. + 31 = query rows
+    const int g = (warp - 2) >> 2;  // keys 64 g .. + 63 of each tile, O columns 64 g .. + 63
     const int row = 32 * q4 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(32 * q4) << 16;
     const int lim = pos0 + i0 + row;  // this query's last key
-    float m = 0.f, l = 0.f;           // reference max (exp2 domain) and row sum
+    float m = 0.f, l = 0.f;           // reference max (exp2 domain) and this half's row sum
+    // post v for the partner thread of this row, return the partner's value
+    auto exchange = [&](int j, float v, float* out) -> bool {
+      sm.red[j & 1][g][row] = v;
+      mbar_arrive(&sm.xbar[q4]);  // release: the partner's wait sees the value
+      if (!wait_bounded(&sm.xbar[q4], j & 1, timeout_ns, &sm.err)) return false;
+      *out = sm.red[j & 1][g ^ 1][row];
+      return true;
+    };
     bool go = true;
     for (int j = 0; j < nt && go; ++j) {
       const int st = j & 1;
       go = warp_wait(&sm.s_full[st], (j >> 1) & 1, timeout_ns, &sm.err);
       if (!go) break;
       tc::fence_after_sync();
-      float s[128];
+      uint32_t sr[2][32];
+      tc::tmem_ld32_nowait(tbase + lane_off + 128 * st + 64 * g, sr[0]);
+      tc::tmem_ld32_nowait(tbase + lane_off + 128 * st + 64 * g + 32, sr[1]);
+      tc::tmem_wait_ld<true>(sr[0]);
+      tc::tmem_wait_ld<false>(sr[1]);
+      float s[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tc::tmem_ld32(tbase + lane_off + 128 * st + 32 * c, s + 32 * c);
-      const int k0 = 128 * j;
-      if (k0 + 127 > lim) {
+      for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(sr[i >> 5][i & 31]);
+      const int k0 = 128 * j + 64 * g;
+      if (k0 + 63 > lim) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
+        for (int i = 0; i < 64; ++i)
           if (k0 + i > lim) s[i] = -INFINITY;
       }
-      float mx = s[0];
+      float mx8[8];
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);  // finite: key 0 <= lim, and tile 0 holds it
+      for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+#pragma unroll
+      for (int i = 8; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], s[i]);
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      float mo;
+      go = __all_sync(0xffffffffu, exchange(j, mx, &mo));
+      if (!go) break;
+      mx = fmaxf(mx, mo);  // the row's tile max, identical in both threads (key 0 <= lim: finite in tile 0)
+      // the reference max moves (and O is rescaled) only when some row of the
+      // warp grew by more than 8; the decision is warp-uniform (tcgen05.ld/st)
+      // and the same in both warps of the rows
+      float sc = 1.f;
+      const bool rescale = j > 0 && __any_sync(0xffffffffu, mx > m + 8.f);
+      if (j == 0) {
+        m = mx;
+      } else if (rescale) {
+        sc = mx > m ? ex2_approx(m - mx) : 1.f;
+        m = fmaxf(m, mx);
+      }
+      // P = 2^(S - m) in BF16 (ex2.approx gives 0 at -inf) while PV(j - 1) runs
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pw[32];
+#pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        const float pa = ex2_approx(s[2 * t] - m), pb = ex2_approx(s[2 * t + 1] - m);
+        rs[t & 3] += pa + pb;
+        pw[t] = pack_bf2(pa, pb);
+      }
       if (j > 0) {
         // PV(j - 1) has completed: the P buffer is free and O may be rescaled
         go = warp_wait(&sm.o_done, (j - 1) & 1, timeout_ns, &sm.err);
         if (!go) break;
         tc::fence_after_sync();
-        if (__any_sync(0xffffffffu, mx > m + 8.f)) {
-          const float sc = mx > m ? ex2_approx(m - mx) : 1.f;
-          m = fmaxf(m, mx);
+        if (rescale) {
           l *= sc;
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             float o[32];
-            tc::tmem_ld32(t_o + lane_off + 32 * c, o);
+            tc::tmem_ld32(t_o + lane_off + 64 * g + 32 * c, o);
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= sc;
-            tc::tmem_st32(t_o + lane_off + 32 * c, o);
+            tc::tmem_st32(t_o + lane_off + 64 * g + 32 * c, o);
           }
         }
-      } else {
-        m = mx;
       }
-      // P = 2^(S - m) in BF16, row r of each 64-key atom at r * 128 bytes with the
-      // 16-byte chunks swizzled by r & 7 (the layout a 128-byte-swizzle TMA writes)
-      float rs = 0.f;
+      // row r of the 64-key atom at r * 128 bytes, 16-byte chunks swizzled by
+      // r & 7 (the layout a 128-byte-swizzle TMA writes)
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float a = s[8 * c + 2 * t], b = s[8 * c + 2 * t + 1];
-          const float pa = a > -INFINITY ? ex2_approx(a - m) : 0.f;
-          const float pb = b > -INFINITY ? ex2_approx(b - m) : 0.f;
-          rs += pa + pb;
-          w[t] = pack_bf2(pa, pb);
-        }
-        *reinterpret_cast<uint4*>(sm.p[c >> 3] + row * 128 + (((c & 7) ^ (row & 7)) << 4)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      l += rs;
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(sm.p[g] + row * 128 + ((c ^ (row & 7)) << 4)) =
+            make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
+      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       fence_proxy_async_shared();  // P is read by the tensor cores (async proxy)
       tc::fence_before_sync();
-      mbar_arrive(&sm.p_full);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full);
     }
+    float lo = 0.f;
+    if (go) go = __all_sync(0xffffffffu, exchange(nt, l, &lo));  // the row sum of both halves
     if (go) go = warp_wait(&sm.o_done, (nt - 1) & 1, timeout_ns, &sm.err);
     if (go) {
       tc::fence_after_sync();
       const int qi = i0 + row;
-      const float inv = 1.f / l;
+      const float inv = 1.f / (g == 0 ? l + lo : lo + l);
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float o[32];
-        tc::tmem_ld32(t_o + lane_off + 32 * c, o);
+        tc::tmem_ld32(t_o + lane_off + 64 * g + 32 * c, o);
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] *= inv;
         if (qi < n) {
-          const size_t off = (size_t)qi * kQSize + hq * kHeadDim + 32 * c;
+          const size_t off = (size_t)qi * kQSize + hq * kHeadDim + 64 * g + 32 * c;
           split_store(oh + off, ol + off, o, 4);
         }
       }
@@ -804,7 +987,7 @@ cudaError_t map_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t col
 
 template <int kMode, int kBN>
 cudaError_t gemm_launch(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& b, const CUtensorMap& b2,
-                        const GemmArgs& g, cudaStream_t stream) {
+                        const CUtensorMap& b3, const GemmArgs& g, cudaStream_t stream) {
   static int configured[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -817,8 +1000,12 @@ cudaError_t gemm_launch(const CUtensorMap& ah, const CUtensorMap& al, const CUte
     configured[dev] = 1;
   }
   if (g.K % BK || g.N % kBN || g.M < 1) return cudaErrorInvalidValue;
-  dim3 grid(g.N / kBN, (g.M + BM - 1) / BM);
-  gemm_kernel<kMode, kBN><<<grid, kGemmThreads, gemm_smem<kBN>(), stream>>>(ah, al, b, b2, g);
+  static int sms[64] = {0};
+  if (!sms[dev] && (e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    return e;
+  const int tiles = (g.N / kBN) * ((g.M + BM - 1) / BM);
+  gemm_kernel<kMode, kBN><<<tiles < sms[dev] ? tiles : sms[dev], kGemmThreads, gemm_smem<kBN>(), stream>>>(ah, al, b, b2,
+                                                                                                         b3, g);
   return cudaGetLastError();
 }
 constexpr int kPfBN = 256;  // the prefill's GEMMs (every N a multiple of 256)
@@ -840,7 +1027,6 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
   if (e == cudaSuccess) e = map_2d(&tqh, s.mh, n, kQSize, 128);
   if (e == cudaSuccess) e = map_2d(&tql, s.ml, n, kQSize, 128);
   if (e == cudaSuccess) e = map_2d(&tvt, s.vt, kNKV * kHeadDim, s.vt_cols, 128);
-  const int kv_tiles = (pos0 + n + 127) / 128;
 #else
   cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttSmem);
 #endif
@@ -869,33 +1055,50 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
     if ((e = map_2d(&bg, w.gate_proj_weight, kInter, kHidden, kPfBN / 2)) != cudaSuccess) return e;
     if ((e = map_2d(&bu, w.up_proj_weight, kInter, kHidden, kPfBN / 2)) != cudaSuccess) return e;
     if ((e = map_2d(&bd, w.down_proj_weight, kHidden, kInter, kPfBN)) != cudaSuccess) return e;
-    // input RMSNorm -> QKV (three GEMMs into the [n, 4096] buffer)
+    // input RMSNorm
     rmsnorm_split_kernel<<<n, kHidden / 4, 0, stream>>>(s.h, w.norm_weight, s.ah, s.al);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     g.K = kHidden;
-    g.ldc = kQKVRows;
-    g.N = kQSize;
-    g.c = s.qkv;
-    if ((e = gemm_launch<kEpiStore, kPfBN>(a1h, a1l, bq, bq, g, stream)) != cudaSuccess) return e;
-    g.N = kKVSize;
-    g.c = s.qkv + kQSize;
-    if ((e = gemm_launch<kEpiStore, kPfBN>(a1h, a1l, bk, bk, g, stream)) != cudaSuccess) return e;
-    g.c = s.qkv + kQSize + kKVSize;
-    if ((e = gemm_launch<kEpiStore, kPfBN>(a1h, a1l, bv, bv, g, stream)) != cudaSuccess) return e;
-    // q/k norm + RoPE, K/V rows into the cache, then causal attention
 #if MKB_PF_ATTN_TC
-    qk_rope_kernel<<<dim3(n, 4), 256, 0, stream>>>(s.qkv, w.q_norm_weight, w.k_norm_weight, cos_t, sin_t, rope_fp32,
-                                                   pos0, l, kc, vc, max_seq, nullptr, s.mh, s.ml);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // one GEMM over the q, k and v weights; its epilogue applies the q/k RMSNorm
+    // and RoPE, writes q (BF16 high part / remainder, into the SwiGLU buffers,
+    // free until the gate/up GEMM), the K/V cache rows and V^T of the new keys
     const size_t layer_rows = (size_t)l * kNKV * max_seq;  // this layer's first cache row
-    v_transpose_kernel<<<dim3(2 * kv_tiles, kNKV), 256, 0, stream>>>(vc + layer_rows * kHeadDim, max_seq, pos0 + n,
-                                                                     s.vt_cols, s.vt);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    g.N = kQKVRows;
+    g.qn = w.q_norm_weight;
+    g.kn = w.k_norm_weight;
+    g.cos_t = cos_t;
+    g.sin_t = sin_t;
+    g.rope_fp32 = rope_fp32;
+    g.pos0 = pos0;
+    g.max_seq = max_seq;
+    g.kc_layer = kc + layer_rows * kHeadDim;
+    g.vc_layer = vc + layer_rows * kHeadDim;
+    g.q_hi = s.mh;
+    g.q_lo = s.ml;
+    g.vt = s.vt;
+    g.vt_cols = s.vt_cols;
+    if ((e = gemm_launch<kEpiQKV, kPfBN>(a1h, a1l, bq, bk, bv, g, stream)) != cudaSuccess) return e;
+    if (pos0 > 0) {  // V^T of the keys cached before this prefill (rows of V^T past them: zeros or old finite values)
+      v_transpose_kernel<<<dim3((pos0 + 63) / 64, kNKV), 256, 0, stream>>>(g.vc_layer, max_seq, pos0 + n, s.vt_cols,
+                                                                          s.vt);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
     CUtensorMap tk;
     if ((e = map_2d(&tk, kc + layer_rows * kHeadDim, (uint64_t)kNKV * max_seq, kHeadDim, 128)) != cudaSuccess) return e;
     attn_tc_kernel<<<dim3(kNQ, (n + 127) / 128), kTcThreads, kAttTcSmem, stream>>>(
         tqh, tql, tk, tvt, n, pos0, max_seq, s.ah, s.al, g.timeout_ns, s.err);
 #else
+    // three GEMMs into the [n, 4096] buffer, then q/k norm + RoPE with the K/V rows into the cache
+    g.ldc = kQKVRows;
+    g.N = kQSize;
+    g.c = s.qkv;
+    if ((e = gemm_launch<kEpiStore, kPfBN>(a1h, a1l, bq, bq, bq, g, stream)) != cudaSuccess) return e;
+    g.N = kKVSize;
+    g.c = s.qkv + kQSize;
+    if ((e = gemm_launch<kEpiStore, kPfBN>(a1h, a1l, bk, bk, bk, g, stream)) != cudaSuccess) return e;
+    g.c = s.qkv + kQSize + kKVSize;
+    if ((e = gemm_launch<kEpiStore, kPfBN>(a1h, a1l, bv, bv, bv, g, stream)) != cudaSuccess) return e;
     qk_rope_kernel<<<dim3(n, 4), 256, 0, stream>>>(s.qkv, w.q_norm_weight, w.k_norm_weight, cos_t, sin_t, rope_fp32,
                                                    pos0, l, kc, vc, max_seq, s.q, nullptr, nullptr);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -907,7 +1110,7 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
     g.N = kHidden;
     g.ldc = kHidden;
     g.c = s.h;
-    if ((e = gemm_launch<kEpiAdd, kPfBN>(a2h, a2l, bo, bo, g, stream)) != cudaSuccess) return e;
+    if ((e = gemm_launch<kEpiAdd, kPfBN>(a2h, a2l, bo, bo, bo, g, stream)) != cudaSuccess) return e;
     // post-attention RMSNorm -> gate/up with SwiGLU -> down added into the residual
     rmsnorm_split_kernel<<<n, kHidden / 4, 0, stream>>>(s.h, w.post_attn_norm_weight, s.ah, s.al);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -916,12 +1119,12 @@ cudaError_t prefill_layers(const LayerWeights* host_layers, int n_layers, const 
     g.m_hi = s.mh;  // a separate buffer: the GEMM still reads s.ah / s.al
     g.m_lo = s.ml;
     g.ldm = kInter;
-    if ((e = gemm_launch<kEpiSwiGLU, kPfBN>(a1h, a1l, bg, bu, g, stream)) != cudaSuccess) return e;
+    if ((e = gemm_launch<kEpiSwiGLU, kPfBN>(a1h, a1l, bg, bu, bu, g, stream)) != cudaSuccess) return e;
     g.K = kInter;
     g.N = kHidden;
     g.c = s.h;
     g.ldc = kHidden;
-    if ((e = gemm_launch<kEpiAdd, kPfBN>(a3h, a3l, bd, bd, g, stream)) != cudaSuccess) return e;
+    if ((e = gemm_launch<kEpiAdd, kPfBN>(a3h, a3l, bd, bd, bd, g, stream)) != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
@@ -944,8 +1147,8 @@ cudaError_t gemm_split(const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, con
   g.ldc = N;
   g.timeout_ns = 1000000000ull;
   g.err = err;
-  return wide ? gemm_launch<kEpiStore, 256>(ah, al, bm, bm, g, stream)
-              : gemm_launch<kEpiStore, 128>(ah, al, bm, bm, g, stream);
+  return wide ? gemm_launch<kEpiStore, 256>(ah, al, bm, bm, bm, g, stream)
+              : gemm_launch<kEpiStore, 128>(ah, al, bm, bm, bm, g, stream);
 }
 
 }  // namespace mkb

@@ -26,8 +26,11 @@ def cosine(a, b):
     return torch.nn.functional.cosine_similarity(a.double(), b.double(), dim=0).item()
 
 
-@pytest.mark.parametrize("m,n,k", [(128, 128, 64), (200, 256, 1024), (1, 384, 3072), (333, 128, 2048)])
+@pytest.mark.parametrize("m,n,k", [(128, 128, 64), (200, 256, 1024), (1, 384, 3072), (333, 128, 2048),
+                                   (4096, 4096, 256), (4000, 1920, 128)])
 def test_gemm_split_matches_float64(m, n, k, cuda_device):
+    """The last two shapes give every persistent CTA three or four output tiles
+    (both TMEM accumulators reused; 256- and 128-column tiles)."""
     g = torch.Generator(device=DEV).manual_seed(m + n + k)
     a = torch.randn((m, k), generator=g, device=DEV)
     a_hi = a.to(torch.bfloat16)
@@ -91,7 +94,13 @@ def test_batched_prefill_matches_hf(n_prompt, w_gpu, hf_model):
 
 def test_batched_prefill_matches_token_by_token_prefill(w_gpu):
     """The batched and the token-by-token prefill agree closely (same BF16 cache
-    rounding, FP32 residuals, ~2^-16 products) and continue the same way."""
+    rounding, FP32 residuals, ~2^-16 products) and continue the same way.
+
+    The logits bound is half the HF bound. It leaves room for rounding: two
+    batched builds that differ only in where the compiler fused one multiply-add
+    of the q/k RMSNorm (layer 0's K/V identical to 2e-6) end 1.7e-3 apart in the
+    logits after 28 random-weight layers, and 4.9e-3 vs 5.2e-3 from the
+    token-by-token prefill."""
     ids = torch.randint(0, 151936, (150,), generator=torch.Generator().manual_seed(9))
     k1 = torch.zeros((28, 8, 256, 128), dtype=torch.bfloat16, device=DEV)
     v1, k2, v2 = torch.zeros_like(k1), torch.zeros_like(k1), torch.zeros_like(k1)
@@ -100,7 +109,8 @@ def test_batched_prefill_matches_token_by_token_prefill(w_gpu):
     n1 = e1.prefill(ids, batched=True)
     n2 = e2.prefill(ids)
     l1, l2 = e1.logits.cpu(), e2.logits.cpu()
-    assert (l1 - l2).abs().max().item() <= 5e-3
+    assert (l1 - l2).abs().max().item() <= 1e-2
+    assert cosine(l1, l2) > 0.99999
     t2 = torch.topk(l2.double(), 2).values
     if float(t2[0] - t2[1]) > 5e-3:
         assert n1 == n2
