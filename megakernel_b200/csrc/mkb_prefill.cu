@@ -209,6 +209,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
+    const uint64_t dah0 = tc::desc_sw128(smem_addr(sm.a_hi[0])), dal0 = tc::desc_sw128(smem_addr(sm.a_lo[0])),
+                   db0 = tc::desc_sw128(smem_addr(sm.b[0]));
     int it = 0, lt = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++lt) {
@@ -223,12 +225,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc::fence_after_sync();
-        const uint32_t ah = smem_addr(sm.a_hi[s]), al = smem_addr(sm.a_lo[s]), bb = smem_addr(sm.b[s]);
+        const uint64_t dah = tc::desc_advance(dah0, s * kTile), dal = tc::desc_advance(dal0, s * kTile),
+                       dbb = tc::desc_advance(db0, s * kTileB);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t db = tc::desc_sw128(bb + kk * 32);
-          tc::mma_bf16_ss(acc, tc::desc_sw128(ah + kk * 32), db, idesc, (kt | kk) != 0);
-          tc::mma_bf16_ss(acc, tc::desc_sw128(al + kk * 32), db, idesc, 1u);
+          const uint64_t db = tc::desc_advance(dbb, kk * 32);
+          tc::mma_bf16_ss(acc, tc::desc_advance(dah, kk * 32), db, idesc, (kt | kk) != 0);
+          tc::mma_bf16_ss(acc, tc::desc_advance(dal, kk * 32), db, idesc, 1u);
         }
         tc::commit(&sm.empty[s]);  // the stage is free once these MMAs have read it
       }
@@ -768,17 +771,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr uint32_t idesc = tc::idesc_bf16_f32(128, 128);
     const uint32_t qh = smem_addr(sm.qh[0]), ql = smem_addr(sm.ql[0]), pa = smem_addr(sm.p[0]);
     // S(j) = (Q_hi + Q_lo) K(j)^T into S buffer j & 1
+    // descriptors formed once and advanced by compile-time offsets
+    const uint64_t dqh = tc::desc_sw128(qh), dql = tc::desc_sw128(ql), dp = tc::desc_sw128(pa);
+    const uint64_t dk0 = tc::desc_sw128(smem_addr(sm.k[0][0])), dv0 = tc::desc_sw128(smem_addr(sm.vt[0][0]));
     auto issue_s = [&](int j) -> bool {
       const int st = j & 1;
       if (!wait_bounded(&sm.k_full[st], (j >> 1) & 1, timeout_ns, &sm.err)) return false;
       tc::fence_after_sync();
-      const uint32_t kb = smem_addr(sm.k[st][0]);
+      const uint64_t dk = tc::desc_advance(dk0, st * 2 * kAtom);
 #pragma unroll
       for (int kk = 0; kk < kHeadDim / 16; ++kk) {
         const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-        const uint64_t db = tc::desc_sw128(kb + off);
-        tc::mma_bf16_ss(tbase + 128 * st, tc::desc_sw128(qh + off), db, idesc, kk != 0);
-        tc::mma_bf16_ss(tbase + 128 * st, tc::desc_sw128(ql + off), db, idesc, 1u);
+        const uint64_t db = tc::desc_advance(dk, off);
+        tc::mma_bf16_ss(tbase + 128 * st, tc::desc_advance(dqh, off), db, idesc, kk != 0);
+        tc::mma_bf16_ss(tbase + 128 * st, tc::desc_advance(dql, off), db, idesc, 1u);
       }
       tc::commit(&sm.k_empty[st]);
       tc::commit(&sm.s_full[st]);
@@ -791,11 +797,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!wait_bounded(&sm.p_full, j & 1, timeout_ns, &sm.err)) break;
         if (!wait_bounded(&sm.v_full[j & 1], (j >> 1) & 1, timeout_ns, &sm.err)) break;
         tc::fence_after_sync();
-        const uint32_t vb = smem_addr(sm.vt[j & 1][0]);
+        const uint64_t dv = tc::desc_advance(dv0, (j & 1) * 2 * kAtom);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-          tc::mma_bf16_ss(t_o, tc::desc_sw128(pa + off), tc::desc_sw128(vb + off), idesc, (j | kk) != 0);
+          tc::mma_bf16_ss(t_o, tc::desc_advance(dp, off), tc::desc_advance(dv, off), idesc, (j | kk) != 0);
         }
         tc::commit(&sm.v_empty[j & 1]);
         tc::commit(&sm.o_done);

@@ -42,6 +42,11 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_byte_addr) {
   return d;
 }
 
+// The descriptor of (descriptor's address + bytes): the start address sits in
+// the low 14 bits as address >> 4, and shared-memory addresses stay below
+// 256 KB, so adding bytes >> 4 never carries out of the field.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
+
 // Instruction descriptor, .kind::f16: FP32 accumulator (bits 4-5 = 1), A and B
 // BF16 (bits 7-9 = 1, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 in
 // bits 17-22, M >> 4 in bits 24-28.
