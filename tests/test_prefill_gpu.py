@@ -120,6 +120,33 @@ def test_batched_prefill_matches_token_by_token_prefill(w_gpu):
     e2.close()
 
 
+def test_batched_prefill_continues_at_unaligned_offsets(w_gpu):
+    """Three batched prefills (100 tokens, 157 at position 100, 1 at position 257)
+    into a 300-slot cache (not a multiple of the attention's 128-key tiles) equal
+    one batched prefill of all 258 tokens: the earlier keys' V^T comes from the
+    cache through v_transpose_kernel, over key blocks that the same prefill's
+    QKV epilogue partly wrote."""
+    ids = torch.randint(0, 151936, (258,), generator=torch.Generator().manual_seed(4))
+    k1 = torch.zeros((28, 8, 300, 128), dtype=torch.bfloat16, device=DEV)
+    v1, k2, v2 = torch.zeros_like(k1), torch.zeros_like(k1), torch.zeros_like(k1)
+    e1 = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), k1, v1)
+    e2 = mk.DecodeEngine(w_gpu.embed, w_gpu.final_norm, w_gpu.flat_layer_list(), k2, v2)
+    e1.prefill(ids[:100], batched=True)
+    e1.prefill(ids[100:257], position=100, batched=True)
+    n1 = e1.prefill(ids[257:], position=257, batched=True)
+    n2 = e2.prefill(ids, batched=True)
+    assert (e1.logits - e2.logits).abs().max().item() <= 1e-3
+    for got, ref in ((k1, k2), (v1, v2)):
+        torch.testing.assert_close(got.float(), ref.float(), rtol=1.6e-2, atol=1e-3)
+    assert not k1[:, :, 258:].any() and not v1[:, :, 258:].any()
+    t2 = torch.topk(e2.logits.double(), 2).values
+    if float(t2[0] - t2[1]) > 1e-3:
+        assert n1 == n2
+    assert e1.status()[0] == 0 and e2.status()[0] == 0
+    e1.close()
+    e2.close()
+
+
 def test_batched_prefill_at_an_offset_continues_a_cache(w_gpu):
     """A second batched prefill at position 40 after a first one at 0 equals one
     batched prefill of the concatenated prompt (the causal attention reads the
