@@ -144,7 +144,7 @@ typedef struct mkb_decode_args {
                                   eos_token_id check, model.py:102-105): its id is the last
                                   one written, later out_tokens read -1, and no K/V row is
                                   appended for it. */
-  int tp_rank, tp_size;        /* tensor parallel (SURVEY 4b; no counterpart in the
+  int tp_rank, tp_size;        /* tensor parallel (no counterpart in the
                                   reference): tp_size 1 (default), 2, 4 or 8 GPUs, one
                                   launch per GPU at the same time. Rank r takes KV heads
                                   [r*8/tp_size, (r+1)*8/tp_size), SwiGLU rows and

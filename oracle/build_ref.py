@@ -21,7 +21,9 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 OUT = os.path.join(OUT_DIR, "libref_megakernel.so")
-DEFAULT_REF = os.environ.get("MKB_REFERENCE_DIR", "/root/reference")
+# the reference checkout: MKB_REFERENCE_DIR, else a "reference" directory beside this repository
+DEFAULT_REF = os.environ.get("MKB_REFERENCE_DIR",
+                             os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 
 def build(ref_dir: str = DEFAULT_REF, force: bool = False) -> str | None:
